@@ -1,0 +1,332 @@
+#!/usr/bin/env python3
+"""Benchmark of the b200q decode hot path (one JSON line on stdout, rank 0).
+
+Workload (the fused FFN block of a 4B-like layer): RMSNorm (eps 1e-6, gain N(1, 0.1))
+deferred into the Q8_0 quantizer, gate and up Q8_0 GEMVs [9216 x 2560] in one pass with the SwiGLU epilogue, the
+down Q8_0 GEMV [2560 x 9216] with the residual ADD epilogue — one command list of the reference ISA, replayed as one
+CUDA Graph per step. A step is one pass of the block over one token. Synthetic seeded weights with the config's
+distributions (no model files here). L2: the step rotates through enough distinct weight copies that the weights
+read per round exceed the 126 MB L2 (each step reads weights that are not L2-resident).
+
+metric: GEMV HBM GB/s = algorithmic bytes of the block (weights in their GGUF bits + x, gain, residual, y) per step
+/ device time per step. N GPUs (torchrun): every matrix is row-sharded over the GPUs and the outputs all-gathered
+with NCCL inside the graph; the block is the same, so `value` = total algorithmic bytes / max-over-ranks time
+(strong scaling).
+
+--impl reference: the reference's own CPU arithmetic (fpga/src/gemvq_ref.h built from the reference sources into
+oracle/_ref, OpenMP over row slices) on the same block and metric, on rank 0's host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, F = 2560, 9216
+EPS = 1e-6
+XIN, GAIN, XN, FF, OUT = 0, H, 2 * H, 4 * H, 4 * H + F
+ACT_FLOATS = 1 << 16
+L2_BYTES = 126 << 20
+
+
+def load_package():
+    name = "fpga_llama_gguf_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg_dir = os.path.join(ROOT, "fpga-llama-gguf_b200")
+    spec = importlib.util.spec_from_file_location(name, os.path.join(pkg_dir, "__init__.py"),
+                                                  submodule_search_locations=[pkg_dir])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def weight_bytes() -> int:
+    return 2 * F * (H // 32) * 34 + H * (F // 32) * 34
+
+
+def algorithmic_bytes() -> int:
+    # weights in GGUF bits, x + gain read, residual read, y written
+    return weight_bytes() + 4 * (H + H + H + H)
+
+
+def gen_block(synth, seed: int):
+    r = synth.rng(1, seed)
+    return synth.q8_0(r, F, H), synth.q8_0(r, F, H), synth.q8_0(r, H, F)
+
+
+def block_list(b2, hg, hu, hd):
+    return b2.cmd_list(
+        b2.rmsnorm(H, XIN, GAIN, XN, EPS, flags=b2.NORM_DEFER),
+        b2.gemv(b2.Q8_0, F, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(b2.Q8_0, F, H, hu, XN, FF),
+        b2.gemv(b2.Q8_0, H, F, hd, FF, OUT, b2.GEMV_ADD), b2.add(H, OUT, XIN, OUT))
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [ln.split(",") for ln in open(self.path).read().strip().splitlines() if ln.strip()]
+        except Exception:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peak():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"], "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
+    """The reference CPU path on the host cores: the block's three GEMVs (gemvq_ref.h::reference via oracle/_ref, or
+    the oracle restatement) + the element-wise ops; bounded sample."""
+    import oracle
+    sys.path.insert(0, ROOT)
+    b2 = load_package()
+    import fpga_llama_gguf_b200.synth as synth
+    wg, wu, wd = gen_block(synth, 0)
+    r = synth.rng(1, 99)
+    x = synth.activation(r, H)
+    gain = r.normal(1, 0.1, H).astype(np.float32)
+    cores = os.cpu_count() or 1
+    use_ref = kind == "reference" and oracle.ref_available()
+
+    def block():
+        xn = oracle.rownorm(x, gain, H, 1, EPS, 0)
+        if use_ref:
+            g = oracle.ref_gemv_omp(wg, xn, F, H, 8, cores)
+            u = oracle.ref_gemv_omp(wu, xn, F, H, 8, cores)
+        else:
+            g, _ = oracle.gemv(wg, xn, F, H, 8)
+            u, _ = oracle.gemv(wu, xn, F, H, 8)
+        L = oracle.orc()
+        h = np.array([L.orc_silu_mul1(float(a), float(b), 0) for a, b in zip(g, u)], np.float32)
+        d = oracle.ref_gemv_omp(wd, h, H, F, 8, cores) if use_ref else oracle.gemv(wd, h, H, F, 8)[0]
+        return d + x
+
+    for _ in range(max(0, warmup)):
+        block()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max(1, steps) and (time.perf_counter() < t_end or not times):
+        t0 = time.perf_counter()
+        block()
+        times.append(time.perf_counter() - t0)
+    per = sum(times) / len(times)
+    gbs = algorithmic_bytes() / per / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"{len(times)} FFN blocks (gate+up Q8_0 [9216x2560], down [2560x9216]) at {per * 1e3:.1f} ms "
+                      f"each, gemvq_ref.h generic path, {cores} threads"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": "configs[1] fused FFN block: deferred RMSNorm -> Q8_0 gate+up (SwiGLU) -> Q8_0 down "
+                          "(+residual), hidden 2560, FFN 9216", "global_batch": 1, "seq_len": 1,
+              "parallelism": f"row-sharded x{world}" if world > 1 else "1 GPU"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        cb = cpu_reference(args.steps, min(args.warmup, 1), args.cpu_budget, "reference")
+        line = {"metric": "GEMV HBM GB/s", "value": cb["value"], "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(algorithmic_bytes() / cb["value"] / 1e6, 4),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8/f32",
+                "data": "synthetic", "config": config, "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    b2 = load_package()
+    import fpga_llama_gguf_b200.synth as synth
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = local if world > 1 else 0
+    torch.cuda.set_device(dev)
+
+    # enough weight copies that one round of steps reads more than 3x the L2
+    per_copy = weight_bytes() // world
+    copies = max(2, int(np.ceil(3 * L2_BYTES / max(per_copy, 1))))
+    copies = min(copies, 40)
+    ctx = b2.Context(device=dev, weight_bytes=copies * (per_copy + (8 << 20)) + (64 << 20), act_floats=ACT_FLOATS)
+    if world > 1:
+        obj = [b2.Context.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.comm_init(world, rank, obj[0])
+    graphs, lists = [], []
+    mats = gen_block(synth, 0)
+    for c in range(copies):
+        hg = ctx.upload(mats[0], F, H, b2.Q8_0)
+        hu = ctx.upload(mats[1], F, H, b2.Q8_0)
+        hd = ctx.upload(mats[2], H, F, b2.Q8_0)
+        cl = block_list(b2, hg, hu, hd)
+        lists.append(cl)
+        graphs.append(ctx.graph(cl))
+    r = synth.rng(1, 99)
+    x = synth.activation(r, H)
+    gain = r.normal(1, 0.1, H).astype(np.float32)
+    ctx.write(XIN, x)
+    ctx.write(GAIN, gain)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if not dist:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up
+    ctx.launch_many(graphs, args.warmup)
+    ctx.synchronize()
+    barrier()
+    # timed region: K steps
+    with ClockSampler(dev) as clk:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        ctx.launch_many(graphs, args.steps)
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end) / args.steps
+        ms = max_over_ranks(ms)
+        barrier()
+    clocks = clk.summary()
+    value = algorithmic_bytes() / (ms * 1e-3) / 1e9
+    launches = sum(g.kernels for g in graphs[:1]) * args.steps
+
+    # roofline of the dominant kernel (the gate+up pass): timed alone, rotating copies, CUDA events on the stream
+    peak, peak_kind = measured_peak()
+    ru_graphs = []
+    for c in range(copies):
+        cl = lists[c]
+        ru_graphs.append(ctx.graph(cl[: 3 * 8]))  # deferred norm + gate/up pair: one GEMV kernel
+    ctx.launch_many(ru_graphs, 5)
+    ctx.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_ru = max(20, args.steps)
+    s2.record(stream)
+    ctx.launch_many(ru_graphs, n_ru)
+    e2.record(stream)
+    e2.synchronize()
+    ru_ms = max_over_ranks(s2.elapsed_time(e2) / n_ru)
+    ru_bytes = 2 * F * (H // 32) * 34 + 4 * (H + H)
+    achieved = ru_bytes / (ru_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "kernel": "gemv_q8_kernel (deferred RMSNorm + Q8_0 gate/up pair + SwiGLU)",
+                "algorithmic_bytes_per_launch": ru_bytes, "peak_kind": peak_kind}
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        roofline["traffic"] = prof.get("gemv_q8_kernel_gate_up")
+    except Exception:
+        pass
+
+    # end to end through the public API with host buffers: x in (pinned), run, y out
+    xin = torch.from_numpy(x).pin_memory().numpy()
+    yout = torch.empty(H, dtype=torch.float32).pin_memory().numpy()
+    e2e_steps = min(args.steps, 100)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx.write(XIN, xin)
+        graphs[i % copies].launch()
+        yout[:] = ctx.read(OUT, H)
+    t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
+    e2e = {"value": round(algorithmic_bytes() / t_e2e / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
+           "d2h_bytes_per_step": 4 * H, "ms_per_step": round(t_e2e * 1e3, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        try:
+            cpu = cpu_reference(3, 1, min(args.cpu_budget, 20.0), "reference")
+        except Exception as e:  # the CPU baseline is a reported number only
+            cpu = {"value": None, "error": str(e)}
+
+    for g in graphs + ru_graphs:
+        g.close()
+    ctx.close()
+    if dist:
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {"metric": "GEMV HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32",
+                "data": "synthetic (seeded GGUF Q8_0 weights of config 1)",
+                "config": dict(config, l2=f"{copies} distinct weight copies rotated ({copies * per_copy >> 20} MiB per "
+                                           f"GPU > L2)", frac_of_peak=round(value / peak, 4)),
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

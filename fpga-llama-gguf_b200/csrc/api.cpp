@@ -1,0 +1,973 @@
+// C ABI of b200q (include/b200q.h): the context, the one-time weight upload, the executor that turns a planned
+// command list into kernel launches on the context stream, CUDA Graph capture of whole lists, the bit-exactness
+// check entry points and the NCCL row sharding.
+//
+// Reference counterparts: the XRT backend's device plumbing in llama.cpp/overlay/ggml/src/ggml-xrt/ggml-xrt.cpp —
+// context init (:2794-2983), weight upload (:735-765), act input/output copies (:1136-1143, :1428-1451), state
+// I/O (:455-500), launch + wait (:1241-1280), feature probe (:1284-1300), disable after failure (:2761-2770).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/b200q.h"
+#include "launch.h"
+#include "layout.h"
+#include "plan.h"
+
+using namespace b200q;
+
+namespace {
+
+// ---- NCCL, loaded on first use (the library has no link-time dependency on it) ---------------------------------
+typedef int nccl_result;
+typedef void *nccl_comm;
+struct NcclUniqueId { char internal[128]; };
+struct NcclApi {
+    bool loaded = false;
+    void *h = nullptr;
+    nccl_result (*get_unique_id)(NcclUniqueId *) = nullptr;
+    nccl_result (*comm_init_rank)(nccl_comm *, int, NcclUniqueId, int) = nullptr;
+    nccl_result (*all_gather)(const void *, void *, size_t, int, nccl_comm, cudaStream_t) = nullptr;
+    nccl_result (*comm_destroy)(nccl_comm) = nullptr;
+    const char *(*get_error_string)(nccl_result) = nullptr;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+constexpr int kNcclFloat32 = 7;
+
+bool load_nccl(std::string &err) {
+    std::lock_guard<std::mutex> lock(g_nccl_mu);
+    if (g_nccl.loaded) return true;
+    const char *names[] = {"libnccl.so.2", "libnccl.so"};
+    for (const char *n : names) {
+        g_nccl.h = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+        if (g_nccl.h) break;
+    }
+    if (!g_nccl.h) {
+        err = "libnccl.so.2 not found";
+        return false;
+    }
+    g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(g_nccl.h, "ncclGetUniqueId"));
+    g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(g_nccl.h, "ncclCommInitRank"));
+    g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(g_nccl.h, "ncclAllGather"));
+    g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(g_nccl.h, "ncclCommDestroy"));
+    g_nccl.get_error_string = reinterpret_cast<decltype(g_nccl.get_error_string)>(dlsym(g_nccl.h, "ncclGetErrorString"));
+    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.all_gather || !g_nccl.comm_destroy) {
+        err = "libnccl.so.2 lacks an entry point";
+        return false;
+    }
+    g_nccl.loaded = true;
+    return true;
+}
+
+constexpr size_t kSnapFloats = size_t(1) << 20;  // snapshot scratch (overlapping in/out ranges)
+constexpr unsigned kMaxTraceEvents = 4096;
+
+}  // namespace
+
+struct b200q_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int sms = 148;
+    uint8_t *warena = nullptr;
+    size_t wbytes = 0, wused = 0;
+    float *act = nullptr;
+    size_t act_floats = 0;
+    float *state = nullptr;
+    size_t state_rows = 0;
+    uint16_t *kv = nullptr;
+    size_t kv_bytes = 0;
+    unsigned kv_ctx = 0;
+    // scratch: pre-quantized x, the stored deferred norm row, snapshots, debug outputs, trace stamps
+    int8_t *xq = nullptr;
+    float *xd = nullptr, *xs = nullptr;
+    int32_t *xb = nullptr;
+    uint16_t *xd16 = nullptr;
+    float *ndrow = nullptr;
+    float *snap = nullptr;
+    size_t snap_used = 0;
+    unsigned *dstatus = nullptr;
+    unsigned long long *tstamps = nullptr;
+    uint32_t *ttags = nullptr;
+    std::vector<uint32_t> host_tags;
+    unsigned n_events = 0;
+    std::vector<WeightInfo> weights;
+    bool disabled = false;
+    std::string err;
+    int world = 1, rank = 0;
+    nccl_comm comm = nullptr;
+    bool pdl = true;
+    unsigned launches = 0;  // kernels launched by the last executed list
+    std::mutex mu;
+};
+
+struct b200q_graph {
+    b200q_ctx *ctx = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    unsigned kernels = 0;
+};
+
+namespace {
+
+int set_err(b200q_ctx *c, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    c->err = buf;
+    if (code == B200Q_ERR_CUDA) c->disabled = true;
+    return code;
+}
+
+#define CUDA_TRY(c, expr)                                                                                          \
+    do {                                                                                                           \
+        cudaError_t e_ = (expr);                                                                                   \
+        if (e_ != cudaSuccess) return set_err((c), B200Q_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_));       \
+    } while (0)
+
+const WeightInfo *find_w(const b200q_ctx *c, uint64_t h) {
+    for (const WeightInfo &w : c->weights)
+        if (w.handle == h) return &w;
+    return nullptr;
+}
+
+MatrixView view_of(const b200q_ctx *c, const WeightInfo &w) {
+    MatrixView v;
+    v.base = c->warena + w.base_off;
+    v.format = w.format;
+    v.rows = w.row_end - w.row_begin;
+    v.row0 = w.row_begin;
+    v.rt = w.rt;
+    v.ct = w.ct;
+    v.kc = w.kc;
+    v.n_rt = w.n_rt;
+    v.tile_bytes = w.tile_bytes;
+    v.qs_part = w.qs_part;
+    v.dm_part = w.dm_part;
+    return v;
+}
+
+bool meet(const float *a, size_t an, const float *b, size_t bn) { return a < b + bn && b < a + an; }
+
+struct Range {
+    const float *p;
+    size_t n;
+};
+
+// An input that a kernel of the same launch writes with a different element mapping: copy it first.
+const float *snap_if(b200q_ctx *c, const float *in, size_t n, const std::vector<Range> &writes, const float *same_ok,
+                     int &rc) {
+    bool hit = false;
+    for (const Range &w : writes) {
+        if (!meet(in, n, w.p, w.n)) continue;
+        if (same_ok && in == same_ok && w.p == same_ok) continue;  // element-aligned in place
+        hit = true;
+    }
+    if (!hit) return in;
+    if (c->snap_used + n > kSnapFloats) {
+        rc = set_err(c, B200Q_ERR_NOMEM, "snapshot scratch full");
+        return in;
+    }
+    float *dst = c->snap + c->snap_used;
+    c->snap_used += (n + 63) / 64 * 64;
+    cudaError_t e = cudaMemcpyAsync(dst, in, n * sizeof(float), cudaMemcpyDeviceToDevice, c->stream);
+    if (e != cudaSuccess) rc = set_err(c, B200Q_ERR_CUDA, "snapshot copy: %s", cudaGetErrorString(e));
+    return dst;
+}
+
+int all_gather_rows(b200q_ctx *c, float *base, size_t per_rank) {
+    if (c->world <= 1) return 0;
+    const int r = g_nccl.all_gather(base + per_rank * c->rank, base, per_rank, kNcclFloat32, c->comm, c->stream);
+    if (r != 0) return set_err(c, B200Q_ERR_COMM, "ncclAllGather: %s", g_nccl.get_error_string ? g_nccl.get_error_string(r) : "?");
+    return 0;
+}
+
+// ---- one GEMV group ------------------------------------------------------------------------------------------------
+int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsigned cols, bool from_nd,
+              const DeferredNorm &nd, bool prequant, const float *x_override, int32_t *dbg) {
+    GemvArgs a;
+    a.cols = cols;
+    const unsigned act = act_type(mem[0].format);
+    const bool kq = act == 2;
+    if (x_override) {
+        a.x = x_override;
+    } else if (from_nd && nd.materialize) {
+        a.x = c->ndrow;
+    } else if (from_nd) {
+        a.x = c->act + nd.x_off;
+        a.norm_w = c->act + nd.w_off;
+        a.norm_eps = nd.eps;
+        a.norm_mode = 8u | nd.flags;
+    } else {
+        a.x = c->act + x_off;
+    }
+    int rc = 0;
+    std::vector<Range> writes;
+    bool shard = false;
+    for (unsigned i = 0; i < nm; ++i) {
+        const Member &m = mem[i];
+        const WeightInfo *w = m.w ? m.w : find_w(c, m.handle);
+        if (!w) return set_err(c, B200Q_ERR_ARG, "unknown weight handle");
+        GemvMemberArgs &g = a.m[i];
+        g.w = view_of(c, *w);
+        shard |= g.w.rows != w->rows;
+        g.epi = m.epi;
+        g.total_rows = m.rows;
+        g.y = c->act + m.y_off;
+        if (m.epi == EpiAdd) g.res = c->act + m.r_off;
+        if (m.epi == EpiConv) {
+            g.cw = c->act + m.c_w;
+            g.cs = c->act + m.c_src;
+            g.cd = c->act + m.c_dst;
+            g.csilu = m.c_silu;
+        }
+        if (m.epi != EpiSwigluG) {
+            writes.push_back({g.y, (m.epi == EpiConv || m.epi == EpiAdd) ? m.rows : round16(m.rows)});
+            if (m.epi == EpiConv) writes.push_back({g.cd, size_t(3) * m.rows});
+        }
+    }
+    a.n_members = nm;
+    // inputs read per row by the thread that writes the row: in place is fine, other overlaps are copied first
+    for (unsigned i = 0; i < nm; ++i) {
+        GemvMemberArgs &g = a.m[i];
+        if (g.res) g.res = snap_if(c, g.res, mem[i].rows, writes, g.y, rc);
+        if (g.cs) g.cs = snap_if(c, g.cs, size_t(3) * mem[i].rows, writes, g.cd, rc);
+        if (g.cw) g.cw = snap_if(c, g.cw, size_t(4) * mem[i].rows, writes, nullptr, rc);
+    }
+    if (rc) return rc;
+    if (dbg) a.dbg = dbg;
+    // x read by every CTA while others write: quantize it first when a member's output overlaps it
+    bool xhit = false;
+    for (const Range &w : writes) xhit |= meet(a.x, cols, w.p, w.n);
+    if (a.norm_w) for (const Range &w : writes) xhit |= meet(a.norm_w, cols, w.p, w.n);
+    if ((prequant || xhit) && !dbg) {
+        QuantArgs q;
+        q.x = a.x;
+        q.n = cols;
+        q.act = act;
+        q.norm_w = a.norm_w;
+        q.norm_eps = a.norm_eps;
+        q.norm_mode = a.norm_mode;
+        q.q = c->xq;
+        q.d = c->xd;
+        q.s = c->xs;
+        q.b = c->xb;
+        CUDA_TRY(c, launch_quantize(q, c->stream));
+        ++c->launches;
+        a.xq = c->xq;
+        a.xd = c->xd;
+        a.xs = c->xs;
+        a.xb = c->xb;
+    }
+    // work units (a member, or a SwiGLU pair) and their row tiles
+    unsigned u = 0, items = 0;
+    for (unsigned i = 0; i < nm; ++i) {
+        const bool pair = mem[i].epi == EpiSwigluG && i + 1 < nm;
+        a.unit_member[u] = i;
+        a.unit_pair[u] = pair ? int(i + 1) : -1;
+        a.item_start[u] = items;
+        items += a.m[i].w.n_rt;
+        ++u;
+        if (pair) ++i;
+    }
+    a.n_units = u;
+    a.item_start[u] = items;
+    a.err = c->dstatus + 1;
+    size_t smem = 0;
+    if (kq) plan_gemv_kq(a, smem);
+    else plan_gemv_q8(a, smem);
+    const unsigned per_sm = smem <= 113 * 1024 ? 2u : 1u;
+    const unsigned grid = std::min(items, unsigned(c->sms) * per_sm);
+    CUDA_TRY(c, kq ? launch_gemv_kq(a, grid, smem, c->stream, c->pdl) : launch_gemv_q8(a, grid, smem, c->stream, c->pdl));
+    ++c->launches;
+    if (shard && !dbg) {
+        for (unsigned i = 0; i < nm; ++i) {
+            const GemvMemberArgs &g = a.m[i];
+            if (g.epi == EpiSwigluG || g.w.rows == mem[i].rows) continue;
+            const size_t per = g.w.rows;
+            if ((rc = all_gather_rows(c, g.y, per))) return rc;
+            if (g.epi == EpiConv && (rc = all_gather_rows(c, g.cd, 3 * per))) return rc;
+        }
+    }
+    return 0;
+}
+
+int exec_elementwise(b200q_ctx *c, const Pass &p) {
+    const uint32_t *cmd = p.cmd[0];
+    float *A = c->act;
+    int rc = 0;
+    switch (p.op) {
+    case 2: {  // RMSNORM stored
+        const unsigned n = cmd[1], rows = cmd[6] ? cmd[6] : 1u, stride = (cmd[7] >> 8) & 0xffffu;
+        const unsigned xs = stride ? stride * 16 : n;
+        float *y = A + cmd[4];
+        std::vector<Range> w{{y, size_t(rows) * n}};
+        const float *x = snap_if(c, A + cmd[2], size_t(rows - 1) * xs + n, w, xs == n ? y : nullptr, rc);
+        const float *wt = (cmd[7] & 2u) ? nullptr : snap_if(c, A + cmd[3], n, w, nullptr, rc);
+        if (rc) return rc;
+        CUDA_TRY(c, launch_rmsnorm(x, wt, y, n, rows, xs, *reinterpret_cast<const float *>(&cmd[5]), cmd[7] & 3u,
+                                   c->stream, c->pdl));
+        break;
+    }
+    case 3: case 4: case 5: case 6: {
+        EwArgs e;
+        e.op = p.op;
+        e.n = cmd[1];
+        e.y = A + cmd[4];
+        const bool unary = p.op == 6;
+        e.row = unary ? cmd[5] : (p.op == 4 ? cmd[6] : 0u);
+        e.stride = unary ? cmd[6] : cmd[7];
+        e.kind = unary ? cmd[3] : 0u;
+        e.sigmoid = p.op == 4 ? (cmd[5] & 1u) : 0u;
+        std::vector<Range> w{{e.y, e.n}};
+        const size_t span = e.row ? size_t(e.n / e.row - 1) * e.stride + e.row : e.n;
+        e.a = snap_if(c, A + cmd[2], span, w, e.row ? nullptr : e.y, rc);
+        if (!unary) e.b = snap_if(c, A + cmd[3], e.n, w, e.y, rc);
+        if (rc) return rc;
+        CUDA_TRY(c, launch_ew(e, c->stream, c->pdl));
+        break;
+    }
+    case 8: {  // CONV
+        const unsigned ch = cmd[1];
+        float *y = A + cmd[4], *sd = A + cmd[6];
+        std::vector<Range> w{{y, ch}, {sd, size_t(3) * ch}};
+        const float *x = snap_if(c, A + cmd[2], ch, w, y, rc);
+        const float *wt = snap_if(c, A + cmd[3], size_t(4) * ch, w, nullptr, rc);
+        const float *ss = snap_if(c, A + cmd[5], size_t(3) * ch, w, sd, rc);
+        if (rc) return rc;
+        CUDA_TRY(c, launch_conv(x, wt, y, ss, sd, ch, cmd[7] & 1u, c->stream, c->pdl));
+        break;
+    }
+    case 10: {  // ROPE
+        const unsigned nd = cmd[1], ne0 = cmd[5], rows = cmd[6];
+        float *y = A + cmd[4];
+        std::vector<Range> w{{y, size_t(ne0) * rows}};
+        const float *x = snap_if(c, A + cmd[2], size_t(ne0) * rows, w, y, rc);
+        const float *cs = snap_if(c, A + cmd[3], nd, w, nullptr, rc);
+        if (rc) return rc;
+        CUDA_TRY(c, launch_rope(x, cs, y, nd, ne0, rows, c->stream, c->pdl));
+        break;
+    }
+    default: return set_err(c, B200Q_ERR_ARG, "unexpected element-wise opcode %u", p.op);
+    }
+    ++c->launches;
+    return 0;
+}
+
+int exec_gdn(b200q_ctx *c, const Pass &p) {
+    const uint32_t *cmd = p.cmd[0], *ext = p.cmd[1], *ext2 = p.cmd[2];
+    float *A = c->act;
+    GdnArgs g;
+    g.hv = cmd[1] & 0xffffu;
+    g.hk = cmd[1] >> 16;
+    const unsigned fl = ext[3], S = 128;
+    g.y = A + cmd[7];
+    std::vector<Range> w{{g.y, size_t(g.hv) * S}};
+    int rc = 0;
+    g.q = snap_if(c, A + cmd[2], size_t(g.hk) * S, w, nullptr, rc);
+    g.k = snap_if(c, A + cmd[3], size_t(g.hk) * S, w, nullptr, rc);
+    g.v = snap_if(c, A + cmd[4], size_t(g.hv) * S, w, g.y, rc);
+    g.g = snap_if(c, A + cmd[5], g.hv, w, nullptr, rc);
+    g.beta = snap_if(c, A + cmd[6], g.hv, w, nullptr, rc);
+    g.state_in = c->state + size_t(ext[0]) * S;
+    g.state_out = c->state + size_t(ext[1]) * S;
+    g.scale = *reinterpret_cast<const float *>(&ext[2]);
+    g.l2 = (fl & 2u) ? 1u : 0u;
+    g.l2_eps = *reinterpret_cast<const float *>(&ext[4]);
+    g.rms_eps = *reinterpret_cast<const float *>(&ext[5]);
+    if (fl & 4u) {
+        g.wn = snap_if(c, A + ext[6], S, w, nullptr, rc);
+        g.z = snap_if(c, A + ext[7], size_t(g.hv) * S, w, g.y, rc);
+    }
+    if (fl & 8u) {
+        g.dt = snap_if(c, A + ext2[0], g.hv, w, nullptr, rc);
+        g.a = snap_if(c, A + ext2[1], g.hv, w, nullptr, rc);
+    }
+    if (rc) return rc;
+    CUDA_TRY(c, launch_gdn(g, c->stream, c->pdl));
+    ++c->launches;
+    DeferredNorm none;
+    if (p.gdn_with_gemv) {
+        if ((rc = exec_gemv(c, &p.gdn_gemv, 1, p.gdn_gemv.x_off, p.gdn_gemv.cols, false, none, false, nullptr,
+                            nullptr)))
+            return rc;
+    }
+    if (p.gdn_with_out) {
+        if ((rc = exec_gemv(c, &p.gdn_out, 1, cmd[7], p.gdn_out.cols, false, none, false, nullptr, nullptr)))
+            return rc;
+    }
+    return 0;
+}
+
+int exec_ext(b200q_ctx *c, const Pass &p) {
+    const uint32_t *cmd = p.cmd[0];
+    float *A = c->act;
+    int rc = 0;
+    if (p.op == 12) {
+        AttnArgs t;
+        t.n_head = cmd[1] & 0xffu;
+        t.n_kv_head = (cmd[1] >> 8) & 0xffu;
+        t.head_dim = (cmd[1] >> 16) * 16u;
+        t.pos = cmd[6];
+        t.kv_ctx = c->kv_ctx;
+        t.y = A + cmd[5];
+        std::vector<Range> w{{t.y, size_t(t.n_head) * t.head_dim}};
+        t.q = snap_if(c, A + cmd[2], size_t(t.n_head) * t.head_dim, w, nullptr, rc);
+        t.k = snap_if(c, A + cmd[3], size_t(t.n_kv_head) * t.head_dim, w, nullptr, rc);
+        t.v = snap_if(c, A + cmd[4], size_t(t.n_kv_head) * t.head_dim, w, nullptr, rc);
+        if (rc) return rc;
+        const size_t slot_elems = size_t(t.n_kv_head) * c->kv_ctx * t.head_dim;
+        t.kcache = c->kv + size_t(cmd[7]) * slot_elems * 2;
+        t.vcache = t.kcache + slot_elems;
+        t.scale = 1.0f / std::sqrt(float(t.head_dim));
+        CUDA_TRY(c, launch_attn(t, c->stream, c->pdl));
+    } else if (p.op == 13) {
+        CUDA_TRY(c, launch_argmax(A + cmd[2], cmd[1], A + cmd[3], c->stream, c->pdl));
+    } else if (p.op == 14) {
+        const WeightInfo *w = find_w(c, uint64_t(cmd[3]) | (uint64_t(cmd[4]) << 32));
+        if (!w) return set_err(c, B200Q_ERR_ARG, "GET_ROW: unknown weight");
+        float *y = A + cmd[6];
+        std::vector<Range> wr{{y, cmd[2]}};
+        const float *idx = snap_if(c, A + cmd[5], 1, wr, nullptr, rc);
+        if (rc) return rc;
+        CUDA_TRY(c, launch_get_row(view_of(c, *w), cmd[2], idx, y, c->dstatus, c->stream, c->pdl));
+    }
+    ++c->launches;
+    return 0;
+}
+
+int stamp(b200q_ctx *c, bool on, unsigned cmd, unsigned kind) {
+    if (!on || c->n_events >= kMaxTraceEvents) return 0;
+    c->host_tags.push_back((cmd & 0xffffu) | (kind << 16));
+    CUDA_TRY(c, launch_trace_stamp(c->tstamps + c->n_events, c->stream));
+    ++c->n_events;
+    return 0;
+}
+
+// Executes the passes of a plan on the context stream (no synchronization).
+int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
+    c->snap_used = 0;
+    c->launches = 0;
+    c->n_events = 0;
+    c->host_tags.clear();
+    const bool tr = plan.has_trace;
+    int rc = 0;
+    for (const Pass &p : plan.passes) {
+        if ((rc = stamp(c, tr, p.first, 0))) return rc;
+        const bool is_pass = p.kind == PassKind::Gemv || p.kind == PassKind::Gdn;
+        if (is_pass && (rc = stamp(c, tr, p.first, 1))) return rc;
+        switch (p.kind) {
+        case PassKind::Gemv:
+            rc = exec_gemv(c, p.m, p.n_members, p.x_off, p.cols, p.from_nd, p.nd, p.prequant, nullptr, nullptr);
+            break;
+        case PassKind::Elementwise: rc = exec_elementwise(c, p); break;
+        case PassKind::Gdn: rc = exec_gdn(c, p); break;
+        case PassKind::Ext: rc = exec_ext(c, p); break;
+        case PassKind::Nop:
+            if (p.nd_store) {  // a deferred RMSNORM whose x or weight changes before its GEMVs: store its row now
+                const DeferredNorm &nd = p.nd;
+                CUDA_TRY(c, launch_rmsnorm(c->act + nd.x_off, c->act + nd.w_off, c->ndrow, nd.n, 1, nd.n, nd.eps,
+                                           nd.flags, c->stream, c->pdl));
+                ++c->launches;
+            }
+            break;
+        }
+        if (rc) return rc;
+        if (is_pass && (rc = stamp(c, tr, p.first, 2))) return rc;
+    }
+    if (tr) {
+        const unsigned end_c = plan.status ? unsigned(plan.status - 1) : n_cmds;
+        if ((rc = stamp(c, tr, end_c, 0))) return rc;
+        if ((rc = stamp(c, tr, end_c + 1, 3))) return rc;
+        CUDA_TRY(c, cudaMemcpyAsync(c->ttags, c->host_tags.data(), sizeof(uint32_t) * c->n_events,
+                                    cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(c, launch_trace_write(c->tstamps, c->ttags, c->n_events, c->act + plan.trace_off, c->stream));
+        c->launches += c->n_events + 1;
+    }
+    return 0;
+}
+
+Limits limits_of(const b200q_ctx *c) {
+    Limits L;
+    L.act_floats = c->act_floats;
+    L.state_rows = c->state_rows;
+    L.kv_bytes = c->kv_bytes;
+    L.kv_ctx = c->kv_ctx;
+    L.check_weights = true;
+    L.weights = &c->weights;
+    return L;
+}
+
+int check_ctx(b200q_ctx *c) {
+    if (!c) return B200Q_ERR_ARG;
+    if (c->disabled) return B200Q_ERR_DISABLED;
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return set_err(c, B200Q_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+bool shardable(const b200q_ctx *c, unsigned rows, unsigned flags) {
+    return c->world > 1 && !(flags & B200Q_UPLOAD_REPLICATE) && rows % (16u * unsigned(c->world)) == 0;
+}
+
+}  // namespace
+
+// =================================================================================================================
+extern "C" {
+
+void b200q_features(uint32_t out[3]) {
+    out[0] = B200Q_FEATURES;
+    out[1] = B200Q_FEATURES2;
+    out[2] = B200Q_FEATURES3;
+}
+
+int b200q_create(const b200q_config *cfg, b200q_ctx **out) {
+    if (!cfg || !out) return B200Q_ERR_ARG;
+    *out = nullptr;
+    if (cfg->act_floats < 16 || cfg->act_floats % 16) return B200Q_ERR_ARG;
+    b200q_ctx *c = new b200q_ctx();
+    c->device = cfg->device;
+    auto fail = [&](cudaError_t e, const char *what) {
+        fprintf(stderr, "b200q_create: %s: %s\n", what, cudaGetErrorString(e));
+        b200q_destroy(c);
+        return B200Q_ERR_CUDA;
+    };
+    cudaError_t e;
+    if ((e = cudaSetDevice(cfg->device)) != cudaSuccess) return fail(e, "cudaSetDevice");
+    cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, cfg->device);
+    if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) return fail(e, "stream");
+    c->wbytes = cfg->weight_bytes;
+    if (c->wbytes && (e = cudaMalloc(&c->warena, c->wbytes)) != cudaSuccess) return fail(e, "weight arena");
+    c->act_floats = cfg->act_floats;
+    if ((e = cudaMalloc(&c->act, c->act_floats * sizeof(float))) != cudaSuccess) return fail(e, "act");
+    cudaMemset(c->act, 0, c->act_floats * sizeof(float));
+    c->state_rows = cfg->state_rows;
+    if (c->state_rows) {
+        if ((e = cudaMalloc(&c->state, c->state_rows * 128 * sizeof(float))) != cudaSuccess) return fail(e, "state");
+        cudaMemset(c->state, 0, c->state_rows * 128 * sizeof(float));
+    }
+    c->kv_bytes = cfg->kv_bytes;
+    c->kv_ctx = cfg->kv_ctx;
+    if (c->kv_bytes) {
+        if ((e = cudaMalloc(&c->kv, c->kv_bytes)) != cudaSuccess) return fail(e, "kv");
+        cudaMemset(c->kv, 0, c->kv_bytes);
+    }
+    const size_t scratch = kMaxCols + 4 * (kMaxCols / 16) * 4 + kMaxCols * 4 + kSnapFloats * 4 + 4096 +
+                           kMaxTraceEvents * 12;
+    uint8_t *s = nullptr;
+    if ((e = cudaMalloc(&s, scratch)) != cudaSuccess) return fail(e, "scratch");
+    cudaMemset(s, 0, scratch);
+    c->xq = reinterpret_cast<int8_t *>(s);
+    s += kMaxCols;
+    c->xd = reinterpret_cast<float *>(s);
+    s += kMaxCols / 16 * 4;
+    c->xs = reinterpret_cast<float *>(s);
+    s += kMaxCols / 16 * 4;
+    c->xb = reinterpret_cast<int32_t *>(s);
+    s += kMaxCols / 16 * 4;
+    c->xd16 = reinterpret_cast<uint16_t *>(s);
+    s += kMaxCols / 16 * 4;
+    c->ndrow = reinterpret_cast<float *>(s);
+    s += kMaxCols * 4;
+    c->snap = reinterpret_cast<float *>(s);
+    s += kSnapFloats * 4;
+    c->dstatus = reinterpret_cast<unsigned *>(s);
+    s += 4096;
+    c->tstamps = reinterpret_cast<unsigned long long *>(s);
+    s += kMaxTraceEvents * 8;
+    c->ttags = reinterpret_cast<uint32_t *>(s);
+    const char *pdl = getenv("B200Q_NO_PDL");
+    c->pdl = !(pdl && pdl[0] == '1');
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return fail(e, "init");
+    *out = c;
+    return 0;
+}
+
+void b200q_destroy(b200q_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->comm && g_nccl.comm_destroy) g_nccl.comm_destroy(c->comm);
+    cudaFree(c->warena);
+    cudaFree(c->act);
+    cudaFree(c->state);
+    cudaFree(c->kv);
+    cudaFree(c->xq);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+const char *b200q_last_error(const b200q_ctx *c) { return c ? c->err.c_str() : "null context"; }
+void *b200q_stream(b200q_ctx *c) { return c ? c->stream : nullptr; }
+void *b200q_act_device_ptr(b200q_ctx *c) { return c ? c->act : nullptr; }
+void *b200q_state_device_ptr(b200q_ctx *c) { return c ? c->state : nullptr; }
+void *b200q_kv_device_ptr(b200q_ctx *c) { return c ? c->kv : nullptr; }
+
+int b200q_synchronize(b200q_ctx *c) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+size_t b200q_gguf_row_bytes(unsigned cols, unsigned format) { return gguf_row_bytes(cols, format); }
+
+size_t b200q_weight_device_bytes(unsigned rows, unsigned cols, unsigned format) {
+    if (!format_supported(format)) return 0;
+    return device_layout(rows, cols, format, 148).total;
+}
+
+int b200q_upload_weight_ex(b200q_ctx *c, const void *gguf, unsigned rows, unsigned cols, unsigned format,
+                           unsigned block_cols, unsigned flags, uint64_t *w_off) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(c->mu);
+    if (!gguf || !w_off || !format_supported(format) || rows == 0 || rows > 1u << 20 || cols == 0 ||
+        cols > kMaxCols || cols % ((format == 13 || format == 14) ? 256u : 32u) != 0 ||
+        (block_cols != 0 && block_cols != 256))
+        return set_err(c, B200Q_ERR_ARG, "upload: bad shape or format");
+    unsigned r0 = 0, r1 = rows;
+    if (shardable(c, rows, flags)) {
+        const unsigned per = rows / unsigned(c->world);
+        r0 = per * unsigned(c->rank);
+        r1 = r0 + per;
+    }
+    const DeviceLayout L = device_layout(r1 - r0, cols, format, unsigned(c->sms));
+    if (c->wused + L.total > c->wbytes) return set_err(c, B200Q_ERR_NOMEM, "weight arena full");
+    std::vector<uint8_t> host(L.total);
+    repack_rows(static_cast<const uint8_t *>(gguf), r0, r1, L, host.data());
+    CUDA_TRY(c, cudaMemcpy(c->warena + c->wused, host.data(), L.total, cudaMemcpyHostToDevice));
+    WeightInfo w;
+    w.handle = c->wused;
+    w.format = format;
+    w.rows = rows;
+    w.cols = cols;
+    w.row_begin = r0;
+    w.row_end = r1;
+    w.base_off = c->wused;
+    w.rt = L.rt;
+    w.ct = L.ct;
+    w.kc = L.kc;
+    w.n_rt = L.n_rt;
+    w.tile_bytes = L.tile_bytes;
+    w.qs_part = L.qs_part;
+    w.dm_part = L.dm_part;
+    c->weights.push_back(w);
+    *w_off = w.handle;
+    c->wused += (L.total + 255) & ~size_t(255);
+    return 0;
+}
+
+int b200q_upload_weight(b200q_ctx *c, const void *gguf, unsigned rows, unsigned cols, unsigned format,
+                        unsigned block_cols, uint64_t *w_off) {
+    return b200q_upload_weight_ex(c, gguf, rows, cols, format, block_cols, 0, w_off);
+}
+
+int b200q_weights_reset(b200q_ctx *c) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(c->mu);
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    c->weights.clear();
+    c->wused = 0;
+    return 0;
+}
+
+int b200q_act_write(b200q_ctx *c, size_t off, const float *src, size_t n) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!src || off > c->act_floats || n > c->act_floats - off) return set_err(c, B200Q_ERR_ARG, "act_write range");
+    CUDA_TRY(c, cudaMemcpyAsync(c->act + off, src, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+int b200q_act_read(b200q_ctx *c, size_t off, float *dst, size_t n) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!dst || off > c->act_floats || n > c->act_floats - off) return set_err(c, B200Q_ERR_ARG, "act_read range");
+    CUDA_TRY(c, cudaMemcpyAsync(dst, c->act + off, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+int b200q_act_fill(b200q_ctx *c, size_t off, float value, size_t n) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (off > c->act_floats || n > c->act_floats - off) return set_err(c, B200Q_ERR_ARG, "act_fill range");
+    std::vector<float> v(n, value);
+    CUDA_TRY(c, cudaMemcpy(c->act + off, v.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int b200q_state_write(b200q_ctx *c, size_t row, const float *src, size_t rows) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!src || row > c->state_rows || rows > c->state_rows - row) return set_err(c, B200Q_ERR_ARG, "state range");
+    CUDA_TRY(c, cudaMemcpy(c->state + row * 128, src, rows * 128 * sizeof(float), cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int b200q_state_read(b200q_ctx *c, size_t row, float *dst, size_t rows) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!dst || row > c->state_rows || rows > c->state_rows - row) return set_err(c, B200Q_ERR_ARG, "state range");
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    CUDA_TRY(c, cudaMemcpy(dst, c->state + row * 128, rows * 128 * sizeof(float), cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int b200q_kv_write(b200q_ctx *c, size_t byte_off, const void *src, size_t bytes) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!src || byte_off > c->kv_bytes || bytes > c->kv_bytes - byte_off) return set_err(c, B200Q_ERR_ARG, "kv range");
+    CUDA_TRY(c, cudaMemcpy(reinterpret_cast<uint8_t *>(c->kv) + byte_off, src, bytes, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int b200q_run_async(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(c->mu);
+    if (n_cmds == 0) {  // feature probe (gemvqc16.h:124-134)
+        uint32_t f[3];
+        b200q_features(f);
+        CUDA_TRY(c, cudaMemcpyAsync(c->act, f, sizeof(f), cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+        return 0;
+    }
+    if (!cmds) return B200Q_ERR_ARG;
+    const Plan plan = plan_list(cmds, n_cmds, limits_of(c));
+    if (plan.status == 129) return 129;
+    if ((rc = exec_plan(c, plan, n_cmds))) return rc;
+    if (plan.status) c->err = plan.error;
+    return plan.status;
+}
+
+int b200q_run(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
+    const int status = b200q_run_async(c, cmds, n_cmds);
+    if (status < 0) return status;
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    return status;
+}
+
+int b200q_graph_create(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds, b200q_graph **out) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!out || (!cmds && n_cmds)) return B200Q_ERR_ARG;
+    *out = nullptr;
+    std::lock_guard<std::mutex> lock(c->mu);
+    const Plan plan = plan_list(cmds, n_cmds, limits_of(c));
+    if (plan.status) {
+        c->err = plan.error;
+        return plan.status;
+    }
+    b200q_graph *g = new b200q_graph();
+    g->ctx = c;
+    CUDA_TRY(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    rc = exec_plan(c, plan, n_cmds);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+    if (rc || e != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        delete g;
+        return rc ? rc : set_err(c, B200Q_ERR_CUDA, "capture: %s", cudaGetErrorString(e));
+    }
+    g->graph = graph;
+    g->kernels = c->launches;
+    const cudaError_t ie = cudaGraphInstantiate(&g->exec, graph, 0);
+    if (ie != cudaSuccess) {
+        cudaGraphDestroy(graph);
+        delete g;
+        return set_err(c, B200Q_ERR_CUDA, "instantiate: %s", cudaGetErrorString(ie));
+    }
+    *out = g;
+    return 0;
+}
+
+int b200q_graph_launch(b200q_ctx *c, b200q_graph *g) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!g || g->ctx != c) return B200Q_ERR_STATE;
+    CUDA_TRY(c, cudaGraphLaunch(g->exec, c->stream));
+    return 0;
+}
+
+int b200q_graph_launch_many(b200q_ctx *c, b200q_graph *const *graphs, unsigned n_graphs, unsigned launches) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!graphs || n_graphs == 0) return B200Q_ERR_ARG;
+    for (unsigned i = 0; i < n_graphs; ++i)
+        if (!graphs[i] || graphs[i]->ctx != c) return B200Q_ERR_STATE;
+    for (unsigned i = 0; i < launches; ++i) CUDA_TRY(c, cudaGraphLaunch(graphs[i % n_graphs]->exec, c->stream));
+    return 0;
+}
+
+void b200q_graph_destroy(b200q_graph *g) {
+    if (!g) return;
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    delete g;
+}
+
+unsigned b200q_graph_kernel_count(const b200q_graph *g) { return g ? g->kernels : 0; }
+
+int b200q_plan(const uint32_t *cmds, unsigned n_cmds, b200q_pass_info *passes, unsigned max_passes,
+               unsigned *n_passes) {
+    if (n_passes) *n_passes = 0;
+    if (n_cmds == 0) return 0;
+    if (!cmds) return B200Q_ERR_ARG;
+    Limits L;
+    L.kv_ctx = 1u << 30;
+    const Plan plan = plan_list(cmds, n_cmds, L);
+    unsigned k = 0;
+    for (const Pass &p : plan.passes) {
+        if (passes && k < max_passes) {
+            b200q_pass_info &o = passes[k];
+            o.first_cmd = p.first;
+            o.n_cmds = p.count;
+            o.kind = uint32_t(p.kind);
+            o.n_members = p.kind == PassKind::Gemv ? p.n_members
+                                                   : (p.kind == PassKind::Gdn ? unsigned(p.gdn_with_gemv) + unsigned(p.gdn_with_out) : 0u);
+            o.fused_norm = p.from_nd ? 1u : 0u;
+        }
+        ++k;
+    }
+    if (n_passes) *n_passes = k;
+    return plan.status;
+}
+
+int b200q_debug_quantize(b200q_ctx *c, unsigned format, size_t x_off, unsigned n, uint32_t norm_w_off,
+                         float norm_eps, unsigned norm_flags, int8_t *q, void *scales, int32_t *bsums) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(c->mu);
+    const unsigned act = act_type(format);
+    if (!format_supported(format) || n == 0 || n > kMaxCols || n % (act == 2 ? 256u : 32u) || x_off % 16 ||
+        x_off + n > c->act_floats || (norm_w_off != UINT32_MAX && norm_w_off + size_t(n) > c->act_floats))
+        return set_err(c, B200Q_ERR_ARG, "debug_quantize: bad arguments");
+    QuantArgs a;
+    a.x = c->act + x_off;
+    a.n = n;
+    a.act = act;
+    if (norm_w_off != UINT32_MAX) {
+        a.norm_w = c->act + norm_w_off;
+        a.norm_eps = norm_eps;
+        a.norm_mode = 8u | (norm_flags & 3u);
+    }
+    a.q = c->xq;
+    a.d = c->xd;
+    a.s = c->xs;
+    a.b = c->xb;
+    a.d16 = c->xd16;
+    CUDA_TRY(c, launch_quantize(a, c->stream));
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    if (q) CUDA_TRY(c, cudaMemcpy(q, c->xq, n, cudaMemcpyDeviceToHost));
+    if (scales) {
+        if (act == 0) CUDA_TRY(c, cudaMemcpy(scales, c->xd16, n / 32 * 2, cudaMemcpyDeviceToHost));
+        else if (act == 1) CUDA_TRY(c, cudaMemcpy(scales, c->xd16, n / 32 * 4, cudaMemcpyDeviceToHost));
+        else CUDA_TRY(c, cudaMemcpy(scales, c->xd, n / 256 * 4, cudaMemcpyDeviceToHost));
+    }
+    if (bsums) CUDA_TRY(c, cudaMemcpy(bsums, c->xb, (act == 2 ? n / 16 : n / 32) * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int b200q_debug_block_sums(b200q_ctx *c, const uint32_t cmd[8], int32_t *out) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!cmd || !out) return B200Q_ERR_ARG;
+    std::lock_guard<std::mutex> lock(c->mu);
+    uint32_t one[8];
+    std::memcpy(one, cmd, sizeof(one));
+    one[1] &= 0xffu;  // no epilogue
+    const Plan plan = plan_list(one, 1, limits_of(c));
+    if (plan.status || plan.passes.size() != 1 || plan.passes[0].kind != PassKind::Gemv)
+        return set_err(c, B200Q_ERR_ARG, "debug_block_sums: invalid GEMV (%s)", plan.error.c_str());
+    const Member &m = plan.passes[0].m[0];
+    const bool kq = act_type(m.format) == 2;
+    const size_t count = kq ? size_t(m.rows) * (m.cols / 256) * 9 : size_t(m.rows) * (m.cols / 32);
+    int32_t *d = nullptr;
+    CUDA_TRY(c, cudaMalloc(&d, count * 4));
+    cudaMemset(d, 0, count * 4);
+    DeferredNorm none;
+    rc = exec_gemv(c, &m, 1, one[6], m.cols, false, none, false, nullptr, d);
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (!rc && e == cudaSuccess) e = cudaMemcpy(out, d, count * 4, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (rc) return rc;
+    if (e != cudaSuccess) return set_err(c, B200Q_ERR_CUDA, "debug_block_sums: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int b200q_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms, b200q_layout_info *out) {
+    if (!out || !format_supported(format) || rows == 0 || cols == 0) return B200Q_ERR_ARG;
+    const DeviceLayout L = device_layout(rows, cols, format, sms);
+    if (L.blocks == 0) return B200Q_ERR_ARG;
+    out->rows_per_tile = L.rt;
+    out->blocks_per_tile = L.ct;
+    out->tiles_per_row_tile = L.kc;
+    out->row_tiles = L.n_rt;
+    out->tile_bytes = L.tile_bytes;
+    out->total_bytes = L.total;
+    return 0;
+}
+
+int b200q_repack_host(const void *gguf, unsigned rows, unsigned cols, unsigned format, unsigned sms, void *dst) {
+    if (!gguf || !dst || !format_supported(format) || rows == 0) return B200Q_ERR_ARG;
+    const DeviceLayout L = device_layout(rows, cols, format, sms);
+    if (L.blocks == 0) return B200Q_ERR_ARG;
+    repack_rows(static_cast<const uint8_t *>(gguf), 0, rows, L, static_cast<uint8_t *>(dst));
+    return 0;
+}
+
+int b200q_unpack_row_host(const void *dev, unsigned rows, unsigned cols, unsigned format, unsigned sms, unsigned row,
+                          void *gguf_row) {
+    if (!dev || !gguf_row || !format_supported(format) || row >= rows) return B200Q_ERR_ARG;
+    const DeviceLayout L = device_layout(rows, cols, format, sms);
+    if (L.blocks == 0) return B200Q_ERR_ARG;
+    unpack_row(static_cast<const uint8_t *>(dev), L, row, static_cast<uint8_t *>(gguf_row));
+    return 0;
+}
+
+int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]) {
+    std::string err;
+    if (!id || !load_nccl(err)) return B200Q_ERR_COMM;
+    NcclUniqueId u;
+    if (g_nccl.get_unique_id(&u) != 0) return B200Q_ERR_COMM;
+    std::memcpy(id, u.internal, B200Q_UNIQUE_ID_BYTES);
+    return 0;
+}
+
+int b200q_comm_init(b200q_ctx *c, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (world < 1 || rank < 0 || rank >= world || !id) return B200Q_ERR_ARG;
+    if (!c->weights.empty()) return set_err(c, B200Q_ERR_STATE, "comm_init after uploads");
+    if (world == 1) return 0;
+    std::string err;
+    if (!load_nccl(err)) return set_err(c, B200Q_ERR_COMM, "%s", err.c_str());
+    NcclUniqueId u;
+    std::memcpy(u.internal, id, B200Q_UNIQUE_ID_BYTES);
+    const int r = g_nccl.comm_init_rank(&c->comm, world, u, rank);
+    if (r != 0) return set_err(c, B200Q_ERR_COMM, "ncclCommInitRank: %d", r);
+    c->world = world;
+    c->rank = rank;
+    return 0;
+}
+
+int b200q_comm_world(const b200q_ctx *c) { return c ? c->world : 0; }
+
+}  // extern "C"

@@ -1,0 +1,101 @@
+// Gated DeltaNet decode step (ggml GATED_DELTA_NET, one token, scalar gate, head size 128): the reference's GDN
+// opcode (fpga/src/gemvqc16.cpp:801-904, gemvqc_gdn.h:74-346) with its CPU arithmetic (gemvq_ref.h:360-397):
+// per value head h (key head h % H_k) and state row j (column j of S):
+//   x = S_j * exp(g);  delta = (v_j - x . k) * beta;  S_j' = x + k * delta;  y_j = (S_j' . q) * scale
+// optionally with q/k L2-normalized per head (RMSNORM with flags 3), the gates beta = sigmoid(beta),
+// g = softplus(g + dt) * a, and the gated output (RMSNORM(y) * w) * silu(z) per head.
+//
+// One CTA per value head, one thread per state row: the thread holds its 128-float row in registers for the whole
+// step (read once, written once) and sums both dot products in index order with IEEE-rounded FP32 adds, the CPU
+// reference's order, so the new state and y match it bit for bit whenever exp() does.
+#include "launch.h"
+#include "quant.cuh"
+
+namespace b200q {
+
+__device__ __forceinline__ double cta128_sum(double v, double *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+    __syncthreads();
+    return ((red[0] + red[1]) + red[2]) + red[3];
+}
+
+__global__ void __launch_bounds__(128) gdn_kernel(const GdnArgs a) {
+    __shared__ float qs[128], ks[128];
+    __shared__ double red[4];
+    __shared__ float gate[2];
+    pdl_wait();
+    const unsigned h = blockIdx.x, kh = h % a.hk, j = threadIdx.x;
+    // state row of this thread: issue the loads first (the state is not written by earlier commands' other rows)
+    const float4 *src = reinterpret_cast<const float4 *>(a.state_in + (size_t(h) * 128 + j) * 128);
+    float row[128];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float4 v = src[i];
+        row[4 * i] = v.x;
+        row[4 * i + 1] = v.y;
+        row[4 * i + 2] = v.z;
+        row[4 * i + 3] = v.w;
+    }
+    float qv = a.q[kh * 128 + j], kv = a.k[kh * 128 + j];
+    if (a.l2) {  // 1 / fmaxf(sqrtf(float(sum x^2)), eps), x * scale (gemvq_ref.h:309-324 with flags 3)
+        const double sq = cta128_sum(double(fmul(qv, qv)), red);
+        const double sk = cta128_sum(double(fmul(kv, kv)), red);
+        qv = fmul(qv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sq)), a.l2_eps)));
+        kv = fmul(kv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sk)), a.l2_eps)));
+    }
+    qs[j] = qv;
+    ks[j] = kv;
+    if (j == 0) {
+        float g = a.g[h], b = a.beta[h];
+        if (a.dt) {  // gemvqc_gdn.h:265-280: g = softplus(g + dt) * a, beta = sigmoid(beta)
+            g = fmul(softplus_f32(fadd(g, a.dt[h])), a.a[h]);
+            b = sigmoid_f32(b);
+        }
+        gate[0] = exp_f32(g);
+        gate[1] = b;
+    }
+    __syncthreads();
+    const float decay = gate[0], beta = gate[1];
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 128; ++i) {
+        row[i] = fmul(row[i], decay);
+        dot = fadd(dot, fmul(row[i], ks[i]));
+    }
+    const float delta = fmul(fsub(a.v[h * 128 + j], dot), beta);
+    float out = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 128; ++i) {
+        row[i] = fadd(row[i], fmul(ks[i], delta));
+        out = fadd(out, fmul(row[i], qs[i]));
+    }
+    float4 *dst = reinterpret_cast<float4 *>(a.state_out + (size_t(h) * 128 + j) * 128);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) dst[i] = make_float4(row[4 * i], row[4 * i + 1], row[4 * i + 2], row[4 * i + 3]);
+    float yv = fmul(out, a.scale);
+    if (a.z) {  // (y * rms scale) * w, then silu(z) * that (RMSNORM + SILU_MUL, gemvqc_gdn.h:284-346)
+        const double s = cta128_sum(double(fmul(yv, yv)), red);
+        const float sc = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(s, 128.0)), a.rms_eps)));
+        const float nv = fmul(fmul(yv, sc), a.wn[j]);
+        yv = fmul(silu_f32(a.z[h * 128 + j]), nv);
+    }
+    a.y[h * 128 + j] = yv;
+}
+
+cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.hv);
+    cfg.blockDim = dim3(128);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gdn_kernel, a);
+}
+
+}  // namespace b200q

@@ -1,0 +1,74 @@
+// Launch argument blocks shared by the host executor (api.cpp) and the kernels. Plain structs of device pointers
+// and sizes, passed by value as kernel parameters.
+#pragma once
+#include <cstdint>
+
+namespace b200q {
+
+// One weight matrix in the device arena: the tiled layout of layout.h (tile (t, k) = R rows x C blocks, one
+// contiguous run of tile_bytes: quants, then scales, then the K-quant d/dmin part).
+struct MatrixView {
+    const uint8_t *base = nullptr;
+    unsigned format = 0;
+    unsigned rows = 0;            // rows held here (the local row slice)
+    unsigned row0 = 0;            // global index of the first local row
+    unsigned rt = 1, ct = 1, kc = 1, n_rt = 0;
+    unsigned tile_bytes = 0, qs_part = 0, dm_part = 0;
+};
+
+struct GemvMemberArgs {
+    MatrixView w;
+    float *y = nullptr;           // act + y_off (the member's output, global row indexing)
+    unsigned epi = 0;             // Epi (plan.h)
+    unsigned total_rows = 0;      // rows of the full matrix (zero padding of y up to a multiple of 16)
+    const float *res = nullptr;   // ADD residual (global row indexing)
+    const float *cw = nullptr;    // CONV kernel [4 x channels]
+    const float *cs = nullptr;    // CONV state in [3 x channels]
+    float *cd = nullptr;          // CONV state out
+    unsigned csilu = 0;
+};
+
+constexpr unsigned kMaxUnits = 4;
+
+struct GemvArgs {
+    const float *x = nullptr;     // act + x_off (or the deferred norm's x)
+    unsigned cols = 0;
+    // fused deferred RMSNORM (norm_mode bit 3 set: active; bits 0..1 the RMSNORM flags L2 / no weight)
+    const float *norm_w = nullptr;
+    float norm_eps = 0.0f;
+    unsigned norm_mode = 0;
+    // quantized x prepared by a separate launch (when a member's y overlaps x); null: quantize in the prologue
+    const int8_t *xq = nullptr;
+    const float *xd = nullptr;    // per 32-block scale (Q8_0: FP16 value as float; Q8_1: d) / per 256 (Q8_K)
+    const float *xs = nullptr;    // Q8_1: FP16 s as float
+    const int32_t *xb = nullptr;  // per-block sums of q (Q8_0/Q8_1) / per 16 (Q8_K)
+    GemvMemberArgs m[4];
+    unsigned n_members = 0;
+    // work units: a member alone, or a SwiGLU pair (g = unit_member, u = unit_pair); a work item is one row tile
+    // of a unit, streamed as the unit's kc tiles (pairs: the g and u tiles of the same rows in one stage)
+    unsigned n_units = 0;
+    unsigned unit_member[kMaxUnits] = {};
+    int unit_pair[kMaxUnits] = {-1, -1, -1, -1};
+    unsigned item_start[kMaxUnits + 1] = {};   // prefix sums of the units' row tiles
+    // shared-memory plan (host-computed): stages of stage_bytes, per-stage compute results, x image
+    unsigned n_stages = 0, stage_bytes = 0, res_bytes = 0;
+    unsigned *err = nullptr;      // set when a bounded wait runs out
+    int32_t *dbg = nullptr;       // debug: per-block integer sums of member 0 (no y written)
+};
+
+// Quantize x (optionally through the RMSNORM arithmetic) to scratch: the same device code as the GEMV prologue.
+struct QuantArgs {
+    const float *x = nullptr;
+    unsigned n = 0;
+    unsigned act = 0;             // 0 Q8_0, 1 Q8_1, 2 Q8_K
+    const float *norm_w = nullptr;
+    float norm_eps = 0.0f;
+    unsigned norm_mode = 0;
+    int8_t *q = nullptr;
+    float *d = nullptr;
+    float *s = nullptr;
+    int32_t *b = nullptr;
+    uint16_t *d16 = nullptr;      // optional FP16 bits of the scales (Q8_0: d, Q8_1: d and s interleaved)
+};
+
+}  // namespace b200q

@@ -1,0 +1,64 @@
+// Kernel launchers (host side of the .cu files), called by the executor in api.cpp. Every launcher takes the
+// context stream; `pdl` launches with programmatic stream serialization so the kernel may start while the
+// previous one drains (each kernel calls griddepcontrol.wait before reading what earlier kernels wrote).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "kernel_args.h"
+
+namespace b200q {
+
+struct EwArgs {
+    unsigned op = 0;      // 3 ADD, 4 SILU_MUL, 5 MUL, 6 UNARY
+    unsigned n = 0;
+    const float *a = nullptr;
+    const float *b = nullptr;
+    float *y = nullptr;
+    unsigned row = 0, stride = 0;  // strided a (UNARY x / SILU_MUL g): rows of `row` floats every `stride` floats
+    unsigned kind = 0;    // UNARY kind
+    unsigned sigmoid = 0; // SILU_MUL sigmoid flag
+};
+
+struct GdnArgs {
+    unsigned hv = 0, hk = 0;
+    const float *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *beta = nullptr;
+    const float *dt = nullptr, *a = nullptr;  // gates (null: g, beta used as they are)
+    const float *z = nullptr, *wn = nullptr;  // gated RMS norm (null: plain y)
+    const float *state_in = nullptr;
+    float *state_out = nullptr;
+    float *y = nullptr;
+    float scale = 0.0f, l2_eps = 0.0f, rms_eps = 0.0f;
+    unsigned l2 = 0;
+};
+
+struct AttnArgs {
+    unsigned n_head = 0, n_kv_head = 0, head_dim = 0, pos = 0, kv_ctx = 0;
+    const float *q = nullptr, *k = nullptr, *v = nullptr;
+    float *y = nullptr;
+    uint16_t *kcache = nullptr, *vcache = nullptr;  // [n_kv_head][kv_ctx][head_dim] F16 each
+    float scale = 0.0f;
+};
+
+// fill in the shared-memory plan of a pass (stages, result buffers) and return its dynamic shared memory
+void plan_gemv_q8(GemvArgs &a, size_t &smem);
+void plan_gemv_kq(GemvArgs &a, size_t &smem);
+cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
+cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st);
+cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,
+                           float eps, unsigned flags, cudaStream_t st, bool pdl);
+cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_conv(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
+                        unsigned use_silu, cudaStream_t st, bool pdl);
+cudaError_t launch_rope(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows,
+                        cudaStream_t st, bool pdl);
+cudaError_t launch_argmax(const float *x, unsigned n, float *y, cudaStream_t st, bool pdl);
+cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx, float *y, unsigned *status,
+                           cudaStream_t st, bool pdl);
+cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_trace_stamp(unsigned long long *slot, cudaStream_t st);
+cudaError_t launch_trace_write(const unsigned long long *stamps, const uint32_t *tags, unsigned n_events,
+                               float *log, cudaStream_t st);
+
+}  // namespace b200q

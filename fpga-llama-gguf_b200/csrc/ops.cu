@@ -1,0 +1,197 @@
+// Element-wise commands of the reference ISA and the extension opcodes, one kernel each:
+//   RMSNORM (fpga/src/gemvqc_ops.h:169-234, CPU gemvq_ref.h:309-324), ADD/MUL (:314-336), SILU_MUL (:338-361),
+//   UNARY (:363-385), CONV (:387-431, CPU gemvq_ref.h:344-358), ROPE (:275-312), ARGMAX, GET_ROW.
+// All FP32 arithmetic uses the _rn intrinsics in the CPU reference's operation order, so results match the CPU
+// bit for bit except where exp/log are involved (see common.cuh). Bandwidth-bound and tiny (<= 65536 floats).
+#include "launch.h"
+#include "quant.cuh"
+
+namespace b200q {
+
+// ---- RMSNORM rows: one CTA per row --------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *w, float *y, unsigned n,
+                                                       unsigned stride, float eps, unsigned flags) {
+    __shared__ double red[32];
+    __shared__ float scale_s;
+    pdl_wait();
+    const float *xr = x + size_t(blockIdx.x) * stride;
+    float *yr = y + size_t(blockIdx.x) * n;
+    const float s = cta_norm_scale(xr, n, eps, flags & 1u, red, &scale_s);
+    for (unsigned i = threadIdx.x; i < n; i += blockDim.x) {
+        const float t = fmul(xr[i], s);
+        yr[i] = (flags & 2u) ? t : fmul(t, w[i]);
+    }
+}
+
+// ---- ADD / MUL / SILU_MUL / UNARY ---------------------------------------------------------------------------------
+__global__ void ew_kernel(const EwArgs a) {
+    pdl_wait();
+    for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < a.n; e += gridDim.x * blockDim.x) {
+        const size_t ai = a.row ? size_t(e / a.row) * a.stride + e % a.row : e;
+        const float av = a.a[ai];
+        float r;
+        switch (a.op) {
+        case 3: r = fadd(av, a.b[e]); break;
+        case 5: r = fmul(av, a.b[e]); break;
+        case 4: r = a.sigmoid ? fmul(sigmoid_f32(av), a.b[e]) : fmul(silu_f32(av), a.b[e]); break;
+        default:
+            r = a.kind == 1 ? silu_f32(av) : a.kind == 2 ? sigmoid_f32(av) : a.kind == 3 ? softplus_f32(av) : av;
+            break;
+        }
+        a.y[e] = r;
+    }
+}
+
+// ---- CONV (ggml_ssm_conv, one token, d_conv 4) --------------------------------------------------------------------
+__global__ void conv_kernel(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
+                            unsigned use_silu) {
+    pdl_wait();
+    const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= ch) return;
+    const float s0 = s_src[3 * c], s1 = s_src[3 * c + 1], s2 = s_src[3 * c + 2], xv = x[c];
+    float sum = 0.0f;
+    sum = fadd(sum, fmul(s0, w[4 * c]));
+    sum = fadd(sum, fmul(s1, w[4 * c + 1]));
+    sum = fadd(sum, fmul(s2, w[4 * c + 2]));
+    sum = fadd(sum, fmul(xv, w[4 * c + 3]));
+    y[c] = use_silu ? silu_f32(sum) : sum;
+    s_dst[3 * c] = s1;
+    s_dst[3 * c + 1] = s2;
+    s_dst[3 * c + 2] = xv;
+}
+
+// ---- ROPE, NEOX pairing --------------------------------------------------------------------------------------------
+__global__ void rope_kernel(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows) {
+    pdl_wait();
+    const unsigned half = n_dims / 2;
+    const unsigned per_row = half + (ne0 - n_dims);
+    for (unsigned t = blockIdx.x * blockDim.x + threadIdx.x; t < rows * per_row; t += gridDim.x * blockDim.x) {
+        const unsigned r = t / per_row, i = t % per_row;
+        const float *xr = x + size_t(r) * ne0;
+        float *yr = y + size_t(r) * ne0;
+        if (i < half) {
+            const float x0 = xr[i], x1 = xr[i + half], c = cs[2 * i], s = cs[2 * i + 1];
+            const float a = fsub(fmul(x0, c), fmul(x1, s));
+            const float b = fadd(fmul(x0, s), fmul(x1, c));
+            yr[i] = a;
+            yr[i + half] = b;
+        } else {
+            const unsigned k = n_dims + (i - half);
+            yr[k] = xr[k];
+        }
+    }
+}
+
+// ---- ARGMAX (extension): first index of the maximum ---------------------------------------------------------------
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *x, unsigned n, float *y) {
+    __shared__ float bv[32];
+    __shared__ unsigned bi[32];
+    pdl_wait();
+    float best = -INFINITY;
+    unsigned idx = 0xffffffffu;
+    for (unsigned i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (v > best || (idx == 0xffffffffu)) { best = v; idx = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const unsigned oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+    }
+    if (threadIdx.x % 32 == 0) { bv[threadIdx.x / 32] = best; bi[threadIdx.x / 32] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (unsigned w = 1; w < (blockDim.x + 31) / 32; ++w)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
+        y[0] = __uint_as_float(idx);
+        y[1] = best;
+    }
+}
+
+// ---- GET_ROW (extension): one dequantized row, index read from act (ggml dequantize_row_q4_0 / q8_0) -------------
+__global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *idx_f, float *y, unsigned *status) {
+    pdl_wait();
+    const unsigned row = __float_as_uint(*idx_f);
+    if (row < w.row0 || row >= w.row0 + w.rows) {
+        if (blockIdx.x == 0 && threadIdx.x == 0 && status) atomicExch(status, 1u);
+        return;
+    }
+    const unsigned r = row - w.row0;
+    const unsigned QB = w.format == 2 ? 16u : 32u;
+    for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < cols; e += gridDim.x * blockDim.x) {
+        const unsigned b = e / 32, j = e % 32;
+        // tiled layout: tile (r / R, b / C), item (r % R) * C + b % C
+        const uint8_t *tile = w.base + (size_t(r / w.rt) * w.kc + b / w.ct) * w.tile_bytes;
+        const unsigned i = (r % w.rt) * w.ct + b % w.ct;
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(tile + w.qs_part + i * 2));
+        int q;
+        if (w.format == 2) {
+            const uint8_t byte = tile[i * QB + (j & 15)];
+            q = int(j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
+        } else {
+            q = int(int8_t(tile[i * QB + j]));
+        }
+        y[e] = fmul(float(q), d);
+    }
+}
+
+// ---- launchers ------------------------------------------------------------------------------------------------------
+static cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                                   cudaLaunchAttribute *attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,
+                           float eps, unsigned flags, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(rows), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, rmsnorm_kernel, x, w, y, n, stride, eps, flags);
+}
+
+cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    const unsigned grid = (a.n + 255) / 256 < 296 ? (a.n + 255) / 256 : 296;
+    cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, ew_kernel, a);
+}
+
+cudaError_t launch_conv(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
+                        unsigned use_silu, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3((ch + 127) / 128), dim3(128), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, conv_kernel, x, w, y, s_src, s_dst, ch, use_silu);
+}
+
+cudaError_t launch_rope(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows,
+                        cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    const unsigned work = rows * (n_dims / 2 + ne0 - n_dims);
+    const unsigned grid = (work + 255) / 256 < 148 ? (work + 255) / 256 : 148;
+    cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, rope_kernel, x, cs, y, n_dims, ne0, rows);
+}
+
+cudaError_t launch_argmax(const float *x, unsigned n, float *y, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(1024), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, x, n, y);
+}
+
+cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx, float *y, unsigned *status,
+                           cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3((cols + 255) / 256), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, get_row_kernel, w, cols, idx, y, status);
+}
+
+}  // namespace b200q

@@ -1,0 +1,73 @@
+// Weight streaming for the GEMV passes: 1-D bulk copies (cp.async.bulk, the TMA engine without a tensor map)
+// of whole weight tiles from HBM into a ring of shared-memory stages, completion tracked by one mbarrier per stage.
+// No cluster multicast: every CTA reads its own tiles of this GPU's memory.
+//
+// Waits are bounded: a stage that does not arrive within kWaitLimitNs sets the pass's error word and the
+// CTA stops issuing work (it then drains its outstanding copies with the same bound before it returns).
+#pragma once
+#include <cstdint>
+
+namespace b200q {
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far above any copy, far below any watchdog
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return uint32_t(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) that completes on `bar`. The evict-first
+// L2 policy keeps streamed weights from displacing activations and recurrent state.
+__device__ __forceinline__ void bulk_copy(void *dst_smem, const void *src, unsigned bytes, uint64_t *bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_addr(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for phase `parity` of `bar`; false if kWaitLimitNs passed first.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+    const uint32_t a = smem_addr(bar);
+    unsigned long long start = 0;
+    for (unsigned i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 63u) == 0) {
+            const unsigned long long now = global_ns();
+            if (start == 0) start = now;
+            else if (now - start > kWaitLimitNs) return false;
+        }
+    }
+}
+
+}  // namespace b200q

@@ -1,0 +1,245 @@
+/*
+ * b200q — B200-native decode hot path for GGUF-quantized models, behind a plain C ABI.
+ *
+ * This header is the drop-in boundary. It replaces what the reference's llama.cpp backend binds on its device side:
+ *   - the kernel entry point gemvqc16(w0..w19, act, cmds, n_cmds, st0..st3, act_rd)
+ *     (reference: fpga/src/gemvqc16.h:122-149), here b200q_run();
+ *   - the one-time repack + upload of each GGUF weight tensor (reference: ggml-xrt.cpp:735-765 with
+ *     fpga/src/gemvqw_layout.h:137-152), here b200q_upload_weight();
+ *   - host<->device copies of the activation buffer act (reference: ggml-xrt.cpp:1136-1143, 1428-1451), here
+ *     b200q_act_write() / b200q_act_read();
+ *   - the recurrent-state buffer I/O (reference: ggml-xrt.cpp:455-500, xrt_rs_io), here b200q_state_write() /
+ *     b200q_state_read();
+ *   - the feature probe, a launch with zero commands (reference: ggml-xrt.cpp:1284-1300, gemvqc16.h:124-134);
+ *   - the direct-register start + poll with timeout (reference: ggml-xrt.cpp:1241-1280), here one CUDA Graph per
+ *     command list (b200q_graph_create / b200q_graph_launch).
+ *
+ * Command list: B200Q_CMD_WORDS (8) uint32 words per command, at most B200Q_MAX_CMDS (128) commands per list. The
+ * words, opcodes, flag bits and validity rules are those of the reference command ISA (fpga/src/gemvqc16.h:24-121),
+ * so a list built by the reference backend runs unchanged. Two differences, both invisible to a list builder:
+ *   - GEMV words 4/5 (w_off lo/hi) carry the 64-bit handle that b200q_upload_weight() returned (a byte offset into
+ *     the device weight arena) instead of a word offset into 20 engine arenas;
+ *   - GDN state rows are 512-byte rows of one device buffer (row r at byte 512 r) instead of rows striped over four
+ *     HBM ports.
+ * Opcodes 12 and up are extensions of this library (decode attention, argmax, embedding row); the reference rejects
+ * them, and their feature bits tell a builder whether they exist.
+ *
+ * All functions return 0 on success. b200q_run() returns a positive 1-based command index when that command is
+ * invalid (the commands before it ran, none after it), B200Q_MAX_CMDS + 1 for a list that is too long, and a
+ * negative B200Q_ERR_* for host or CUDA failures. After a CUDA failure the context refuses further work
+ * (B200Q_ERR_DISABLED), as the reference backend does after a failed launch (ggml-xrt.cpp:2761-2770).
+ * No function throws; no torch or CUDA types appear in the signatures (streams are passed as void *).
+ */
+#ifndef B200Q_H
+#define B200Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200Q_API __attribute__((visibility("default")))
+#else
+#define B200Q_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- command ISA (reference fpga/src/gemvqc16.h:100-135) ---------------------------------------------------- */
+#define B200Q_CMD_WORDS 8u
+#define B200Q_MAX_CMDS 128u
+#define B200Q_OP_GEMV 1u
+#define B200Q_OP_RMSNORM 2u
+#define B200Q_OP_ADD 3u
+#define B200Q_OP_SILU_MUL 4u
+#define B200Q_OP_MUL 5u
+#define B200Q_OP_UNARY 6u
+#define B200Q_OP_GDN 7u
+#define B200Q_OP_CONV 8u
+#define B200Q_OP_STATE_LOAD 9u
+#define B200Q_OP_ROPE 10u
+#define B200Q_OP_TRACE 11u
+/* extensions (no reference counterpart; see the feature word 3 bits below) */
+/* [12, n_head | n_kv_head << 8 | (head_dim / 16) << 16, q_off, k_off, v_off, y_off, pos, slot]: stores this token's
+ * k, v (F16) at position pos of KV slot `slot`, then y = softmax(q K^T / sqrt(head_dim)) V over positions 0..pos */
+#define B200Q_OP_ATTN 12u
+/* [13, n, x_off, y_off, 0, 0, 0, 0]: y[0] = first index of the maximum (uint32 bits), y[1] = the maximum */
+#define B200Q_OP_ARGMAX 13u
+/* [14, format (Q4_0 / Q8_0), cols, w_off lo, w_off hi, idx_off, y_off, 0]: y = dequantized row act[idx_off]
+ * (uint32 bits) of the matrix, as ggml get_rows */
+#define B200Q_OP_GET_ROW 14u
+
+#define B200Q_GEMV_SWIGLU 0x100u
+#define B200Q_GEMV_CONV 0x200u
+#define B200Q_GEMV_ADD 0x400u
+#define B200Q_GROUP 4u
+#define B200Q_GDN_WITH_GEMV 1u
+#define B200Q_GDN_L2_QK 2u
+#define B200Q_GDN_GATED 4u
+#define B200Q_GDN_GATES 8u
+#define B200Q_GDN_WITH_OUT 16u
+#define B200Q_SILU_MUL_SIGMOID 1u
+#define B200Q_NORM_L2 1u
+#define B200Q_NORM_NO_WEIGHT 2u
+#define B200Q_NORM_DEFER 4u
+#define B200Q_UNARY_SILU 1u
+#define B200Q_UNARY_SIGMOID 2u
+#define B200Q_UNARY_SOFTPLUS 3u
+#define B200Q_UNARY_COPY 4u
+#define B200Q_TRACE_ENTRIES 512u
+
+/* ggml type ids of the weight formats (reference fpga/src/gemvqw.h:5-11) */
+#define B200Q_Q4_0 2u
+#define B200Q_Q4_1 3u
+#define B200Q_Q8_0 8u
+#define B200Q_Q5_K 13u
+#define B200Q_Q6_K 14u
+#define B200Q_F16 1u /* only for B200Q_OP_GET_ROW and the KV cache */
+#define B200Q_MAX_ROWS 65536u
+#define B200Q_MAX_COLS 16384u
+
+/* feature words written by a zero-command b200q_run() into act[0], act[1] (reference gemvqc16.h:126-134): the
+ * reference's marker and bit meanings, all bits set (Q5_K, Q6_K, Q4_1, every fusion, ROPE, TRACE). act[2] holds
+ * this library's own word: marker 0x6B53 in the high half, bit 0 ATTN, bit 1 ARGMAX, bit 2 GET_ROW, bit 3
+ * row-sharded multi-GPU lists. */
+#define B200Q_FEATURES 0x6B51FFFFu
+#define B200Q_FEATURES2 0x6B520001u
+#define B200Q_FEATURES3 0x6B53000Fu
+
+/* ---- status codes ------------------------------------------------------------------------------------------ */
+#define B200Q_OK 0
+#define B200Q_ERR_ARG (-1)      /* bad argument (null pointer, range outside a buffer, unknown format) */
+#define B200Q_ERR_CUDA (-2)     /* a CUDA call failed; see b200q_last_error(); the context is disabled */
+#define B200Q_ERR_NOMEM (-3)    /* the weight arena or a device allocation is full */
+#define B200Q_ERR_DISABLED (-4) /* an earlier CUDA failure disabled the context */
+#define B200Q_ERR_COMM (-5)     /* NCCL failure or missing communicator */
+#define B200Q_ERR_STATE (-6)    /* call out of order (e.g. graph launch on another context) */
+
+typedef struct b200q_ctx b200q_ctx;
+typedef struct b200q_graph b200q_graph;
+
+typedef struct b200q_config {
+    int device;            /* CUDA device ordinal */
+    size_t weight_bytes;   /* device weight arena (bump allocated by b200q_upload_weight) */
+    size_t act_floats;     /* activation buffer act, in floats (reference: 64 MiB act BO) */
+    size_t state_rows;     /* DeltaNet state rows of 128 floats (reference: 4 state BOs) */
+    size_t kv_bytes;       /* F16 KV cache of the ATTN extension (0: none) */
+    unsigned kv_ctx;       /* tokens per KV slot of the ATTN extension */
+} b200q_config;
+
+/* Context: one device, one stream, one weight arena, act, state, scratch. Thread-safe for one caller at a time. */
+B200Q_API int b200q_create(const b200q_config *cfg, b200q_ctx **out);
+B200Q_API void b200q_destroy(b200q_ctx *ctx);
+B200Q_API const char *b200q_last_error(const b200q_ctx *ctx);
+/* the context's CUDA stream (a cudaStream_t), for callers that time or order work around it */
+B200Q_API void *b200q_stream(b200q_ctx *ctx);
+B200Q_API int b200q_synchronize(b200q_ctx *ctx);
+/* device addresses of the buffers (for callers that keep inputs resident in HBM) */
+B200Q_API void *b200q_act_device_ptr(b200q_ctx *ctx);
+B200Q_API void *b200q_state_device_ptr(b200q_ctx *ctx);
+B200Q_API void *b200q_kv_device_ptr(b200q_ctx *ctx);
+
+/* Feature words (the three words a zero-command b200q_run writes into act[0..2]), without a launch. */
+B200Q_API void b200q_features(uint32_t out[3]);
+
+/* One-time repack + upload of a GGUF matrix (rows x cols, row-major GGUF blocks; format a B200Q_Q* id). The bits
+ * of every scale and quant stay as they are; only their arrangement changes (scales and quants in separate
+ * row-major regions; K-quant quant fields permuted within each super-block).
+ * block_cols: 0, or 256 for a matrix that a GDN_WITH_OUT step consumes (accepted for list compatibility; the
+ * device layout is the same). *w_off receives the handle for GEMV words 4/5. In a row-sharded context (after
+ * b200q_comm_init) only this rank's row slice is kept. */
+B200Q_API int b200q_upload_weight(b200q_ctx *ctx, const void *gguf, unsigned rows, unsigned cols, unsigned format,
+                        unsigned block_cols, uint64_t *w_off);
+/* As b200q_upload_weight; flags B200Q_UPLOAD_REPLICATE keeps all rows on every rank of a row-sharded context
+ * (for matrices read by GET_ROW, such as the token embedding). */
+#define B200Q_UPLOAD_REPLICATE 1u
+B200Q_API int b200q_upload_weight_ex(b200q_ctx *ctx, const void *gguf, unsigned rows, unsigned cols, unsigned format,
+                           unsigned block_cols, unsigned flags, uint64_t *w_off);
+/* Device bytes one matrix takes in the arena (all rows, one rank). */
+B200Q_API size_t b200q_weight_device_bytes(unsigned rows, unsigned cols, unsigned format);
+/* Bytes of one GGUF row of the format (0 for an unknown format). */
+B200Q_API size_t b200q_gguf_row_bytes(unsigned cols, unsigned format);
+/* Reset the bump allocator of the weight arena (all handles become invalid). */
+B200Q_API int b200q_weights_reset(b200q_ctx *ctx);
+
+/* act and state I/O (synchronous; offsets in floats / rows). */
+B200Q_API int b200q_act_write(b200q_ctx *ctx, size_t off, const float *src, size_t n);
+B200Q_API int b200q_act_read(b200q_ctx *ctx, size_t off, float *dst, size_t n);
+B200Q_API int b200q_act_fill(b200q_ctx *ctx, size_t off, float value, size_t n);
+B200Q_API int b200q_state_write(b200q_ctx *ctx, size_t row, const float *src, size_t rows);
+B200Q_API int b200q_state_read(b200q_ctx *ctx, size_t row, float *dst, size_t rows);
+B200Q_API int b200q_kv_write(b200q_ctx *ctx, size_t byte_off, const void *src, size_t bytes);
+
+/* Run one command list (reference gemvqc16 contract, see the top of this header); synchronous: returns once the
+ * GPU finished the list. n_cmds = 0 writes the feature words into act[0..2]. */
+B200Q_API int b200q_run(b200q_ctx *ctx, const uint32_t *cmds, unsigned n_cmds);
+/* Same, asynchronous on the context stream (validation still on the host, before any launch). */
+B200Q_API int b200q_run_async(b200q_ctx *ctx, const uint32_t *cmds, unsigned n_cmds);
+
+/* A valid list captured once as a CUDA Graph (one per token in a decode loop); launch replays it on the context
+ * stream. Returns the list's status (a rejected list makes no graph). */
+B200Q_API int b200q_graph_create(b200q_ctx *ctx, const uint32_t *cmds, unsigned n_cmds, b200q_graph **out);
+B200Q_API int b200q_graph_launch(b200q_ctx *ctx, b200q_graph *graph);
+B200Q_API void b200q_graph_destroy(b200q_graph *graph);
+/* Launches graphs[i % n_graphs] for i = 0 .. launches - 1 on the context stream (a token loop without host
+ * round trips between launches). */
+B200Q_API int b200q_graph_launch_many(b200q_ctx *ctx, b200q_graph *const *graphs, unsigned n_graphs,
+                                      unsigned launches);
+/* kernels one replay of the graph launches */
+B200Q_API unsigned b200q_graph_kernel_count(const b200q_graph *graph);
+
+/* ---- host-only planning (no GPU needed) ---------------------------------------------------------------------- */
+typedef struct b200q_pass_info {
+    uint32_t first_cmd;   /* index of the first command of the pass */
+    uint32_t n_cmds;      /* commands the pass consumes */
+    uint32_t kind;        /* B200Q_PASS_* */
+    uint32_t n_members;   /* GEMVs in the pass */
+    uint32_t fused_norm;  /* 1: the GEMVs quantize a deferred RMSNORM's row */
+} b200q_pass_info;
+#define B200Q_PASS_GEMV 1u
+#define B200Q_PASS_ELEMENTWISE 2u
+#define B200Q_PASS_GDN 3u
+#define B200Q_PASS_NOP 4u
+#define B200Q_PASS_EXT 5u
+/* Validate a list and return its pass structure as the device run would execute it; the return value is the one
+ * b200q_run would give (0 or the 1-based index of the first invalid command). */
+B200Q_API int b200q_plan(const uint32_t *cmds, unsigned n_cmds, b200q_pass_info *passes, unsigned max_passes,
+               unsigned *n_passes);
+
+/* ---- host-only layout (no GPU): the device layout of a matrix, its repack and the inverse, for tests ---------- */
+typedef struct b200q_layout_info {
+    uint32_t rows_per_tile, blocks_per_tile, tiles_per_row_tile, row_tiles, tile_bytes;
+    uint64_t total_bytes;
+} b200q_layout_info;
+B200Q_API int b200q_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms, b200q_layout_info *out);
+/* Repack all rows (dst: total_bytes of the layout for `sms`), and the inverse of one row back to GGUF bytes. */
+B200Q_API int b200q_repack_host(const void *gguf, unsigned rows, unsigned cols, unsigned format, unsigned sms,
+                                void *dst);
+B200Q_API int b200q_unpack_row_host(const void *dev, unsigned rows, unsigned cols, unsigned format, unsigned sms,
+                                    unsigned row, void *gguf_row);
+
+/* ---- checks of the bit-exact intermediate values (same device code as the GEMV passes) ---------------------- */
+/* Quantize act[x_off .. x_off + n) as a GEMV pass of format `format` would (Q8_0 for Q4_0/Q8_0, Q8_K for
+ * Q5_K/Q6_K, Q8_1 for Q4_1), optionally through a deferred RMSNORM (norm_w_off = UINT32_MAX: none; else the
+ * RMSNORM's w_off, eps, flags). Outputs: q (n int8), scales (Q8_0: n/32 uint16 FP16 bits; Q8_K: n/256 floats;
+ * Q8_1: n/32 pairs of uint16), bsums (Q8_0/Q8_1: n/32 int32 block sums of q; Q8_K: n/16 int32). */
+B200Q_API int b200q_debug_quantize(b200q_ctx *ctx, unsigned format, size_t x_off, unsigned n, uint32_t norm_w_off,
+                         float norm_eps, unsigned norm_flags, int8_t *q, void *scales, int32_t *bsums);
+/* Per-block integer dot products of one GEMV command (Q4_0/Q8_0: rows x cols/32 int32 sumi, the ints that scale
+ * into each FP32 term; Q5_K/Q6_K: rows x cols/256 x 9 int32: the 8 lane sums of the scaled products, then the
+ * mins sum (0 for Q6_K); Q4_1: rows x cols/32). */
+B200Q_API int b200q_debug_block_sums(b200q_ctx *ctx, const uint32_t cmd[8], int32_t *out);
+
+/* ---- multi-GPU (one process per GPU, NCCL over NVLink) ------------------------------------------------------- */
+#define B200Q_UNIQUE_ID_BYTES 128
+B200Q_API int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]);
+/* Join a communicator of world ranks; from then on uploads keep only this rank's row slice of each shardable
+ * matrix and every pass all-gathers its GEMV outputs so all ranks hold the full act, as with one GPU. */
+B200Q_API int b200q_comm_init(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]);
+B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200Q_H */

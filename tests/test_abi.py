@@ -1,0 +1,52 @@
+"""The C-ABI library loads and exports every entry point include/b200q.h declares; the host-only layout repack keeps
+every bit (no GPU needed)."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, rng
+
+
+def test_exports_every_declared_symbol(b2):
+    header = open(os.path.join(ROOT, "include", "b200q.h")).read()
+    declared = set(re.findall(r"B200Q_API[^;(]*?\b(b200q_\w+)\s*\(", header))
+    assert len(declared) >= 30
+    L = b2.lib()
+    missing = [s for s in declared if not hasattr(L, s)]
+    assert not missing, missing
+    assert declared == set(b2.EXPORTED)
+
+
+def test_features(b2):
+    assert b2.features() == b2.FEATURES
+    f = b2.features()
+    assert f[0] >> 16 == 0x6B51 and f[1] >> 16 == 0x6B52 and f[2] >> 16 == 0x6B53
+
+
+@pytest.mark.parametrize("fmt,cols", [(2, 2560), (2, 128), (8, 9216), (3, 384), (13, 2560), (14, 2560), (14, 256)])
+@pytest.mark.parametrize("rows", [1, 17, 300])
+def test_repack_roundtrip_keeps_bits(b2, synth, fmt, cols, rows):
+    w = synth.matrix(fmt, rng(20, fmt, rows), rows, cols)
+    dev = b2.repack_host(w, rows, cols, fmt)
+    lay = b2.layout(rows, cols, fmt)
+    assert dev.size == lay["total_bytes"] and lay["tile_bytes"] % 16 == 0
+    for r in sorted({0, rows // 2, rows - 1}):
+        assert np.array_equal(b2.unpack_row_host(dev, rows, cols, fmt, r), w[r])
+    # the repack only moves bytes around: the multiset of bits is unchanged for the byte-aligned formats
+    if fmt in (2, 8, 3):
+        assert np.unpackbits(dev).sum() == np.unpackbits(w).sum()
+
+
+def test_layout_tiles_balance_the_sms(b2):
+    lay = b2.layout(9216, 2560, 2)
+    assert lay["row_tiles"] >= 4 * 148 and lay["tile_bytes"] <= 12288
+    lay = b2.layout(151936, 2560, 14)
+    assert lay["row_tiles"] >= 4 * 148
+
+
+def test_device_bytes_and_row_bytes(b2):
+    assert b2.gguf_row_bytes(2560, 2) == 80 * 18
+    assert b2.gguf_row_bytes(2560, 14) == 10 * 210
+    assert b2.lib().b200q_weight_device_bytes(9216, 2560, 2) >= 9216 * 80 * 18
