@@ -36,7 +36,7 @@ FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53000F)
 UPLOAD_REPLICATE = 1
 
 ERR = {-1: "bad argument", -2: "CUDA failure", -3: "out of memory", -4: "context disabled", -5: "NCCL failure",
-       -6: "call out of order"}
+       -6: "call out of order", -7: "bounded wait ran out"}
 
 
 class B200QError(RuntimeError):

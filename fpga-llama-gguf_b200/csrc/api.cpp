@@ -509,6 +509,19 @@ Limits limits_of(const b200q_ctx *c) {
     return L;
 }
 
+// A pass whose bounded wait ran out sets the device error word (dstatus[1]); read and clear it after a sync.
+int check_device_status(b200q_ctx *c) {
+    unsigned st[2] = {0, 0};
+    CUDA_TRY(c, cudaMemcpy(st, c->dstatus, sizeof(st), cudaMemcpyDeviceToHost));
+    if (st[0] | st[1]) {
+        const unsigned zero[2] = {0, 0};
+        CUDA_TRY(c, cudaMemcpy(c->dstatus, zero, sizeof(zero), cudaMemcpyHostToDevice));
+        if (st[1]) return set_err(c, B200Q_ERR_TIMEOUT, "a pass gave up waiting for its weight tiles (bounded wait)");
+        return set_err(c, B200Q_ERR_ARG, "GET_ROW: the row index in act is outside the matrix");
+    }
+    return 0;
+}
+
 int check_ctx(b200q_ctx *c) {
     if (!c) return B200Q_ERR_ARG;
     if (c->disabled) return B200Q_ERR_DISABLED;
@@ -618,7 +631,7 @@ int b200q_synchronize(b200q_ctx *c) {
     int rc = check_ctx(c);
     if (rc) return rc;
     CUDA_TRY(c, cudaStreamSynchronize(c->stream));
-    return 0;
+    return check_device_status(c);
 }
 
 size_t b200q_gguf_row_bytes(unsigned cols, unsigned format) { return gguf_row_bytes(cols, format); }
@@ -761,6 +774,7 @@ int b200q_run(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
     int rc = check_ctx(c);
     if (rc) return rc;
     CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    if ((rc = check_device_status(c))) return rc;
     return status;
 }
 

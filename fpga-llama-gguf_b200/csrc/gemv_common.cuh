@@ -1,5 +1,16 @@
-// Pieces shared by the two GEMV pass kernels (gemv_q8.cu, gemv_kq.cu): the walk over a CTA's weight tiles, the
-// bulk-copy issue into the stage ring, and the result writer (epilogues of fpga/src/gemvqc16.cpp:203-316).
+// Warp-specialized pass framework shared by the two GEMV kernels (gemv_q8.cu, gemv_kq.cu).
+//
+// A CTA (two per SM) walks its weight tiles (row tiles of the pass's units, round-robin over the grid; each row
+// tile streamed as kc tiles of R rows x C blocks) with three roles:
+//   warp 0    producer: bulk copies (cp.async.bulk) of tiles into a ring of n_stages shared-memory stages; the
+//             first stages start before the wait on the previous kernel (weights never change within a list);
+//   warps 2-9 compute: per tile, the exact integer block dots and the FP32 block terms, into a result buffer;
+//   warp 1    fold: per row (lane), the row's block terms added in block order — the CPU's FP32 sum, bit for bit —
+//             and after the row's last tile the epilogue (SwiGLU / residual add / conv1d) and the store of y.
+// Hand-offs go through mbarriers (full/empty per stage, rfull/rempty per result buffer), so the copies, the integer
+// work and the sequential fold of different tiles overlap. Every wait is bounded; a wait that runs out sets the
+// CTA's abort flag and the pass's error word, and all roles leave (the producer first waits, bounded, for the
+// copies it started).
 #pragma once
 #include "kernel_args.h"
 #include "pipeline.cuh"
@@ -8,7 +19,12 @@
 
 namespace b200q {
 
-constexpr unsigned kPassThreads = 256;
+constexpr unsigned kComputeWarps = 8;
+constexpr unsigned kPassThreads = 32 * (2 + kComputeWarps);  // producer + fold + compute
+constexpr unsigned kComputeThreads = 32 * kComputeWarps;
+constexpr unsigned kXThreads = kPassThreads - 32;              // fold + compute warps prepare x
+constexpr unsigned kNR = 2;                                     // result buffers
+constexpr unsigned kMaxStages = 6;
 
 // Position in the tile sequence of one CTA: items (row tiles of units) blockIdx.x, blockIdx.x + gridDim.x, ...;
 // each item is streamed as its unit's kc tiles.
@@ -51,7 +67,7 @@ __device__ __forceinline__ const uint8_t *tile_src(const MatrixView &w, unsigned
 // Pair tile offset inside a stage.
 __host__ __device__ inline unsigned pair_offset(unsigned tile_bytes) { return (tile_bytes + 127u) & ~127u; }
 
-// Thread 0: bulk copies of one stage (the unit's tile, and for a pair the u tile of the same rows and columns).
+// Bulk copies of one stage (the unit's tile, and for a pair the u tile of the same rows and columns).
 __device__ __forceinline__ void issue_stage(const GemvArgs &a, const TileIt &it, uint8_t *stage, uint64_t *bar,
                                             uint64_t policy) {
     const GemvMemberArgs &M = unit_member(a, it.unit);
@@ -64,7 +80,7 @@ __device__ __forceinline__ void issue_stage(const GemvArgs &a, const TileIt &it,
 }
 
 // Result writer for one output row: SwiGLU silu(g) * u (silu_mul_f), residual add (add_mul_f), conv1d + SiLU +
-// state shift (conv_chan, silu_f), else the row value.
+// state shift (conv_chan, silu_f), else the row value (fpga/src/gemvqc16.cpp:203-316).
 __device__ __forceinline__ void write_row(const GemvMemberArgs &M, unsigned gr, float v, float g) {
     switch (M.epi) {
     case EpiSwigluU: M.y[gr] = fmul(silu_f32(g), v); break;
@@ -95,45 +111,279 @@ __device__ __forceinline__ void write_padding(const GemvMemberArgs &OUT, unsigne
     }
 }
 
-// Shared memory of a pass: [mbarriers 64 B][stages][results x 2][x image]
+// ---- shared memory of a pass ------------------------------------------------------------------------------------
+// [256 B: full[NS] empty[NS] rfull[2] rempty[2] abort go][stages][results x 2][x image][raw x][raw norm weight][extra]
+constexpr unsigned kBarRegion = 256;
+static_assert((2 * kMaxStages + 2 * kNR) * 8 + 12 <= kBarRegion, "barriers and the flags fit their region");
 struct PassSmem {
-    uint64_t *bar;
+    uint64_t *full, *empty, *rfull, *rempty;
+    unsigned *abort;
+    unsigned *go;  // the lead compute warp's verdicts for the other compute warps (two, alternating)
     uint8_t *stages;
-    uint8_t *res[2];
+    uint8_t *res[kNR];
     unsigned char *ximg;
+    float *xraw, *wraw;
+    unsigned char *extra;
 };
 
+__host__ __device__ inline size_t align128(size_t v) { return (v + 127) & ~size_t(127); }
+
 __host__ __device__ inline size_t pass_smem_bytes(unsigned n_stages, unsigned stage_bytes, unsigned res_bytes,
-                                                  size_t extra) {
-    return 64 + size_t(n_stages) * stage_bytes + 2 * size_t(res_bytes) + extra;
+                                                  unsigned cols, bool wraw, size_t extra) {
+    return kBarRegion + size_t(n_stages) * stage_bytes + kNR * size_t(res_bytes) + align128(ximage_bytes(cols)) +
+           align128(size_t(cols) * 4) + (wraw ? align128(size_t(cols) * 4) : 0) + extra;
 }
 
 __device__ __forceinline__ PassSmem carve_pass(unsigned char *smem, const GemvArgs &a) {
     PassSmem P;
-    P.bar = reinterpret_cast<uint64_t *>(smem);
-    P.stages = smem + 64;
-    P.res[0] = P.stages + size_t(a.n_stages) * a.stage_bytes;
-    P.res[1] = P.res[0] + a.res_bytes;
-    P.ximg = P.res[1] + a.res_bytes;
+    uint64_t *b = reinterpret_cast<uint64_t *>(smem);
+    P.full = b;
+    P.empty = b + a.n_stages;
+    P.rfull = b + 2 * a.n_stages;
+    P.rempty = P.rfull + kNR;
+    P.abort = reinterpret_cast<unsigned *>(P.rempty + kNR);
+    P.go = P.abort + 1;
+    unsigned char *p = smem + kBarRegion;
+    P.stages = p;
+    p += size_t(a.n_stages) * a.stage_bytes;
+    for (unsigned i = 0; i < kNR; ++i) {
+        P.res[i] = p;
+        p += a.res_bytes;
+    }
+    P.ximg = p;
+    p += align128(ximage_bytes(a.cols));
+    P.xraw = reinterpret_cast<float *>(p);
+    p += align128(size_t(a.cols) * 4);
+    P.wraw = nullptr;
+    if (a.wraw) {
+        P.wraw = reinterpret_cast<float *>(p);
+        p += align128(size_t(a.cols) * 4);
+    }
+    P.extra = p;
     return P;
 }
 
-// Thread 0: mbarrier init; then the first stages are issued (weights never change during a list, so this runs
-// before the wait on the previous kernel).
-__device__ __forceinline__ unsigned pass_prologue(const GemvArgs &a, const PassSmem &P, TileIt &issue,
-                                                  uint64_t policy) {
-    unsigned issued = 0;
-    if (threadIdx.x == 0) {
-        for (unsigned s = 0; s < a.n_stages; ++s) mbar_init(&P.bar[s], 1);
-        mbar_fence_init();
-        while (issued < a.n_stages && tile_valid(a, issue)) {
-            issue_stage(a, issue, P.stages + size_t(issued) * a.stage_bytes, &P.bar[issued], policy);
-            tile_next(a, issue);
-            ++issued;
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// A bounded wait that also gives up once another role set the abort flag.
+__device__ __forceinline__ bool role_wait(uint64_t *bar, unsigned parity, volatile unsigned *abort) {
+    const uint32_t a = smem_addr(bar);
+    unsigned long long start = 0;
+    for (unsigned i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(kSuspendHintNs)
+            : "memory");
+        if (done) return true;
+        if ((i & 1023u) == 0) {
+            if (*abort) return false;
+            const unsigned long long now = global_ns();
+            if (start == 0) start = now;
+            else if (now - start > kWaitLimitNs) return false;
         }
     }
-    __syncthreads();
-    return issued;
+}
+
+__device__ __forceinline__ void fail_pass(const GemvArgs &a, volatile unsigned *abort) {
+    *abort = 1u;
+    if (a.err) atomicExch(a.err, 1u);
+}
+
+// Thread 0: barrier init (full: the producer's arrival + bytes; empty / rfull: one arrival per compute warp;
+// rempty: the fold warp).
+__device__ __forceinline__ void init_pass_barriers(const GemvArgs &a, const PassSmem &P) {
+    for (unsigned s = 0; s < a.n_stages; ++s) {
+        mbar_init(&P.full[s], 1);
+        mbar_init(&P.empty[s], kComputeWarps);
+    }
+    for (unsigned b = 0; b < kNR; ++b) {
+        mbar_init(&P.rfull[b], kComputeWarps);
+        mbar_init(&P.rempty[b], 1);
+    }
+    *P.abort = 0u;
+    mbar_fence_init();
+}
+
+// Producer (one thread): streams the CTA's tiles through the stage ring.
+__device__ __forceinline__ void producer_loop(const GemvArgs &a, const PassSmem &P) {
+    const uint64_t policy = evict_first_policy();
+    TileIt it = tile_first(a);
+    unsigned seq = 0;
+    bool failed = false;
+    while (tile_valid(a, it)) {
+        const unsigned s = seq % a.n_stages;
+        if (seq >= a.n_stages && !role_wait(&P.empty[s], ((seq / a.n_stages) - 1u) & 1u, P.abort)) {
+            failed = true;
+            break;
+        }
+        issue_stage(a, it, P.stages + size_t(s) * a.stage_bytes, &P.full[s], policy);
+        tile_next(a, it);
+        ++seq;
+    }
+    if (failed) {
+        fail_pass(a, P.abort);
+        // the last issued copy of every stage: wait (bounded) until it has landed before the CTA may exit
+        const unsigned from = seq > a.n_stages ? seq - a.n_stages : 0u;
+        for (unsigned q = from; q < seq; ++q) mbar_wait(&P.full[q % a.n_stages], (q / a.n_stages) & 1u);
+    }
+}
+
+__device__ __forceinline__ void named_sync_x() { asm volatile("bar.sync 1, %0;" ::"n"(kXThreads) : "memory"); }
+// The 8 compute warps: the lead warp waits on the mbarriers, the others sleep on this hardware barrier.
+__device__ __forceinline__ void named_sync_compute() {
+    asm volatile("bar.sync 2, %0;" ::"n"(kComputeThreads) : "memory");
+}
+
+// Compute warps: wait until stage s holds the tile and result buffer b is free. The lead warp polls; the others
+// sleep on the named barrier, then take their own (already complete, so non-blocking) acquire of the stage.
+// The verdict alternates between two flags, so the lead never overwrites one another warp has not read yet.
+// False (for every compute warp) if a wait gave up.
+__device__ __forceinline__ bool compute_acquire(const PassSmem &P, unsigned seq, unsigned n_stages) {
+    const unsigned warp = threadIdx.x / 32, s = seq % n_stages, b = seq % kNR;
+    volatile unsigned *flag = P.go + (seq & 1u);
+    if (warp == 2) {
+        bool ok = role_wait(&P.full[s], (seq / n_stages) & 1u, P.abort);
+        if (ok && seq >= kNR) ok = role_wait(&P.rempty[b], ((seq / kNR) - 1u) & 1u, P.abort);
+        if (threadIdx.x == 64) *flag = ok ? 1u : 0u;
+    }
+    named_sync_compute();
+    const bool ok = *flag != 0u;
+    if (ok && warp != 2) role_wait(&P.full[s], (seq / n_stages) & 1u, P.abort);
+    return ok;
+}
+
+// x into shared memory (coalesced), then quantized by warps: threads of warps 1.. (kXThreads of them).
+__device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, const XImage &X, unsigned act) {
+    const unsigned t = threadIdx.x - 32, warp = t / 32, lane = t % 32, nw = kXThreads / 32;
+    const unsigned n = a.cols;
+    if (a.xq) {
+        for (unsigned i = t; i < n / 16; i += kXThreads)
+            reinterpret_cast<uint4 *>(X.q)[i] = reinterpret_cast<const uint4 *>(a.xq)[i];
+        const unsigned nd = act == 2 ? n / 256 : n / 32, nb = act == 2 ? n / 16 : n / 32;
+        for (unsigned i = t; i < nd; i += kXThreads) {
+            X.d[i] = a.xd[i];
+            if (act == 1) X.s[i] = a.xs[i];
+        }
+        for (unsigned i = t; i < nb; i += kXThreads) X.b[i] = a.xb[i];
+        named_sync_x();
+        return;
+    }
+    const bool norm = (a.norm_mode & 8u) != 0, weighted = (a.norm_mode & 2u) == 0;
+    const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
+    float4 *xr4 = reinterpret_cast<float4 *>(P.xraw);
+    double acc = 0.0;
+    for (unsigned i = t; i < n / 4; i += kXThreads) {
+        const float4 v = x4[i];
+        xr4[i] = v;
+        if (norm) {
+            acc += double(fmul(v.x, v.x));
+            acc += double(fmul(v.y, v.y));
+            acc += double(fmul(v.z, v.z));
+            acc += double(fmul(v.w, v.w));
+        }
+    }
+    if (norm && weighted && P.wraw) {
+        const float4 *w4 = reinterpret_cast<const float4 *>(a.norm_w);
+        for (unsigned i = t; i < n / 4; i += kXThreads) reinterpret_cast<float4 *>(P.wraw)[i] = w4[i];
+    }
+    float scale = 1.0f;
+    if (norm) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) X.red[warp] = acc;
+        named_sync_x();
+        if (t == 0) {
+            double sum = 0.0;
+            for (unsigned w = 0; w < nw; ++w) sum += X.red[w];
+            float sc;
+            if (a.norm_mode & 1u) sc = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sum)), a.norm_eps));
+            else sc = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(sum, double(n))), a.norm_eps)));
+            *X.scale = sc;
+        }
+    }
+    named_sync_x();
+    if (norm) scale = *X.scale;
+    const float *wn = P.wraw ? P.wraw : a.norm_w;
+    if (act == 2) {
+        for (unsigned sb = warp; sb < n / 256; sb += nw) {
+            float v[8];
+            float amax = 0.0f, mx = 0.0f;
+            int idx = 0x7fffffff;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const unsigned e = sb * 256 + lane + 32 * k;
+                v[k] = norm_value(P.xraw, e, norm, scale, wn, weighted);
+                const float av = fabsf(v[k]);
+                if (av > amax) { amax = av; mx = v[k]; idx = int(lane + 32 * k); }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {  // largest magnitude, first index on ties (gemvq_ref.h:68-75)
+                const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+                const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+                if (oa > amax || (oa == amax && oi < idx)) { amax = oa; mx = om; idx = oi; }
+            }
+            const float iscale = amax != 0.0f ? fdiv(-127.0f, mx) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                int q = 0;
+                if (amax != 0.0f) {
+                    q = __float2int_rn(fmul(iscale, v[k]));
+                    q = q < 127 ? q : 127;
+                }
+                X.q[sb * 256 + lane + 32 * k] = int8_t(q);
+                int part = q;  // sums of 16: lanes 0..15 -> group 2k, lanes 16..31 -> group 2k + 1
+                part += __shfl_xor_sync(0xffffffffu, part, 8);
+                part += __shfl_xor_sync(0xffffffffu, part, 4);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                if (lane == 0) X.b[sb * 16 + 2 * k] = part;
+                if (lane == 16) X.b[sb * 16 + 2 * k + 1] = part;
+            }
+            if (lane == 0) X.d[sb] = amax != 0.0f ? fdiv(1.0f, iscale) : 0.0f;
+        }
+    } else {
+        // four lanes per 32-block, eight elements each: lane j of the quad of block b takes the elements
+        // (8j + e + b) % 32, e < 8, so the 32 lanes of a warp (8 blocks) read 32 different banks; amax and the sum
+        // over the quad by shuffles. The loop runs warp-uniformly (whole warps per round).
+        const unsigned nq = n / 32 * 4;
+        for (unsigned wbase = t & ~31u; wbase < nq; wbase += kXThreads) {
+            const unsigned item = wbase + (t & 31u), b = item / 4, j = item & 3u;
+            const bool live = item < nq;
+            float v[8];
+            float amax = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const unsigned off = (8u * j + unsigned(e) + b) & 31u;
+                v[e] = live ? norm_value(P.xraw, b * 32 + off, norm, scale, wn, weighted) : 0.0f;
+                amax = fmaxf(amax, fabsf(v[e]));
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float s = fdiv(amax, 127.0f);
+            const float id = s != 0.0f ? fdiv(1.0f, s) : 0.0f;
+            int sum = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int q = int(roundf(fmul(v[e], id)));
+                sum += q;
+                const unsigned off = (8u * j + unsigned(e) + b) & 31u;
+                if (live) X.q[b * 32 + off] = int8_t(q);
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            if (live && j == 0) {
+                X.d[b] = half_bits_to_float(float_to_half_bits(s));
+                X.b[b] = sum;
+                if (act == 1) X.s[b] = half_bits_to_float(float_to_half_bits(fmul(float(sum), s)));
+            }
+        }
+    }
+    named_sync_x();
 }
 
 }  // namespace b200q

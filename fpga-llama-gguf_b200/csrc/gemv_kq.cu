@@ -22,9 +22,9 @@ constexpr unsigned kRecWords = 12;  // per (row, super-block): aux[8], mins, d |
 // (y[16j+l], y[16j+l+8]).
 __device__ __forceinline__ void build_transposed(const XImage &X, unsigned cols, bool need5, bool need6, uint32_t *y5,
                                                  uint32_t *y6) {
-    const unsigned nsb = cols / 256;
+    const unsigned nsb = cols / 256, t = threadIdx.x - 32;
     if (need5) {
-        for (unsigned i = threadIdx.x; i < nsb * 64; i += blockDim.x) {
+        for (unsigned i = t; i < nsb * 64; i += kXThreads) {
             const unsigned sb = i / 64, j = (i / 8) % 8, l = i % 8;
             const int8_t *y = X.q + sb * 256 + 32 * j + l;
             y5[i] = uint32_t(uint8_t(y[0])) | uint32_t(uint8_t(y[8])) << 8 | uint32_t(uint8_t(y[16])) << 16 |
@@ -32,13 +32,13 @@ __device__ __forceinline__ void build_transposed(const XImage &X, unsigned cols,
         }
     }
     if (need6) {
-        for (unsigned i = threadIdx.x; i < nsb * 128; i += blockDim.x) {
+        for (unsigned i = t; i < nsb * 128; i += kXThreads) {
             const unsigned sb = i / 128, j = (i / 8) % 16, l = i % 8;
             const int8_t *y = X.q + sb * 256 + 16 * j + l;
             y6[i] = uint32_t(uint16_t(int16_t(y[0]))) | uint32_t(uint16_t(int16_t(y[8]))) << 16;
         }
     }
-    __syncthreads();
+    named_sync_x();
 }
 
 // get_scale_min_k4 (gemvq_ref.h:83-92) on the 12 packed bytes
@@ -136,9 +136,9 @@ __device__ __forceinline__ void compute_tile_kq(const uint8_t *tile, const Matri
     const unsigned DD = w.format == 13 ? 4u : 2u;
     const uint8_t *dmp = tile + w.qs_part, *ddp = tile + w.qs_part + w.dm_part;
     // items beyond the tile run the shuffles with zero work (the whole warp takes part in every round)
-    const unsigned rounds = (items + kPassThreads - 1) / kPassThreads;
+    const unsigned rounds = (items + kComputeThreads - 1) / kComputeThreads, ct = threadIdx.x - 64;
     for (unsigned rd = 0; rd < rounds; ++rd) {
-        const unsigned idx = rd * kPassThreads + threadIdx.x;
+        const unsigned idx = rd * kComputeThreads + ct;
         const bool live = idx < items;
         const unsigned i = live ? idx / 8 : 0, p = idx & 7u;  // i = r * C + c
         const unsigned c = i % C, sb = k * C + c;
@@ -203,19 +203,22 @@ __device__ __forceinline__ float kq_final(const KqAcc &A) {
     return s;
 }
 
-__global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const PassSmem P = carve_pass(smem, a);
     const XImage X = carve_ximage(P.ximg, a.cols);
-    uint32_t *y5 = reinterpret_cast<uint32_t *>(P.ximg + ((ximage_bytes(a.cols) + 127) & ~size_t(127)));
+    uint32_t *y5 = reinterpret_cast<uint32_t *>(P.extra);
     uint32_t *y6 = y5 + a.cols / 4;
-    const uint64_t policy = evict_first_policy();
-    TileIt issue = tile_first(a);
-    unsigned issued = pass_prologue(a, P, issue, policy);  // copies started (thread 0's count)
-    pdl_launch_dependents();  // the next kernel may start its own weight copies as SMs free up
+    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) init_pass_barriers(a, P);
+    __syncthreads();
+    pdl_launch_dependents();
+    if (warp == 0) {
+        if (lane == 0) producer_loop(a, P);
+        return;
+    }
     pdl_wait();
-    if (a.xq) load_quant_cta(a.xq, a.xd, a.xs, a.xb, a.cols, 2, X);
-    else quantize_cta(a.x, a.cols, 2, a.norm_w, a.norm_eps, a.norm_mode, X);
+    prepare_x(a, P, X, 2);
     bool need5 = false, need6 = false;
     for (unsigned i = 0; i < a.n_members; ++i) {
         need5 |= a.m[i].w.format == 13;
@@ -223,62 +226,71 @@ __global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const GemvArgs
     }
     build_transposed(X, a.cols, need5, need6, y5, y6);
     TileIt it = tile_first(a);
+    unsigned seq = 0;
+    if (warp >= 2) {  // compute
+        while (tile_valid(a, it)) {
+            const unsigned s = seq % a.n_stages, b = seq % kNR;
+            const bool ok = compute_acquire(P, seq, a.n_stages);
+            if (!ok) {
+                fail_pass(a, P.abort);
+                break;
+            }
+            const GemvMemberArgs &M0 = unit_member(a, it.unit);
+            const int pair = a.unit_pair[it.unit];
+            const unsigned t = it.item - a.item_start[it.unit];
+            const unsigned R = M0.w.rt, C = M0.w.ct;
+            const unsigned r0 = t * R, nr = min(R, M0.w.rows - r0);
+            uint32_t *rec = reinterpret_cast<uint32_t *>((b ? P.res[1] : P.res[0]));
+            const uint8_t *stage = P.stages + size_t(s) * a.stage_bytes;
+            compute_tile_kq(stage, M0.w, nr, it.k, X, y5, y6, rec, a.dbg, r0);
+            if (pair >= 0)
+                compute_tile_kq(stage + pair_offset(M0.w.tile_bytes), a.m[pair].w, nr, it.k, X, y5, y6,
+                                rec + size_t(R) * C * kRecWords, nullptr, r0);
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&P.empty[s]);
+                mbar_arrive(&P.rfull[b]);
+            }
+            ++seq;
+            tile_next(a, it);
+        }
+        return;
+    }
+    // fold (warp 1)
     KqAcc A0, A1;
     kq_reset(A0);
     kq_reset(A1);
-    unsigned seq = 0;
-    bool failed = false;
     while (tile_valid(a, it)) {
-        const unsigned s = seq % a.n_stages;
-        const bool ok = mbar_wait(&P.bar[s], (seq / a.n_stages) & 1u);
+        const unsigned b = seq % kNR;
+        if (!role_wait(&P.rfull[b], (seq / kNR) & 1u, P.abort)) {
+            fail_pass(a, P.abort);
+            break;
+        }
         const GemvMemberArgs &M0 = unit_member(a, it.unit);
         const int pair = a.unit_pair[it.unit];
         const unsigned t = it.item - a.item_start[it.unit];
         const unsigned R = M0.w.rt, C = M0.w.ct;
         const unsigned r0 = t * R, nr = min(R, M0.w.rows - r0);
-        uint32_t *rec = reinterpret_cast<uint32_t *>(P.res[seq & 1u]);
-        const uint8_t *stage = P.stages + size_t(s) * a.stage_bytes;
-        if (ok) {
-            compute_tile_kq(stage, M0.w, nr, it.k, X, y5, y6, rec, a.dbg, r0);
-            if (pair >= 0)
-                compute_tile_kq(stage + pair_offset(M0.w.tile_bytes), a.m[pair].w, nr, it.k, X, y5, y6,
-                                rec + size_t(R) * C * kRecWords, nullptr, r0);
-        }
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
-        }
-        if (threadIdx.x == 0 && tile_valid(a, issue)) {
-            issue_stage(a, issue, P.stages + size_t(s) * a.stage_bytes, &P.bar[s], policy);
-            tile_next(a, issue);
-            ++issued;
-        }
+        const uint32_t *rec = reinterpret_cast<const uint32_t *>((b ? P.res[1] : P.res[0]));
         if (!a.dbg) {
             const bool last = it.k + 1 == M0.w.kc;
-            if (threadIdx.x < nr) {
-                kq_fold(A0, rec + size_t(threadIdx.x) * C * kRecWords, C, it.k, M0.w.format, X);
-                if (pair >= 0)
-                    kq_fold(A1, rec + size_t(R + threadIdx.x) * C * kRecWords, C, it.k, a.m[pair].w.format, X);
+            if (lane < nr) {
+                kq_fold(A0, rec + size_t(lane) * C * kRecWords, C, it.k, M0.w.format, X);
+                if (pair >= 0) kq_fold(A1, rec + size_t(R + lane) * C * kRecWords, C, it.k, a.m[pair].w.format, X);
                 if (last) {
-                    const unsigned gr = M0.w.row0 + r0 + threadIdx.x;
+                    const unsigned gr = M0.w.row0 + r0 + lane;
                     if (pair >= 0) write_row(a.m[pair], gr, kq_final(A1), kq_final(A0));
                     else write_row(M0, gr, kq_final(A0), 0.0f);
                     kq_reset(A0);
                     kq_reset(A1);
                 }
             }
-            if (last && threadIdx.x >= 32 && threadIdx.x < 48)
-                write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, threadIdx.x - 32);
+            if (last) write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, lane);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&P.rempty[b]);
         ++seq;
         tile_next(a, it);
-    }
-    if (failed) {
-        if (threadIdx.x == 0) {
-            if (a.err) atomicExch(a.err, 1u);
-            for (unsigned q = seq; q < issued; ++q) mbar_wait(&P.bar[q % a.n_stages], (q / a.n_stages) & 1u);
-        }
-        __syncthreads();
     }
 }
 
@@ -294,11 +306,13 @@ void plan_gemv_kq(GemvArgs &a, size_t &smem) {
     }
     a.stage_bytes = (stage + 127u) & ~127u;
     a.res_bytes = (res + 127u) & ~127u;
-    const size_t xb = ((ximage_bytes(a.cols) + 127) & ~size_t(127)) + size_t(a.cols) / 4 * 4 + size_t(a.cols) / 2 * 4;
-    unsigned ns = 4;
-    while (ns > 2 && pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, xb) > 113 * 1024) --ns;
+    const bool norm_w = (a.norm_mode & 8u) && !(a.norm_mode & 2u) && !a.xq;
+    a.wraw = norm_w && a.cols <= 4096 ? 1u : 0u;
+    const size_t extra = size_t(a.cols) / 4 * 4 + size_t(a.cols) / 2 * 4;
+    unsigned ns = kMaxStages;
+    while (ns > 2 && pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, a.cols, a.wraw, extra) > 113 * 1024) --ns;
     a.n_stages = ns;
-    smem = pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, xb);
+    smem = pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, a.cols, a.wraw, extra);
 }
 
 cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl) {

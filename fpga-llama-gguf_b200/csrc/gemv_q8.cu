@@ -19,157 +19,187 @@ namespace b200q {
 
 __host__ __device__ inline unsigned res_stride(unsigned C) { return C + ((36u - C % 32u) % 32u); }
 
+// One tile (R rows x C blocks, C a power of two <= 32) by the 8 compute warps: a warp instruction covers 32 / C
+// rows x C blocks (lane = row sub-index * C + block), so a lane's x block (and its scale and sum) is loaded once per
+// tile; the warp walks its row groups two at a time. Per item: exact integer block dot (dp4a), FP32 term
+// float(sumi) * (d_w * d_x), stored to the result buffer (row stride cs).
 template <unsigned FMT>
-__device__ __forceinline__ void compute_tile(const uint8_t *tile, const MatrixView &w, unsigned nr, unsigned k,
-                                             const XImage &X, float *res, unsigned cs, int32_t *dbg, unsigned r0) {
+__device__ __forceinline__ void compute_tile(uint32_t s_tile, uint32_t qs_part, unsigned C, unsigned nr, unsigned kC,
+                                             uint32_t s_xq, uint32_t s_xd, uint32_t s_xs, uint32_t s_xb,
+                                             uint32_t s_res, unsigned cs, int32_t *dbg, size_t dbg_row0,
+                                             unsigned nb) {
+    constexpr unsigned QB = FMT == 8 ? 32 : 16;
     constexpr unsigned DB = FMT == 3 ? 4 : 2;
-    const unsigned C = w.ct, items = nr * C;
-    const uint8_t *qs = tile, *dm = tile + w.qs_part;
-    unsigned r = threadIdx.x / C, c = threadIdx.x % C;
-    const unsigned dr = kPassThreads / C, dc = kPassThreads % C;
-    for (unsigned idx = threadIdx.x; idx < items; idx += kPassThreads) {
-        const unsigned i = r * C + c, blk = k * C + c;
-        const int4 x0 = *reinterpret_cast<const int4 *>(X.q + blk * 32);
-        const int4 x1 = *reinterpret_cast<const int4 *>(X.q + blk * 32 + 16);
-        int dot = 0;
+    const unsigned warp = threadIdx.x / 32 - 2, lane = threadIdx.x % 32;
+    const unsigned c = lane & (C - 1), rsub = lane / C, rows_per_group = 32 / C;
+    const unsigned groups = (nr + rows_per_group - 1) / rows_per_group;
+    const unsigned blk = kC + c;
+    const uint32_t s_dm = s_tile + qs_part;
+    // this lane's x block, for all rows of the tile
+    const uint4 x0 = lds128(s_xq + blk * 32), x1 = lds128(s_xq + blk * 32 + 16);
+    const float xd = ldsf(s_xd + blk * 4);
+    const int xcorr = FMT == 2 ? 8 * int(lds32(s_xb + blk * 4)) : 0;
+    const float xs = FMT == 3 ? ldsf(s_xs + blk * 4) : 0.0f;
+    auto item = [&](unsigned r) {
+        const unsigned i = r * C + c;
+        int d0 = 0, d1 = 0;
         if (FMT == 8) {
-            const int4 w0 = *reinterpret_cast<const int4 *>(qs + i * 32);
-            const int4 w1 = *reinterpret_cast<const int4 *>(qs + i * 32 + 16);
-            dot = __dp4a(w0.x, x0.x, dot);
-            dot = __dp4a(w0.y, x0.y, dot);
-            dot = __dp4a(w0.z, x0.z, dot);
-            dot = __dp4a(w0.w, x0.w, dot);
-            dot = __dp4a(w1.x, x1.x, dot);
-            dot = __dp4a(w1.y, x1.y, dot);
-            dot = __dp4a(w1.z, x1.z, dot);
-            dot = __dp4a(w1.w, x1.w, dot);
+            const uint4 w0 = lds128(s_tile + i * QB), w1 = lds128(s_tile + i * QB + 16);
+            d0 = __dp4a(int(w0.x), int(x0.x), d0);
+            d1 = __dp4a(int(w1.x), int(x1.x), d1);
+            d0 = __dp4a(int(w0.y), int(x0.y), d0);
+            d1 = __dp4a(int(w1.y), int(x1.y), d1);
+            d0 = __dp4a(int(w0.z), int(x0.z), d0);
+            d1 = __dp4a(int(w1.z), int(x1.z), d1);
+            d0 = __dp4a(int(w0.w), int(x0.w), d0);
+            d1 = __dp4a(int(w1.w), int(x1.w), d1);
         } else {
             // byte j: low nibble = element j, high nibble = element j + 16
-            const uint4 wv = *reinterpret_cast<const uint4 *>(qs + i * 16);
+            const uint4 wv = lds128(s_tile + i * QB);
             const uint32_t m = 0x0F0F0F0Fu;
-            dot = __dp4a(int(wv.x & m), x0.x, dot);
-            dot = __dp4a(int(wv.y & m), x0.y, dot);
-            dot = __dp4a(int(wv.z & m), x0.z, dot);
-            dot = __dp4a(int(wv.w & m), x0.w, dot);
-            dot = __dp4a(int((wv.x >> 4) & m), x1.x, dot);
-            dot = __dp4a(int((wv.y >> 4) & m), x1.y, dot);
-            dot = __dp4a(int((wv.z >> 4) & m), x1.z, dot);
-            dot = __dp4a(int((wv.w >> 4) & m), x1.w, dot);
+            d0 = __dp4a(int(wv.x & m), int(x0.x), d0);
+            d1 = __dp4a(int((wv.x >> 4) & m), int(x1.x), d1);
+            d0 = __dp4a(int(wv.y & m), int(x0.y), d0);
+            d1 = __dp4a(int((wv.y >> 4) & m), int(x1.y), d1);
+            d0 = __dp4a(int(wv.z & m), int(x0.z), d0);
+            d1 = __dp4a(int((wv.z >> 4) & m), int(x1.z), d1);
+            d0 = __dp4a(int(wv.w & m), int(x0.w), d0);
+            d1 = __dp4a(int((wv.w >> 4) & m), int(x1.w), d1);
         }
-        int sumi = dot;
-        if (FMT == 2) sumi -= 8 * X.b[blk];  // sum (w - 8) q = sum w q - 8 sum q
+        const int sumi = d0 + d1 - xcorr;  // Q4_0: sum (w - 8) q = sum w q - 8 sum q
         float term;
         if (FMT == 3) {
             // (d_w * d_8) * sumi + m_w * s_8 (gemvq_ref.h:221-223)
-            const uint32_t dmv = *reinterpret_cast<const uint32_t *>(dm + i * 4);
+            const uint32_t dmv = lds32(s_dm + i * 4);
             const float dw = half_bits_to_float(uint16_t(dmv & 0xffffu)), mw = half_bits_to_float(uint16_t(dmv >> 16));
-            term = fadd(fmul(fmul(dw, X.d[blk]), float(sumi)), fmul(mw, X.s[blk]));
+            term = fadd(fmul(fmul(dw, xd), float(sumi)), fmul(mw, xs));
         } else {
-            const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(dm + i * DB));
-            term = fmul(float(sumi), fmul(dw, X.d[blk]));
+            const float dw = half_bits_to_float(lds16(s_dm + i * DB));
+            term = fmul(float(sumi), fmul(dw, xd));
         }
-        res[r * cs + c] = term;
-        if (dbg) dbg[size_t(w.row0 + r0 + r) * (w.kc * C) + blk] = sumi;
-        r += dr;
-        c += dc;
-        if (c >= C) { c -= C; ++r; }
+        stsf(s_res + (r * cs + c) * 4, term);
+        if (dbg) dbg[(dbg_row0 + r) * nb + blk] = sumi;
+    };
+    unsigned g = warp;
+    for (; g + kComputeWarps < groups; g += 2 * kComputeWarps) {
+        const unsigned ra = g * rows_per_group + rsub, rb = (g + kComputeWarps) * rows_per_group + rsub;
+        if (ra < nr) item(ra);
+        if (rb < nr) item(rb);
+    }
+    if (g < groups) {
+        const unsigned ra = g * rows_per_group + rsub;
+        if (ra < nr) item(ra);
     }
 }
 
 __device__ __forceinline__ void compute_tile_any(const uint8_t *tile, const MatrixView &w, unsigned nr, unsigned k,
                                                  const XImage &X, float *res, unsigned cs, int32_t *dbg, unsigned r0) {
+    const uint32_t st = smem_addr(tile), sq = smem_addr(X.q), sd = smem_addr(X.d), ss = smem_addr(X.s);
+    const uint32_t sb = smem_addr(X.b), sr = smem_addr(res);
+    const unsigned C = w.ct, nb = w.kc * w.ct;
+    const size_t drow = size_t(w.row0) + r0;
     switch (w.format) {
-    case 2: compute_tile<2>(tile, w, nr, k, X, res, cs, dbg, r0); break;
-    case 8: compute_tile<8>(tile, w, nr, k, X, res, cs, dbg, r0); break;
-    default: compute_tile<3>(tile, w, nr, k, X, res, cs, dbg, r0); break;
+    case 2: compute_tile<2>(st, w.qs_part, C, nr, k * C, sq, sd, ss, sb, sr, cs, dbg, drow, nb); break;
+    case 8: compute_tile<8>(st, w.qs_part, C, nr, k * C, sq, sd, ss, sb, sr, cs, dbg, drow, nb); break;
+    default: compute_tile<3>(st, w.qs_part, C, nr, k * C, sq, sd, ss, sb, sr, cs, dbg, drow, nb); break;
     }
 }
 
-// sum += term over one tile's C terms, in block order
-__device__ __forceinline__ float fold_terms(float s, const float *row, unsigned C) {
+// sum += term over one tile's C terms, in block order (row at shared address a, 16-byte aligned)
+__device__ __forceinline__ float fold_terms(float s, uint32_t a, unsigned C) {
     unsigned c = 0;
     for (; c + 4 <= C; c += 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(row + c);
-        s = fadd(s, v.x);
-        s = fadd(s, v.y);
-        s = fadd(s, v.z);
-        s = fadd(s, v.w);
+        const uint4 v = lds128(a + c * 4);
+        s = fadd(s, __uint_as_float(v.x));
+        s = fadd(s, __uint_as_float(v.y));
+        s = fadd(s, __uint_as_float(v.z));
+        s = fadd(s, __uint_as_float(v.w));
     }
-    for (; c < C; ++c) s = fadd(s, row[c]);
+    for (; c < C; ++c) s = fadd(s, ldsf(a + c * 4));
     return s;
 }
 
-__global__ void __launch_bounds__(kPassThreads, 2) gemv_q8_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kPassThreads, 2) gemv_q8_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const PassSmem P = carve_pass(smem, a);
     const XImage X = carve_ximage(P.ximg, a.cols);
-    const uint64_t policy = evict_first_policy();
-    TileIt issue = tile_first(a);
-    unsigned issued = pass_prologue(a, P, issue, policy);  // copies started (thread 0's count)
+    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) init_pass_barriers(a, P);
+    __syncthreads();
     pdl_launch_dependents();  // the next kernel may start its own weight copies as SMs free up
+    if (warp == 0) {
+        if (lane == 0) producer_loop(a, P);
+        return;
+    }
     pdl_wait();
-    const unsigned act = a.m[0].w.format == 3 ? 1u : 0u;
-    if (a.xq) load_quant_cta(a.xq, a.xd, a.xs, a.xb, a.cols, act, X);
-    else quantize_cta(a.x, a.cols, act, a.norm_w, a.norm_eps, a.norm_mode, X);
+    prepare_x(a, P, X, a.m[0].w.format == 3 ? 1u : 0u);
     TileIt it = tile_first(a);
-    float acc0 = 0.0f, acc1 = 0.0f;
     unsigned seq = 0;
-    bool failed = false;
+    if (warp >= 2) {  // compute
+        while (tile_valid(a, it)) {
+            const unsigned s = seq % a.n_stages, b = seq % kNR;
+            const bool ok = compute_acquire(P, seq, a.n_stages);
+            if (!ok) {
+                fail_pass(a, P.abort);
+                break;
+            }
+            const GemvMemberArgs &M0 = unit_member(a, it.unit);
+            const int pair = a.unit_pair[it.unit];
+            const unsigned t = it.item - a.item_start[it.unit];
+            const unsigned R = M0.w.rt, cs = res_stride(M0.w.ct);
+            const unsigned r0 = t * R, nr = min(R, M0.w.rows - r0);
+            float *res = reinterpret_cast<float *>((b ? P.res[1] : P.res[0]));
+            const uint8_t *stage = P.stages + size_t(s) * a.stage_bytes;
+            compute_tile_any(stage, M0.w, nr, it.k, X, res, cs, a.dbg, r0);
+            if (pair >= 0)
+                compute_tile_any(stage + pair_offset(M0.w.tile_bytes), a.m[pair].w, nr, it.k, X, res + R * cs, cs,
+                                 nullptr, r0);
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&P.empty[s]);
+                mbar_arrive(&P.rfull[b]);
+            }
+            ++seq;
+            tile_next(a, it);
+        }
+        return;
+    }
+    // fold (warp 1): lane r adds row r's terms in block order
+    float acc0 = 0.0f, acc1 = 0.0f;
     while (tile_valid(a, it)) {
-        const unsigned s = seq % a.n_stages;
-        const bool ok = mbar_wait(&P.bar[s], (seq / a.n_stages) & 1u);
+        const unsigned b = seq % kNR;
+        if (!role_wait(&P.rfull[b], (seq / kNR) & 1u, P.abort)) {
+            fail_pass(a, P.abort);
+            break;
+        }
         const GemvMemberArgs &M0 = unit_member(a, it.unit);
         const int pair = a.unit_pair[it.unit];
         const unsigned t = it.item - a.item_start[it.unit];
         const unsigned R = M0.w.rt, C = M0.w.ct, cs = res_stride(C);
         const unsigned r0 = t * R, nr = min(R, M0.w.rows - r0);
-        float *res = reinterpret_cast<float *>(P.res[seq & 1u]);
-        const uint8_t *stage = P.stages + size_t(s) * a.stage_bytes;
-        if (ok) {
-            compute_tile_any(stage, M0.w, nr, it.k, X, res, cs, a.dbg, r0);
-            if (pair >= 0)
-                compute_tile_any(stage + pair_offset(M0.w.tile_bytes), a.m[pair].w, nr, it.k, X, res + R * cs, cs,
-                                 nullptr, r0);
-        }
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
-        }
-        // the stage is consumed: refill it with the tile n_stages positions ahead
-        if (threadIdx.x == 0 && tile_valid(a, issue)) {
-            issue_stage(a, issue, P.stages + size_t(s) * a.stage_bytes, &P.bar[s], policy);
-            tile_next(a, issue);
-            ++issued;
-        }
+        const uint32_t res = smem_addr((b ? P.res[1] : P.res[0]));
         if (!a.dbg) {
             const bool last = it.k + 1 == M0.w.kc;
-            if (threadIdx.x < nr) {
-                acc0 = fold_terms(acc0, res + threadIdx.x * cs, C);
-                if (pair >= 0) acc1 = fold_terms(acc1, res + (R + threadIdx.x) * cs, C);
+            if (lane < nr) {
+                acc0 = fold_terms(acc0, res + lane * cs * 4, C);
+                if (pair >= 0) acc1 = fold_terms(acc1, res + (R + lane) * cs * 4, C);
                 if (last) {
-                    const unsigned gr = M0.w.row0 + r0 + threadIdx.x;
+                    const unsigned gr = M0.w.row0 + r0 + lane;
                     if (pair >= 0) write_row(a.m[pair], gr, acc1, acc0);
                     else write_row(M0, gr, acc0, 0.0f);
                     acc0 = acc1 = 0.0f;
                 }
             }
-            if (last && threadIdx.x >= 32 && threadIdx.x < 48)
-                write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, threadIdx.x - 32);
+            if (last) write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, lane);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&P.rempty[b]);
         ++seq;
         tile_next(a, it);
     }
-    if (failed) {
-        // a copy did not arrive in time: report, then wait (bounded) for the copies still in flight
-        if (threadIdx.x == 0) {
-            if (a.err) atomicExch(a.err, 1u);
-            for (unsigned q = seq; q < issued; ++q) mbar_wait(&P.bar[q % a.n_stages], (q / a.n_stages) & 1u);
-        }
-        __syncthreads();
-    }
 }
 
-__global__ void __launch_bounds__(kPassThreads) quantize_kernel(const QuantArgs a) {
+__global__ void __launch_bounds__(256) quantize_kernel(const QuantArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const XImage X = carve_ximage(smem, a.n);
     pdl_wait();
@@ -193,7 +223,7 @@ __global__ void __launch_bounds__(kPassThreads) quantize_kernel(const QuantArgs 
 }
 
 // Shared memory plan of a Q8 pass (see PassSmem): stage = the largest unit tile (x2 for a pair), results = the
-// largest R x stride terms (x2 for a pair).
+// largest R x stride terms (x2 for a pair); as many stages as fit two CTAs per SM.
 void plan_gemv_q8(GemvArgs &a, size_t &smem) {
     unsigned stage = 0, res = 0;
     for (unsigned u = 0; u < a.n_units; ++u) {
@@ -206,12 +236,12 @@ void plan_gemv_q8(GemvArgs &a, size_t &smem) {
     }
     a.stage_bytes = (stage + 127u) & ~127u;
     a.res_bytes = (res + 127u) & ~127u;
-    const size_t xb = (ximage_bytes(a.cols) + 127) & ~size_t(127);
-    // as many stages as fit two CTAs per SM (<= 113 KB each), at least 2, at most 4
-    unsigned ns = 4;
-    while (ns > 2 && pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, xb) > 113 * 1024) --ns;
+    const bool norm_w = (a.norm_mode & 8u) && !(a.norm_mode & 2u) && !a.xq;
+    a.wraw = norm_w && a.cols <= 4096 ? 1u : 0u;
+    unsigned ns = kMaxStages;
+    while (ns > 2 && pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, a.cols, a.wraw, 0) > 113 * 1024) --ns;
     a.n_stages = ns;
-    smem = pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, xb);
+    smem = pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, a.cols, a.wraw, 0);
 }
 
 cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl) {
@@ -240,7 +270,7 @@ cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st) {
         attr_set = true;
     }
     const size_t smem = (ximage_bytes(a.n) + 127) & ~size_t(127);
-    quantize_kernel<<<1, kPassThreads, smem, st>>>(a);
+    quantize_kernel<<<1, 256, smem, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -52,6 +52,7 @@ struct GemvArgs {
     unsigned item_start[kMaxUnits + 1] = {};   // prefix sums of the units' row tiles
     // shared-memory plan (host-computed): stages of stage_bytes, per-stage compute results, x image
     unsigned n_stages = 0, stage_bytes = 0, res_bytes = 0;
+    unsigned wraw = 0;            // the norm weight is staged in shared memory next to x
     unsigned *err = nullptr;      // set when a bounded wait runs out
     int32_t *dbg = nullptr;       // debug: per-block integer sums of member 0 (no y written)
 };

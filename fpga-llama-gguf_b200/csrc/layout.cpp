@@ -148,15 +148,27 @@ DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sm
     if (rows == 0 || L.blocks == 0) return L;
     const unsigned ub = L.qb + L.db + L.dd;
     const size_t target = (f == 13 || f == 14) ? kTileTargetK : kTileTarget;
-    // R: the largest power of two <= 32 that still gives every SM about four row tiles
-    unsigned R = 32;
-    while (R > 1 && (rows + R - 1) / R < 4u * (sms ? sms : 148u)) R /= 2;
-    // C: the largest divisor of the row's blocks that keeps a tile within the target
+    // R: rows per tile such that the matrix splits into about one tile per CTA of a pass (two CTAs per SM), so
+    // every CTA of a pass streams the same bytes; at most 32 (one fold lane per row)
+    const unsigned ctas = 2u * (sms ? sms : 148u);
+    unsigned R = (rows + ctas - 1) / ctas;
+    R = R < 1 ? 1 : (R > 32 ? 32 : R);
+    // C: Q8_0-family tiles take a power of two <= 32 blocks (lane = (row, block) in the compute warps; a lane's x
+    // block stays in registers for the whole tile); K-quant tiles the largest divisor of the row's super-blocks.
+    // Both within the tile target.
     unsigned C = 1;
-    for (unsigned c = L.blocks; c >= 1; --c) {
-        if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
+    if (f == 13 || f == 14) {
+        for (unsigned c = L.blocks; c >= 1; --c) {
+            if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
+        }
+        while (R > 1 && size_t(R) * C * ub > target) --R;
+    } else {
+        for (unsigned c = 32; c >= 4; c /= 2) {
+            if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
+        }
+        if (C == 1) C = 4;  // cols is a multiple of 128: 4 always divides the blocks
+        while (R > 1 && size_t(R) * C * ub > target) --R;
     }
-    while (R > 1 && size_t(R) * C * ub > target) R /= 2;
     L.rt = R;
     L.ct = C;
     L.kc = L.blocks / C;

@@ -115,6 +115,7 @@ extern "C" {
 #define B200Q_ERR_DISABLED (-4) /* an earlier CUDA failure disabled the context */
 #define B200Q_ERR_COMM (-5)     /* NCCL failure or missing communicator */
 #define B200Q_ERR_STATE (-6)    /* call out of order (e.g. graph launch on another context) */
+#define B200Q_ERR_TIMEOUT (-7)  /* a kernel's bounded wait ran out (reported by b200q_run / b200q_synchronize) */
 
 typedef struct b200q_ctx b200q_ctx;
 typedef struct b200q_graph b200q_graph;
