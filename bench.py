@@ -3,10 +3,11 @@
 
 Workload (the fused FFN block of a 4B-like layer): RMSNorm (eps 1e-6, gain N(1, 0.1))
 deferred into the Q8_0 quantizer, gate and up Q8_0 GEMVs [9216 x 2560] in one pass with the SwiGLU epilogue, the
-down Q8_0 GEMV [2560 x 9216] with the residual ADD epilogue — one command list of the reference ISA, replayed as one
-CUDA Graph per step. A step is one pass of the block over one token. Synthetic seeded weights with the config's
-distributions (no model files here). L2: the step rotates through enough distinct weight copies that the weights
-read per round exceed the 126 MB L2 (each step reads weights that are not L2-resident).
+down Q8_0 GEMV [2560 x 9216] with the residual ADD epilogue. The blocks are stacked as the layers of a model: L
+blocks with distinct weights, each reading the residual stream the previous one wrote, form one command list of the
+reference ISA, replayed as one CUDA Graph per step (one token through the L-layer stack). L is chosen so that the
+weights of one step exceed 3x the 126 MB L2, so every block reads weights that are not L2-resident. Synthetic seeded
+weights with the config's distributions (no model files here).
 
 metric: GEMV HBM GB/s = algorithmic bytes of the block (weights in their GGUF bits + x, gain, residual, y) per step
 / device time per step. N GPUs (torchrun): every matrix is row-sharded over the GPUs and the outputs all-gathered
@@ -35,6 +36,7 @@ sys.path.insert(0, ROOT)
 H, F = 2560, 9216
 EPS = 1e-6
 XIN, GAIN, XN, FF, OUT = 0, H, 2 * H, 4 * H, 4 * H + F
+RES = (XIN, OUT)  # the residual stream alternates between these two rows, layer by layer
 ACT_FLOATS = 1 << 16
 L2_BYTES = 126 << 20
 
@@ -66,11 +68,21 @@ def gen_block(synth, seed: int):
     return synth.q8_0(r, F, H), synth.q8_0(r, F, H), synth.q8_0(r, H, F)
 
 
-def block_list(b2, hg, hu, hd):
+def block_list(b2, hg, hu, hd, xin=XIN, out=OUT):
     return b2.cmd_list(
-        b2.rmsnorm(H, XIN, GAIN, XN, EPS, flags=b2.NORM_DEFER),
+        b2.rmsnorm(H, xin, GAIN, XN, EPS, flags=b2.NORM_DEFER),
         b2.gemv(b2.Q8_0, F, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(b2.Q8_0, F, H, hu, XN, FF),
-        b2.gemv(b2.Q8_0, H, F, hd, FF, OUT, b2.GEMV_ADD), b2.add(H, OUT, XIN, OUT))
+        b2.gemv(b2.Q8_0, H, F, hd, FF, out, b2.GEMV_ADD), b2.add(H, out, xin, out))
+
+
+def stack_list(b2, layers, upto=None):
+    """Command list of the layer stack (layer c: residual RES[c % 2] -> RES[(c + 1) % 2]); `upto` keeps only the
+    first `upto` commands of each block (8 words each)."""
+    parts = []
+    for c, (hg, hu, hd) in enumerate(layers):
+        cl = block_list(b2, hg, hu, hd, RES[c % 2], RES[(c + 1) % 2])
+        parts.append(cl[: upto * 8] if upto else cl)
+    return np.concatenate(parts)
 
 
 class ClockSampler:
@@ -172,8 +184,8 @@ def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     args = ap.parse_args()
@@ -181,15 +193,21 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     config = {"workload": "configs[1] fused FFN block: deferred RMSNorm -> Q8_0 gate+up (SwiGLU) -> Q8_0 down "
-                          "(+residual), hidden 2560, FFN 9216", "global_batch": 1, "seq_len": 1,
+                          "(+residual), hidden 2560, FFN 9216, stacked as the layers of one decode step",
+              "global_batch": 1, "seq_len": 1,
               "parallelism": f"row-sharded x{world}" if world > 1 else "1 GPU"}
+
+    per_layer = weight_bytes() // world
+    n_layers = min(40, max(2, int(np.ceil(3 * L2_BYTES / max(per_layer, 1)))))
+    config["layers"] = n_layers
 
     if args.impl == "reference":
         if rank != 0:
             return 0
         cb = cpu_reference(args.steps, min(args.warmup, 1), args.cpu_budget, "reference")
         line = {"metric": "GEMV HBM GB/s", "value": cb["value"], "unit": "GB/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(algorithmic_bytes() / cb["value"] / 1e6, 4),
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(n_layers * algorithmic_bytes() / cb["value"] / 1e6, 4),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8/f32",
                 "data": "synthetic", "config": config, "impl": "reference", "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -208,24 +226,17 @@ def main():
     dev = local if world > 1 else 0
     torch.cuda.set_device(dev)
 
-    # enough weight copies that one round of steps reads more than 3x the L2
-    per_copy = weight_bytes() // world
-    copies = max(2, int(np.ceil(3 * L2_BYTES / max(per_copy, 1))))
-    copies = min(copies, 40)
-    ctx = b2.Context(device=dev, weight_bytes=copies * (per_copy + (8 << 20)) + (64 << 20), act_floats=ACT_FLOATS)
+    # n_layers: enough layers that one step reads more than 3x the L2
+    ctx = b2.Context(device=dev, weight_bytes=n_layers * (per_layer + (8 << 20)) + (64 << 20), act_floats=ACT_FLOATS)
     if world > 1:
         obj = [b2.Context.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         ctx.comm_init(world, rank, obj[0])
-    graphs, lists = [], []
     mats = gen_block(synth, 0)
-    for c in range(copies):
-        hg = ctx.upload(mats[0], F, H, b2.Q8_0)
-        hu = ctx.upload(mats[1], F, H, b2.Q8_0)
-        hd = ctx.upload(mats[2], H, F, b2.Q8_0)
-        cl = block_list(b2, hg, hu, hd)
-        lists.append(cl)
-        graphs.append(ctx.graph(cl))
+    layers = [tuple(ctx.upload(m, rows, cols, b2.Q8_0) for m, rows, cols in ((mats[0], F, H), (mats[1], F, H),
+                                                                           (mats[2], H, F)))
+              for _ in range(n_layers)]
+    stack = ctx.graph(stack_list(b2, layers))
     r = synth.rng(1, 99)
     x = synth.activation(r, H)
     gain = r.normal(1, 0.1, H).astype(np.float32)
@@ -246,62 +257,62 @@ def main():
         return float(t.item())
 
     # warm-up
-    ctx.launch_many(graphs, args.warmup)
+    ctx.launch_many([stack], args.warmup)
     ctx.synchronize()
     barrier()
-    # timed region: K steps
+    # timed region: K steps (each a replay of the whole stack)
     with ClockSampler(dev) as clk:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        ctx.launch_many(graphs, args.steps)
+        ctx.launch_many([stack], args.steps)
         end.record(stream)
         end.synchronize()
         ms = start.elapsed_time(end) / args.steps
         ms = max_over_ranks(ms)
         barrier()
     clocks = clk.summary()
-    value = algorithmic_bytes() / (ms * 1e-3) / 1e9
-    launches = sum(g.kernels for g in graphs[:1]) * args.steps
+    step_bytes = n_layers * algorithmic_bytes()
+    value = step_bytes / (ms * 1e-3) / 1e9
+    launches = stack.kernels * args.steps
 
-    # roofline of the dominant kernel (the gate+up pass): timed alone, rotating copies, CUDA events on the stream
+    # roofline of the dominant kernel (the gate+up pass): the stack's gate+up passes alone, one graph, CUDA events
     peak, peak_kind = measured_peak()
-    ru_graphs = []
-    for c in range(copies):
-        cl = lists[c]
-        ru_graphs.append(ctx.graph(cl[: 3 * 8]))  # deferred norm + gate/up pair: one GEMV kernel
-    ctx.launch_many(ru_graphs, 5)
+    ru = ctx.graph(stack_list(b2, layers, upto=3))  # per layer: deferred norm + gate/up pair = one GEMV kernel
+    ctx.launch_many([ru], 5)
     ctx.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_ru = max(20, args.steps)
+    n_ru = max(20, args.steps // 4)
     s2.record(stream)
-    ctx.launch_many(ru_graphs, n_ru)
+    ctx.launch_many([ru], n_ru)
     e2.record(stream)
     e2.synchronize()
-    ru_ms = max_over_ranks(s2.elapsed_time(e2) / n_ru)
+    ru_ms = max_over_ranks(s2.elapsed_time(e2) / (n_ru * n_layers))
     ru_bytes = 2 * F * (H // 32) * 34 + 4 * (H + H)
     achieved = ru_bytes / (ru_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": None,
                 "kernel": "gemv_q8_kernel (deferred RMSNorm + Q8_0 gate/up pair + SwiGLU)",
-                "algorithmic_bytes_per_launch": ru_bytes, "peak_kind": peak_kind}
+                "algorithmic_bytes_per_launch": ru_bytes, "us_per_launch": round(ru_ms * 1e3, 3),
+                "peak_kind": peak_kind}
     try:
         prof = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
         roofline["traffic"] = prof.get("gemv_q8_kernel_gate_up")
     except Exception:
         pass
 
-    # end to end through the public API with host buffers: x in (pinned), run, y out
+    # end to end through the public API with host buffers: x in (pinned), one token through the stack, y out
     xin = torch.from_numpy(x).pin_memory().numpy()
     yout = torch.empty(H, dtype=torch.float32).pin_memory().numpy()
-    e2e_steps = min(args.steps, 100)
+    y_row = RES[n_layers % 2]
+    e2e_steps = min(args.steps, 200)
     barrier()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
         ctx.write(XIN, xin)
-        graphs[i % copies].launch()
-        yout[:] = ctx.read(OUT, H)
+        stack.launch()
+        yout[:] = ctx.read(y_row, H)
     t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
-    e2e = {"value": round(algorithmic_bytes() / t_e2e / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
+    e2e = {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
            "d2h_bytes_per_step": 4 * H, "ms_per_step": round(t_e2e * 1e3, 4)}
 
     cpu = None
@@ -311,7 +322,7 @@ def main():
         except Exception as e:  # the CPU baseline is a reported number only
             cpu = {"value": None, "error": str(e)}
 
-    for g in graphs + ru_graphs:
+    for g in (stack, ru):
         g.close()
     ctx.close()
     if dist:
@@ -321,8 +332,9 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32",
                 "data": "synthetic (seeded GGUF Q8_0 weights of config 1)",
-                "config": dict(config, l2=f"{copies} distinct weight copies rotated ({copies * per_copy >> 20} MiB per "
-                                           f"GPU > L2)", frac_of_peak=round(value / peak, 4)),
+                "config": dict(config, l2=f"{n_layers} layers with distinct weights per step "
+                                                             f"({n_layers * per_layer >> 20} MiB per GPU > 3x L2)",
+                               frac_of_peak=round(value / peak, 4)),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     return 0

@@ -93,6 +93,9 @@ struct b200q_ctx {
     int32_t *xb = nullptr;
     uint16_t *xd16 = nullptr;
     float *ndrow = nullptr;
+    // quantized x images handed from a GEMV pass to the next (Q8_0 / Q8_1 of the output, in the GEMV shared-memory
+    // layout), two alternating buffers
+    uint8_t *qimg[2] = {nullptr, nullptr};
     float *snap = nullptr;
     size_t snap_used = 0;
     unsigned *dstatus = nullptr;
@@ -194,8 +197,17 @@ int all_gather_rows(b200q_ctx *c, float *base, size_t per_rank) {
 }
 
 // ---- one GEMV group ------------------------------------------------------------------------------------------------
+// A GEMV pass's output handed to the next GEMV pass as its quantized x image (see link_image).
+struct ImageLink {
+    uint8_t *out = nullptr;      // this pass writes the image of member out_member's y here
+    unsigned out_member = 0;
+    unsigned out_act = 0;        // activation type of the next pass (0 Q8_0, 1 Q8_1)
+    const uint8_t *in = nullptr;  // this pass reads its x image from here
+};
+
 int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsigned cols, bool from_nd,
-              const DeferredNorm &nd, bool prequant, const float *x_override, int32_t *dbg) {
+              const DeferredNorm &nd, bool prequant, const float *x_override, int32_t *dbg,
+              const ImageLink &link = ImageLink()) {
     GemvArgs a;
     a.cols = cols;
     const unsigned act = act_type(mem[0].format);
@@ -251,6 +263,13 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
     bool xhit = false;
     for (const Range &w : writes) xhit |= meet(a.x, cols, w.p, w.n);
     if (a.norm_w) for (const Range &w : writes) xhit |= meet(a.norm_w, cols, w.p, w.n);
+    const bool use_image = link.in && !dbg && !(prequant || xhit);
+    if (use_image) a.qin = link.in;
+    if (link.out && !dbg) {
+        a.qout = link.out;
+        a.qout_member = link.out_member;
+        a.qout_act = link.out_act;
+    }
     if ((prequant || xhit) && !dbg) {
         QuantArgs q;
         q.x = a.x;
@@ -285,12 +304,48 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
     a.item_start[u] = items;
     a.err = c->dstatus + 1;
     size_t smem = 0;
-    if (kq) plan_gemv_kq(a, smem);
-    else plan_gemv_q8(a, smem);
-    const unsigned per_sm = smem <= 113 * 1024 ? 2u : 1u;
-    const unsigned grid = std::min(items, unsigned(c->sms) * per_sm);
-    CUDA_TRY(c, kq ? launch_gemv_kq(a, grid, smem, c->stream, c->pdl) : launch_gemv_q8(a, grid, smem, c->stream, c->pdl));
-    ++c->launches;
+    if (kq) {
+        plan_gemv_kq(a, smem);
+        const unsigned grid = std::min(items, unsigned(c->sms) * (smem <= 113 * 1024 ? 2u : 1u));
+        CUDA_TRY(c, launch_gemv_kq(a, grid, smem, c->stream, c->pdl));
+        ++c->launches;
+    } else {
+        // one launch per format combination of the units (a member alone, or a SwiGLU g/u pair); one panel per
+        // CTA when a launch's panels fit on the GPU at once, else every CTA loops over panels
+        plan_gemv_q8(a, smem);
+        bool done[kMaxUnits] = {};
+        for (unsigned i = 0; i < a.n_units; ++i) {
+            if (done[i]) continue;
+            const int pr = a.unit_pair[i];
+            const unsigned fa = a.m[a.unit_member[i]].w.format, fb = pr >= 0 ? a.m[pr].w.format : 0u;
+            GemvArgs g = a;
+            unsigned gu = 0, gi = 0;
+            for (unsigned k = i; k < a.n_units; ++k) {
+                const int pk = a.unit_pair[k];
+                const unsigned ka = a.m[a.unit_member[k]].w.format, kb = pk >= 0 ? a.m[pk].w.format : 0u;
+                if (done[k] || ka != fa || kb != fb) continue;
+                if (pk >= 0) {
+                    const MatrixView &gw = a.m[a.unit_member[k]].w, &uw = a.m[pk].w;
+                    if (gw.rt != uw.rt || gw.kc != uw.kc || gw.rows != uw.rows)
+                        return set_err(c, B200Q_ERR_ARG, "SwiGLU g and u weights have different panel shapes");
+                }
+                done[k] = true;
+                g.unit_member[gu] = a.unit_member[k];
+                g.unit_pair[gu] = pk;
+                g.item_start[gu] = gi;
+                gi += a.item_start[k + 1] - a.item_start[k];
+                ++gu;
+            }
+            g.n_units = gu;
+            g.item_start[gu] = gi;
+            if (!gemv_q8_supported(fa, fb)) return set_err(c, B200Q_ERR_ARG, "unsupported GEMV format combination");
+            // whole clusters (the x preparation is split over a cluster's CTAs)
+            const unsigned cl = gemv_q8_cluster();
+            const unsigned grid = std::min((gi + cl - 1) / cl * cl, gemv_q8_resident_ctas(fa, fb, smem, c->stream));
+            CUDA_TRY(c, launch_gemv_q8(g, fa, fb, grid, smem, c->stream, c->pdl));
+            ++c->launches;
+        }
+    }
     if (shard && !dbg) {
         for (unsigned i = 0; i < nm; ++i) {
             const GemvMemberArgs &g = a.m[i];
@@ -455,6 +510,30 @@ int stamp(b200q_ctx *c, bool on, unsigned cmd, unsigned kind) {
     return 0;
 }
 
+// Pass p's GEMV output that pass q (the next pass) reads as its whole x: pass p can write q's quantized x image
+// itself (one Q8_0/Q8_1 block per 32-row panel, from the values it writes), so q skips its x preparation. Needs:
+// q a Q8_0-family GEMV pass without a deferred norm reading exactly one member's y; that member and its SwiGLU
+// partner in 32-row panels, unsharded, with a plain / SwiGLU / residual-ADD writer. Returns the member index or -1.
+int link_image(const b200q_ctx *c, const Pass &p, const Pass &q) {
+    if (p.kind != PassKind::Gemv || q.kind != PassKind::Gemv || q.from_nd || q.prequant) return -1;
+    const unsigned qact = act_type(q.m[0].format);
+    if (qact == 2) return -1;
+    for (unsigned i = 0; i < p.n_members; ++i) {
+        const Member &m = p.m[i];
+        if (m.epi == EpiSwigluG || m.epi == EpiConv) continue;
+        if (m.y_off != q.x_off || m.rows != q.cols || act_type(m.format) == 2) continue;
+        if (m.rows % 32) return -1;
+        for (unsigned k = 0; k < p.n_members; ++k) {  // the member and its SwiGLU partner
+            if (k != i && !(m.epi == EpiSwigluU && k + 1 == i)) continue;
+            const WeightInfo *w = p.m[k].w ? p.m[k].w : find_w(c, p.m[k].handle);
+            if (!w || w->rt != 32 || w->row_begin != 0 || w->row_end != w->rows || act_type(w->format) == 2)
+                return -1;
+        }
+        return int(i);
+    }
+    return -1;
+}
+
 // Executes the passes of a plan on the context stream (no synchronization).
 int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
@@ -463,13 +542,32 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->host_tags.clear();
     const bool tr = plan.has_trace;
     int rc = 0;
-    for (const Pass &p : plan.passes) {
+    const uint8_t *img_in = nullptr;  // the image the previous GEMV pass wrote for this one
+    unsigned img_turn = 0;
+    for (size_t pi = 0; pi < plan.passes.size(); ++pi) {
+        const Pass &p = plan.passes[pi];
+        if (p.kind != PassKind::Gemv) img_in = nullptr;
         if ((rc = stamp(c, tr, p.first, 0))) return rc;
         const bool is_pass = p.kind == PassKind::Gemv || p.kind == PassKind::Gdn;
         if (is_pass && (rc = stamp(c, tr, p.first, 1))) return rc;
         switch (p.kind) {
         case PassKind::Gemv:
-            rc = exec_gemv(c, p.m, p.n_members, p.x_off, p.cols, p.from_nd, p.nd, p.prequant, nullptr, nullptr);
+        {
+            ImageLink link;
+            if (img_in) link.in = img_in;
+            img_in = nullptr;
+            if (pi + 1 < plan.passes.size()) {
+                const int mi = link_image(c, p, plan.passes[pi + 1]);
+                if (mi >= 0) {
+                    link.out = c->qimg[img_turn];
+                    link.out_member = unsigned(mi);
+                    link.out_act = act_type(plan.passes[pi + 1].m[0].format);
+                    img_in = c->qimg[img_turn];
+                    img_turn ^= 1u;
+                }
+            }
+            rc = exec_gemv(c, p.m, p.n_members, p.x_off, p.cols, p.from_nd, p.nd, p.prequant, nullptr, nullptr, link);
+        }
             break;
         case PassKind::Elementwise: rc = exec_elementwise(c, p); break;
         case PassKind::Gdn: rc = exec_gdn(c, p); break;
@@ -600,6 +698,10 @@ int b200q_create(const b200q_config *cfg, b200q_ctx **out) {
     c->tstamps = reinterpret_cast<unsigned long long *>(s);
     s += kMaxTraceEvents * 8;
     c->ttags = reinterpret_cast<uint32_t *>(s);
+    uint8_t *qi = nullptr;
+    if ((e = cudaMalloc(&qi, 2 * kQImageBytes)) != cudaSuccess) return fail(e, "image scratch");
+    c->qimg[0] = qi;
+    c->qimg[1] = qi + kQImageBytes;
     const char *pdl = getenv("B200Q_NO_PDL");
     c->pdl = !(pdl && pdl[0] == '1');
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return fail(e, "init");
@@ -613,6 +715,7 @@ void b200q_destroy(b200q_ctx *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->comm && g_nccl.comm_destroy) g_nccl.comm_destroy(c->comm);
     cudaFree(c->warena);
+    cudaFree(c->qimg[0]);
     cudaFree(c->act);
     cudaFree(c->state);
     cudaFree(c->kv);

@@ -81,10 +81,21 @@ __device__ __forceinline__ void issue_stage(const GemvArgs &a, const TileIt &it,
 
 // Result writer for one output row: SwiGLU silu(g) * u (silu_mul_f), residual add (add_mul_f), conv1d + SiLU +
 // state shift (conv_chan, silu_f), else the row value (fpga/src/gemvqc16.cpp:203-316).
-__device__ __forceinline__ void write_row(const GemvMemberArgs &M, unsigned gr, float v, float g) {
+// The value the writer stores for row gr (every epilogue but CONV).
+__device__ __forceinline__ float row_value(const GemvMemberArgs &M, unsigned gr, float v, float g,
+                                           const float *res_pre = nullptr) {
     switch (M.epi) {
-    case EpiSwigluU: M.y[gr] = fmul(silu_f32(g), v); break;
-    case EpiAdd: M.y[gr] = fadd(v, M.res[gr]); break;
+    case EpiSwigluU: return fmul(silu_f32(g), v);
+    case EpiAdd: return fadd(v, res_pre ? *res_pre : M.res[gr]);
+    default: return v;
+    }
+}
+
+__device__ __forceinline__ void write_row(const GemvMemberArgs &M, unsigned gr, float v, float g,
+                                          const float *res_pre = nullptr) {
+    switch (M.epi) {
+    case EpiSwigluU: M.y[gr] = row_value(M, gr, v, g); break;
+    case EpiAdd: M.y[gr] = row_value(M, gr, v, g, res_pre); break;
     case EpiConv: {
         const float s0 = M.cs[3 * gr], s1 = M.cs[3 * gr + 1], s2 = M.cs[3 * gr + 2];
         float sum = 0.0f;
@@ -256,27 +267,42 @@ __device__ __forceinline__ bool compute_acquire(const PassSmem &P, unsigned seq,
     return ok;
 }
 
-// x into shared memory (coalesced), then quantized by warps: threads of warps 1.. (kXThreads of them).
-__device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, const XImage &X, unsigned act) {
-    const unsigned t = threadIdx.x - 32, warp = t / 32, lane = t % 32, nw = kXThreads / 32;
+template <unsigned NT>
+__device__ __forceinline__ void x_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+
+// Index of element e (0..31) of 32-block b in the x image: contiguous 32-byte blocks, or (split) the first 16
+// bytes of every block in one run and the second 16 bytes in another, so that lanes reading consecutive blocks'
+// 16-byte halves hit consecutive banks.
+template <bool SPLIT>
+__device__ __forceinline__ unsigned xq_index(unsigned b, unsigned e, unsigned n) {
+    return SPLIT ? (e / 16) * (n / 2) + b * 16 + (e & 15) : b * 32 + e;
+}
+
+// x into shared memory (coalesced), then quantized by warps: NT threads from thread OFF on, barrier 1 among them.
+template <unsigned NT, unsigned OFF, bool SPLIT>
+__device__ __forceinline__ void prepare_x_t(const GemvArgs &a, float *xraw, float *wraw_buf, const XImage &X,
+                                            unsigned act) {
+    const unsigned t = threadIdx.x - OFF, warp = t / 32, lane = t % 32, nw = NT / 32;
     const unsigned n = a.cols;
     if (a.xq) {
-        for (unsigned i = t; i < n / 16; i += kXThreads)
-            reinterpret_cast<uint4 *>(X.q)[i] = reinterpret_cast<const uint4 *>(a.xq)[i];
+        for (unsigned i = t; i < n / 16; i += NT) {
+            const unsigned dst = SPLIT ? (i & 1u) * (n / 32) + i / 2 : i;
+            reinterpret_cast<uint4 *>(X.q)[dst] = reinterpret_cast<const uint4 *>(a.xq)[i];
+        }
         const unsigned nd = act == 2 ? n / 256 : n / 32, nb = act == 2 ? n / 16 : n / 32;
-        for (unsigned i = t; i < nd; i += kXThreads) {
+        for (unsigned i = t; i < nd; i += NT) {
             X.d[i] = a.xd[i];
             if (act == 1) X.s[i] = a.xs[i];
         }
-        for (unsigned i = t; i < nb; i += kXThreads) X.b[i] = a.xb[i];
-        named_sync_x();
+        for (unsigned i = t; i < nb; i += NT) X.b[i] = a.xb[i];
+        x_sync<NT>();
         return;
     }
     const bool norm = (a.norm_mode & 8u) != 0, weighted = (a.norm_mode & 2u) == 0;
     const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
-    float4 *xr4 = reinterpret_cast<float4 *>(P.xraw);
+    float4 *xr4 = reinterpret_cast<float4 *>(xraw);
     double acc = 0.0;
-    for (unsigned i = t; i < n / 4; i += kXThreads) {
+    for (unsigned i = t; i < n / 4; i += NT) {
         const float4 v = x4[i];
         xr4[i] = v;
         if (norm) {
@@ -286,16 +312,17 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
             acc += double(fmul(v.w, v.w));
         }
     }
-    if (norm && weighted && P.wraw) {
+    float *wraw = (norm && weighted) ? wraw_buf : nullptr;
+    if (wraw) {
         const float4 *w4 = reinterpret_cast<const float4 *>(a.norm_w);
-        for (unsigned i = t; i < n / 4; i += kXThreads) reinterpret_cast<float4 *>(P.wraw)[i] = w4[i];
+        for (unsigned i = t; i < n / 4; i += NT) reinterpret_cast<float4 *>(wraw)[i] = w4[i];
     }
     float scale = 1.0f;
     if (norm) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) X.red[warp] = acc;
-        named_sync_x();
+        x_sync<NT>();
         if (t == 0) {
             double sum = 0.0;
             for (unsigned w = 0; w < nw; ++w) sum += X.red[w];
@@ -305,9 +332,9 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
             *X.scale = sc;
         }
     }
-    named_sync_x();
+    x_sync<NT>();
     if (norm) scale = *X.scale;
-    const float *wn = P.wraw ? P.wraw : a.norm_w;
+    const float *wn = wraw ? wraw : a.norm_w;
     if (act == 2) {
         for (unsigned sb = warp; sb < n / 256; sb += nw) {
             float v[8];
@@ -316,7 +343,7 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const unsigned e = sb * 256 + lane + 32 * k;
-                v[k] = norm_value(P.xraw, e, norm, scale, wn, weighted);
+                v[k] = norm_value(xraw, e, norm, scale, wn, weighted);
                 const float av = fabsf(v[k]);
                 if (av > amax) { amax = av; mx = v[k]; idx = int(lane + 32 * k); }
             }
@@ -351,7 +378,7 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
         // (8j + e + b) % 32, e < 8, so the 32 lanes of a warp (8 blocks) read 32 different banks; amax and the sum
         // over the quad by shuffles. The loop runs warp-uniformly (whole warps per round).
         const unsigned nq = n / 32 * 4;
-        for (unsigned wbase = t & ~31u; wbase < nq; wbase += kXThreads) {
+        for (unsigned wbase = t & ~31u; wbase < nq; wbase += NT) {
             const unsigned item = wbase + (t & 31u), b = item / 4, j = item & 3u;
             const bool live = item < nq;
             float v[8];
@@ -359,7 +386,7 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const unsigned off = (8u * j + unsigned(e) + b) & 31u;
-                v[e] = live ? norm_value(P.xraw, b * 32 + off, norm, scale, wn, weighted) : 0.0f;
+                v[e] = live ? norm_value(xraw, b * 32 + off, norm, scale, wn, weighted) : 0.0f;
                 amax = fmaxf(amax, fabsf(v[e]));
             }
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
@@ -372,7 +399,7 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
                 const int q = int(roundf(fmul(v[e], id)));
                 sum += q;
                 const unsigned off = (8u * j + unsigned(e) + b) & 31u;
-                if (live) X.q[b * 32 + off] = int8_t(q);
+                if (live) X.q[xq_index<SPLIT>(b, off, n)] = int8_t(q);
             }
             sum += __shfl_xor_sync(0xffffffffu, sum, 1);
             sum += __shfl_xor_sync(0xffffffffu, sum, 2);
@@ -383,7 +410,13 @@ __device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, 
             }
         }
     }
-    named_sync_x();
+    x_sync<NT>();
+}
+
+
+// The K-quant pass: fold + compute warps (threads 32..319) prepare x.
+__device__ __forceinline__ void prepare_x(const GemvArgs &a, const PassSmem &P, const XImage &X, unsigned act) {
+    prepare_x_t<kXThreads, 32, false>(a, P.xraw, P.wraw, X, act);
 }
 
 }  // namespace b200q

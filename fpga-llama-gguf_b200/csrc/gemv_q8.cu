@@ -2,201 +2,588 @@
 // one shared x in one launch, with the SwiGLU / residual ADD / causal CONV epilogues of the reference's result
 // writer (fpga/src/gemvqc16.cpp:203-316).
 //
-// Per CTA (persistent over its row tiles):
-//   1. thread 0 starts bulk copies of the first weight tiles into a ring of shared-memory stages — before the
-//      wait on the previous kernel (programmatic dependent launch), since weights never change within a list;
-//   2. after the wait, x is quantized into shared memory (optionally through the deferred RMSNORM);
-//   3. per stage: every thread takes (row, block) items of the tile: an exact integer block dot with dp4a and
-//      the block term float(sumi) * (d_w * d_x) (two IEEE roundings, as the CPU path); then one thread per row adds
-//      the row's terms in block order into its running sum (sum += term), reproducing the CPU's FP32 sum bit for
-//      bit (gemvq_ref.h:248-262); after the row's last tile it applies the epilogue and writes y.
+// A CTA takes one panel at a time (P rows x all blocks of one matrix, or of a SwiGLU g/u pair; one wave of CTAs
+// covers the pass when it fits) and splits the panel's steps over its 8 warps (warp w: steps w, w + 8, ...):
+//   1. before the wait on the previous kernel (programmatic dependent launch) the warps ask L2 for the CTA's
+//      first panels (bulk prefetch; weights never change within a list), so HBM streams while x is prepared;
+//   2. the CTA quantizes x into shared memory once (optionally through the deferred RMSNORM);
+//   3. per step (one 32-unit tile: P rows x 32 / P blocks, lane = unit) each lane loads its unit's 16-byte quant
+//      words and scale with coalesced 128-bit loads, several steps ahead in registers, forms the exact integer
+//      block dot (dp4a) and the block term float(sumi) * (d_w * d_x) (two IEEE roundings, as the CPU path), and
+//      stores the term to the panel's term buffer in shared memory (one 128-byte row per step);
+//   4. after the panel, one lane per row adds the row's terms in block order, reproducing the CPU's FP32 sum bit
+//      for bit (gemvq_ref.h:248-262), applies the epilogue and writes y;
+//   5. a CTA out of panels asks L2 for its share of the next GEMV pass's weights.
 //
 // Roofline: HBM bandwidth. Bytes per row: cols/32 * (16 + 2) for Q4_0, * (32 + 2) for Q8_0, * (16 + 4) for Q4_1.
+#include <algorithm>
+
 #include "gemv_common.cuh"
 #include "launch.h"
 
 namespace b200q {
 
-__host__ __device__ inline unsigned res_stride(unsigned C) { return C + ((36u - C % 32u) % 32u); }
+constexpr unsigned kPanelWarps = 8, kPanelThreads = 32 * kPanelWarps;
 
-// One tile (R rows x C blocks, C a power of two <= 32) by the 8 compute warps: a warp instruction covers 32 / C
-// rows x C blocks (lane = row sub-index * C + block), so a lane's x block (and its scale and sum) is loaded once per
-// tile; the warp walks its row groups two at a time. Per item: exact integer block dot (dp4a), FP32 term
-// float(sumi) * (d_w * d_x), stored to the result buffer (row stride cs).
+// ---- one lane's share of one step ---------------------------------------------------------------------------------
 template <unsigned FMT>
-__device__ __forceinline__ void compute_tile(uint32_t s_tile, uint32_t qs_part, unsigned C, unsigned nr, unsigned kC,
-                                             uint32_t s_xq, uint32_t s_xd, uint32_t s_xs, uint32_t s_xb,
-                                             uint32_t s_res, unsigned cs, int32_t *dbg, size_t dbg_row0,
-                                             unsigned nb) {
-    constexpr unsigned QB = FMT == 8 ? 32 : 16;
-    constexpr unsigned DB = FMT == 3 ? 4 : 2;
-    const unsigned warp = threadIdx.x / 32 - 2, lane = threadIdx.x % 32;
-    const unsigned c = lane & (C - 1), rsub = lane / C, rows_per_group = 32 / C;
-    const unsigned groups = (nr + rows_per_group - 1) / rows_per_group;
-    const unsigned blk = kC + c;
-    const uint32_t s_dm = s_tile + qs_part;
-    // this lane's x block, for all rows of the tile
-    const uint4 x0 = lds128(s_xq + blk * 32), x1 = lds128(s_xq + blk * 32 + 16);
-    const float xd = ldsf(s_xd + blk * 4);
-    const int xcorr = FMT == 2 ? 8 * int(lds32(s_xb + blk * 4)) : 0;
-    const float xs = FMT == 3 ? ldsf(s_xs + blk * 4) : 0.0f;
-    auto item = [&](unsigned r) {
-        const unsigned i = r * C + c;
-        int d0 = 0, d1 = 0;
-        if (FMT == 8) {
-            const uint4 w0 = lds128(s_tile + i * QB), w1 = lds128(s_tile + i * QB + 16);
-            d0 = __dp4a(int(w0.x), int(x0.x), d0);
-            d1 = __dp4a(int(w1.x), int(x1.x), d1);
-            d0 = __dp4a(int(w0.y), int(x0.y), d0);
-            d1 = __dp4a(int(w1.y), int(x1.y), d1);
-            d0 = __dp4a(int(w0.z), int(x0.z), d0);
-            d1 = __dp4a(int(w1.z), int(x1.z), d1);
-            d0 = __dp4a(int(w0.w), int(x0.w), d0);
-            d1 = __dp4a(int(w1.w), int(x1.w), d1);
-        } else {
-            // byte j: low nibble = element j, high nibble = element j + 16
-            const uint4 wv = lds128(s_tile + i * QB);
-            const uint32_t m = 0x0F0F0F0Fu;
-            d0 = __dp4a(int(wv.x & m), int(x0.x), d0);
-            d1 = __dp4a(int((wv.x >> 4) & m), int(x1.x), d1);
-            d0 = __dp4a(int(wv.y & m), int(x0.y), d0);
-            d1 = __dp4a(int((wv.y >> 4) & m), int(x1.y), d1);
-            d0 = __dp4a(int(wv.z & m), int(x0.z), d0);
-            d1 = __dp4a(int((wv.z >> 4) & m), int(x1.z), d1);
-            d0 = __dp4a(int(wv.w & m), int(x0.w), d0);
-            d1 = __dp4a(int((wv.w >> 4) & m), int(x1.w), d1);
+struct Step {
+    uint4 q0, q1;  // quant words (q1: Q8_0 only)
+    uint32_t d;    // FP16 d (Q4_1: d | m << 16)
+};
+
+__device__ __forceinline__ uint4 ldw128(const uint8_t *p, uint64_t pol) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldw32(const uint8_t *p, uint64_t pol) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldw16(const uint8_t *p, uint64_t pol) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u16 %0, [%1], %2;" : "=h"(v) : "l"(p), "l"(pol));
+    return v;
+}
+
+// Step tile layout (layout.h): quants at lane * 16 (Q8_0: + 512 for the second half), scales at 512 (Q8_0: 1024).
+template <unsigned FMT>
+__device__ __forceinline__ void load_step(Step<FMT> &v, const uint8_t *tile, unsigned lane, uint64_t pol) {
+    v.q0 = ldw128(tile + lane * 16, pol);
+    if (FMT == 8) {
+        v.q1 = ldw128(tile + 512 + lane * 16, pol);
+        v.d = ldw16(tile + 1024 + lane * 2, pol);
+    } else if (FMT == 2) {
+        v.d = ldw16(tile + 512 + lane * 2, pol);
+    } else {
+        v.d = ldw32(tile + 512 + lane * 4, pol);
+    }
+}
+
+// x block of a lane: the split image (first 16 quant bytes of block b at q0 + 16 b, the second 16 at q1 + 16 b)
+// and the block's meta word {d, s (Q8_1), sum of q, 0} at meta + 16 b.
+struct XBlock {
+    uint4 q0, q1;
+    float d, s;
+    int bsum;
+};
+
+struct XSmem {
+    const uint4 *q0, *q1, *meta;
+};
+
+// Plain C++ shared-memory loads (not volatile asm): the compiler may issue them early and overlap them.
+__device__ __forceinline__ XBlock load_xblock(const XSmem &xs, unsigned b) {
+    XBlock x;
+    x.q0 = xs.q0[b];
+    x.q1 = xs.q1[b];
+    const uint4 m = xs.meta[b];
+    x.d = __uint_as_float(m.x);
+    x.s = __uint_as_float(m.y);
+    x.bsum = int(m.z);
+    return x;
+}
+
+// Exact integer block dot and the FP32 block term (the CPU path's arithmetic, gemvq_ref.h:215-262).
+template <unsigned FMT>
+__device__ __forceinline__ float block_term(const Step<FMT> &w, const XBlock &x, int &sumi) {
+    int d0 = 0, d1 = 0;
+    if (FMT == 8) {
+        d0 = __dp4a(int(w.q0.x), int(x.q0.x), d0);
+        d1 = __dp4a(int(w.q1.x), int(x.q1.x), d1);
+        d0 = __dp4a(int(w.q0.y), int(x.q0.y), d0);
+        d1 = __dp4a(int(w.q1.y), int(x.q1.y), d1);
+        d0 = __dp4a(int(w.q0.z), int(x.q0.z), d0);
+        d1 = __dp4a(int(w.q1.z), int(x.q1.z), d1);
+        d0 = __dp4a(int(w.q0.w), int(x.q0.w), d0);
+        d1 = __dp4a(int(w.q1.w), int(x.q1.w), d1);
+    } else {
+        // byte j: low nibble = element j, high nibble = element j + 16
+        const uint32_t m = 0x0F0F0F0Fu;
+        d0 = __dp4a(int(w.q0.x & m), int(x.q0.x), d0);
+        d1 = __dp4a(int((w.q0.x >> 4) & m), int(x.q1.x), d1);
+        d0 = __dp4a(int(w.q0.y & m), int(x.q0.y), d0);
+        d1 = __dp4a(int((w.q0.y >> 4) & m), int(x.q1.y), d1);
+        d0 = __dp4a(int(w.q0.z & m), int(x.q0.z), d0);
+        d1 = __dp4a(int((w.q0.z >> 4) & m), int(x.q1.z), d1);
+        d0 = __dp4a(int(w.q0.w & m), int(x.q0.w), d0);
+        d1 = __dp4a(int((w.q0.w >> 4) & m), int(x.q1.w), d1);
+    }
+    sumi = d0 + d1 - (FMT == 2 ? 8 * x.bsum : 0);  // Q4_0: sum (w - 8) q = sum w q - 8 sum q
+    if (FMT == 3) {
+        // (d_w * d_8) * sumi + m_w * s_8 (gemvq_ref.h:221-223)
+        const float dw = half_bits_to_float(uint16_t(w.d & 0xffffu)), mw = half_bits_to_float(uint16_t(w.d >> 16));
+        return fadd(fmul(fmul(dw, x.d), float(sumi)), fmul(mw, x.s));
+    }
+    return fmul(float(sumi), fmul(half_bits_to_float(uint16_t(w.d)), x.d));
+}
+
+// L2 prefetch of [p, p + bytes) (bulk, 16-byte multiples; no data returns to the SM).
+__device__ __forceinline__ void l2_prefetch(const uint8_t *p, unsigned long long bytes) {
+    while (bytes) {
+        const unsigned n = bytes > (1u << 20) ? (1u << 20) : unsigned(bytes);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
+        p += n;
+        bytes -= n;
+    }
+}
+
+// Steps [from, kc) of an item into L2, in step order (a pair: its g and u panels in alternating 16 KB pieces), so
+// the earlier steps arrive first. One thread.
+__device__ __forceinline__ void prefetch_panel(const GemvArgs &a, unsigned item, unsigned from) {
+    if (item >= a.item_start[a.n_units]) return;
+    const unsigned u = unit_of(a, item), pnl = item - a.item_start[u];
+    const int pair = a.unit_pair[u];
+    const MatrixView &g = unit_member(a, u).w;
+    const unsigned ga = from * g.tile_bytes, gb = g.kc * g.tile_bytes;
+    const uint8_t *pg = g.base + size_t(pnl) * gb;
+    const MatrixView &v = pair >= 0 ? a.m[pair].w : g;
+    const unsigned va = pair >= 0 ? from * v.tile_bytes : 0u, vb = pair >= 0 ? v.kc * v.tile_bytes : 0u;
+    const uint8_t *pv = v.base + size_t(pnl) * vb;
+    constexpr unsigned kPiece = 16384;
+    for (unsigned k = 0; ga + k < gb || va + k < vb; k += kPiece) {
+        if (ga + k < gb) l2_prefetch(pg + ga + k, min(kPiece, gb - ga - k));
+        if (va + k < vb) l2_prefetch(pv + va + k, min(kPiece, vb - va - k));
+    }
+}
+
+// ---- x preparation, split over a cluster of kXCluster CTAs ---------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_smem(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ float4 ldg_act4(const float *p) {
+    return *reinterpret_cast<const float4 *>(p);
+}
+
+// Shared-memory image of the quantized x of a Q8 pass: the RMSNORM partial sums, the quants as two runs of
+// 16-byte halves, one meta word {d, s, sum of q, 0} per 32-block.
+struct QImage {
+    double *red;
+    uint8_t *q;
+    uint4 *meta;
+};
+__host__ __device__ inline size_t qimage_bytes(unsigned cols) { return 256 + size_t(cols) + size_t(cols / 32) * 16; }
+__device__ __forceinline__ QImage carve_qimage(unsigned char *p, unsigned cols) {
+    QImage X;
+    X.red = reinterpret_cast<double *>(p);
+    X.q = p + 256;
+    X.meta = reinterpret_cast<uint4 *>(p + 256 + cols);
+    return X;
+}
+
+// Q8_0 / Q8_1 image of x (optionally through the deferred RMSNORM) in the shared memory of every CTA of the
+// cluster: CTA `rank` quantizes the blocks [rank * per, rank * per + per) (per <= 128), two lanes per block (16
+// values each, straight from global memory; lane h of the pair owns the block's h-th 16 quant bytes) and stores
+// each block into all kXCluster images (distributed shared memory, 16-byte stores). The RMSNORM sum of squares
+// over the whole x: every CTA computes it in the same fixed order (per thread, then a shuffle tree, then the warps
+// in order), so all CTAs get the same scale. Same arithmetic as the reference CPU quantizer (quant.cuh,
+// gemvq_ref.h:196-245). Ends with a cluster barrier: afterwards every image is complete.
+constexpr unsigned kXCluster = 4;
+static_assert(kMaxQuantCols / 32 / kXCluster <= kPanelThreads / 2, "one round of two lanes per block");
+template <class Hook>
+__device__ __forceinline__ void prepare_x_cluster(const GemvArgs &a, const QImage &X, unsigned act, Hook after_loads) {
+    const unsigned n = a.cols, nb = n / 32, rank = cluster_rank();
+    const unsigned per = (nb + kXCluster - 1) / kXCluster, b0 = rank * per, b1 = min(nb, b0 + per);
+    const bool norm = (a.norm_mode & 8u) != 0, weighted = (a.norm_mode & 2u) == 0;
+    const unsigned t = threadIdx.x, h = t & 1u, b = b0 + (t >> 1), warp = t / 32, lane = t % 32;
+    const bool live = b < b1;
+    float v[16], w16[16];
+#pragma unroll
+    for (unsigned i = 0; i < 4; ++i) {
+        float4 xv = make_float4(0.f, 0.f, 0.f, 0.f), wv = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (live) {
+            xv = ldg_act4(a.x + b * 32 + h * 16 + i * 4);
+            if (norm && weighted) wv = ldg_act4(a.norm_w + b * 32 + h * 16 + i * 4);
         }
-        const int sumi = d0 + d1 - xcorr;  // Q4_0: sum (w - 8) q = sum w q - 8 sum q
-        float term;
-        if (FMT == 3) {
-            // (d_w * d_8) * sumi + m_w * s_8 (gemvq_ref.h:221-223)
-            const uint32_t dmv = lds32(s_dm + i * 4);
-            const float dw = half_bits_to_float(uint16_t(dmv & 0xffffu)), mw = half_bits_to_float(uint16_t(dmv >> 16));
-            term = fadd(fmul(fmul(dw, xd), float(sumi)), fmul(mw, xs));
-        } else {
-            const float dw = half_bits_to_float(lds16(s_dm + i * DB));
-            term = fmul(float(sumi), fmul(dw, xd));
+        v[4 * i] = xv.x, v[4 * i + 1] = xv.y, v[4 * i + 2] = xv.z, v[4 * i + 3] = xv.w;
+        w16[4 * i] = wv.x, w16[4 * i + 1] = wv.y, w16[4 * i + 2] = wv.z, w16[4 * i + 3] = wv.w;
+    }
+    // the whole x for the RMSNORM sum: the first kNormPre float4 per thread are requested before the hook
+    constexpr unsigned kNormPre = 2;
+    float4 nv[kNormPre];
+#pragma unroll
+    for (unsigned k = 0; k < kNormPre; ++k) {
+        const unsigned i = t + k * kPanelThreads;
+        nv[k] = norm && i < n / 4 ? ldg_act4(a.x + i * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    after_loads();
+    float scale = 1.0f;
+    if (norm) {
+        double acc = 0.0;
+#pragma unroll
+        for (unsigned k = 0; k < kNormPre; ++k) {
+            acc += double(fmul(nv[k].x, nv[k].x));
+            acc += double(fmul(nv[k].y, nv[k].y));
+            acc += double(fmul(nv[k].z, nv[k].z));
+            acc += double(fmul(nv[k].w, nv[k].w));
         }
-        stsf(s_res + (r * cs + c) * 4, term);
-        if (dbg) dbg[(dbg_row0 + r) * nb + blk] = sumi;
-    };
-    unsigned g = warp;
-    for (; g + kComputeWarps < groups; g += 2 * kComputeWarps) {
-        const unsigned ra = g * rows_per_group + rsub, rb = (g + kComputeWarps) * rows_per_group + rsub;
-        if (ra < nr) item(ra);
-        if (rb < nr) item(rb);
+        for (unsigned i = t + kNormPre * kPanelThreads; i < n / 4; i += kPanelThreads) {
+            const float4 u = ldg_act4(a.x + i * 4);
+            acc += double(fmul(u.x, u.x));
+            acc += double(fmul(u.y, u.y));
+            acc += double(fmul(u.z, u.z));
+            acc += double(fmul(u.w, u.w));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) X.red[warp] = acc;
+        __syncthreads();
+        double sum = 0.0;
+        for (unsigned w = 0; w < kPanelWarps; ++w) sum += X.red[w];
+        if (a.norm_mode & 1u) scale = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sum)), a.norm_eps));
+        else scale = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(sum, double(n))), a.norm_eps)));
     }
-    if (g < groups) {
-        const unsigned ra = g * rows_per_group + rsub;
-        if (ra < nr) item(ra);
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        if (norm) v[e] = weighted ? fmul(fmul(v[e], scale), w16[e]) : fmul(v[e], scale);
+        amax = fmaxf(amax, fabsf(v[e]));
     }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float s = fdiv(amax, 127.0f);
+    const float id = s != 0.0f ? fdiv(1.0f, s) : 0.0f;
+    int sum = 0;
+    uint32_t word[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        const int q = int(roundf(fmul(v[e], id)));
+        sum += q;
+        word[e / 4] |= uint32_t(q & 0xff) << (8 * (e % 4));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    if (live) {
+        const uint32_t qa = smem_addr(X.q) + h * (n / 2) + b * 16, ma = smem_addr(X.meta) + b * 16;
+        const uint4 qw = make_uint4(word[0], word[1], word[2], word[3]);
+        const float dh = half_bits_to_float(float_to_half_bits(s));
+        const float sh = act == 1 ? half_bits_to_float(float_to_half_bits(fmul(float(sum), s))) : 0.0f;
+        const uint4 m = make_uint4(__float_as_uint(dh), __float_as_uint(sh), uint32_t(sum), 0u);
+#pragma unroll
+        for (unsigned k = 0; k < kXCluster; ++k) {
+            st_cluster_v4(peer_smem(qa, k), qw);
+            if (h == 0) st_cluster_v4(peer_smem(ma, k), m);
+        }
+    }
+    cluster_sync();
 }
 
-__device__ __forceinline__ void compute_tile_any(const uint8_t *tile, const MatrixView &w, unsigned nr, unsigned k,
-                                                 const XImage &X, float *res, unsigned cs, int32_t *dbg, unsigned r0) {
-    const uint32_t st = smem_addr(tile), sq = smem_addr(X.q), sd = smem_addr(X.d), ss = smem_addr(X.s);
-    const uint32_t sb = smem_addr(X.b), sr = smem_addr(res);
-    const unsigned C = w.ct, nb = w.kc * w.ct;
-    const size_t drow = size_t(w.row0) + r0;
-    switch (w.format) {
-    case 2: compute_tile<2>(st, w.qs_part, C, nr, k * C, sq, sd, ss, sb, sr, cs, dbg, drow, nb); break;
-    case 8: compute_tile<8>(st, w.qs_part, C, nr, k * C, sq, sd, ss, sb, sr, cs, dbg, drow, nb); break;
-    default: compute_tile<3>(st, w.qs_part, C, nr, k * C, sq, sd, ss, sb, sr, cs, dbg, drow, nb); break;
-    }
-}
-
-// sum += term over one tile's C terms, in block order (row at shared address a, 16-byte aligned)
-__device__ __forceinline__ float fold_terms(float s, uint32_t a, unsigned C) {
-    unsigned c = 0;
-    for (; c + 4 <= C; c += 4) {
-        const uint4 v = lds128(a + c * 4);
-        s = fadd(s, __uint_as_float(v.x));
-        s = fadd(s, __uint_as_float(v.y));
-        s = fadd(s, __uint_as_float(v.z));
-        s = fadd(s, __uint_as_float(v.w));
-    }
-    for (; c < C; ++c) s = fadd(s, ldsf(a + c * 4));
-    return s;
-}
-
-__global__ void __launch_bounds__(kPassThreads, 2) gemv_q8_kernel(const __grid_constant__ GemvArgs a) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    const PassSmem P = carve_pass(smem, a);
-    const XImage X = carve_ximage(P.ximg, a.cols);
-    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    if (threadIdx.x == 0) init_pass_barriers(a, P);
+// Copy of a pre-quantized x (scratch of a separate quantize launch) into the image.
+__device__ __forceinline__ void load_xq(const GemvArgs &a, const QImage &X, unsigned act) {
+    const unsigned n = a.cols, nb = n / 32;
+    for (unsigned i = threadIdx.x; i < n / 16; i += kPanelThreads)
+        reinterpret_cast<uint4 *>(X.q)[(i & 1u) * (n / 32) + i / 2] = reinterpret_cast<const uint4 *>(a.xq)[i];
+    for (unsigned i = threadIdx.x; i < nb; i += kPanelThreads)
+        X.meta[i] = make_uint4(__float_as_uint(a.xd[i]), act == 1 ? __float_as_uint(a.xs[i]) : 0u, uint32_t(a.xb[i]), 0u);
     __syncthreads();
-    pdl_launch_dependents();  // the next kernel may start its own weight copies as SMs free up
-    if (warp == 0) {
-        if (lane == 0) producer_loop(a, P);
-        return;
+}
+
+// Copy of an x image written by the previous pass (same layout as the shared-memory image: quants, then meta).
+__device__ __forceinline__ void load_qimage(const GemvArgs &a, const QImage &X) {
+    const unsigned n = a.cols, words = (n + n / 32 * 16) / 16;
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.qin);
+    uint4 *dst = reinterpret_cast<uint4 *>(X.q);
+    for (unsigned i = threadIdx.x; i < words; i += kPanelThreads) dst[i] = src[i];
+    __syncthreads();
+}
+
+// Image block b (32 values, lane r holding value r) of a next pass's x, written by a warp: the reference's Q8_0 /
+// Q8_1 arithmetic (gemvq_ref.h:196-245), the same as the x preparation. n: the values of the whole x.
+__device__ __forceinline__ void write_image_block(uint8_t *img, unsigned n, unsigned b, float y, unsigned lane,
+                                                  unsigned act) {
+    const float amax = warp_max(fabsf(y));
+    const float s = fdiv(amax, 127.0f);
+    const float id = s != 0.0f ? fdiv(1.0f, s) : 0.0f;
+    const int q = int(roundf(fmul(y, id)));
+    const int sum = warp_sum_i(q);
+    const uint32_t qb = uint32_t(q & 0xff);
+    const uint32_t w = qb | (__shfl_down_sync(0xffffffffu, qb, 1) << 8) | (__shfl_down_sync(0xffffffffu, qb, 2) << 16) |
+                       (__shfl_down_sync(0xffffffffu, qb, 3) << 24);
+    if ((lane & 3u) == 0) {  // bytes 4k .. 4k + 3: half k / 4, word k % 4
+        const unsigned k = lane / 4;
+        *reinterpret_cast<uint32_t *>(img + (k / 4) * (n / 2) + b * 16 + (k % 4) * 4) = w;
     }
-    pdl_wait();
-    prepare_x(a, P, X, a.m[0].w.format == 3 ? 1u : 0u);
-    TileIt it = tile_first(a);
-    unsigned seq = 0;
-    if (warp >= 2) {  // compute
-        while (tile_valid(a, it)) {
-            const unsigned s = seq % a.n_stages, b = seq % kNR;
-            const bool ok = compute_acquire(P, seq, a.n_stages);
-            if (!ok) {
-                fail_pass(a, P.abort);
-                break;
-            }
-            const GemvMemberArgs &M0 = unit_member(a, it.unit);
-            const int pair = a.unit_pair[it.unit];
-            const unsigned t = it.item - a.item_start[it.unit];
-            const unsigned R = M0.w.rt, cs = res_stride(M0.w.ct);
-            const unsigned r0 = t * R, nr = min(R, M0.w.rows - r0);
-            float *res = reinterpret_cast<float *>((b ? P.res[1] : P.res[0]));
-            const uint8_t *stage = P.stages + size_t(s) * a.stage_bytes;
-            compute_tile_any(stage, M0.w, nr, it.k, X, res, cs, a.dbg, r0);
-            if (pair >= 0)
-                compute_tile_any(stage + pair_offset(M0.w.tile_bytes), a.m[pair].w, nr, it.k, X, res + R * cs, cs,
-                                 nullptr, r0);
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&P.empty[s]);
-                mbar_arrive(&P.rfull[b]);
-            }
-            ++seq;
-            tile_next(a, it);
-        }
-        return;
+    if (lane == 0) {
+        const float dh = half_bits_to_float(float_to_half_bits(s));
+        const float sh = act == 1 ? half_bits_to_float(float_to_half_bits(fmul(float(sum), s))) : 0.0f;
+        *reinterpret_cast<uint4 *>(img + n + b * 16) =
+            make_uint4(__float_as_uint(dh), __float_as_uint(sh), uint32_t(sum), 0u);
     }
-    // fold (warp 1): lane r adds row r's terms in block order
-    float acc0 = 0.0f, acc1 = 0.0f;
-    while (tile_valid(a, it)) {
-        const unsigned b = seq % kNR;
-        if (!role_wait(&P.rfull[b], (seq / kNR) & 1u, P.abort)) {
-            fail_pass(a, P.abort);
-            break;
+}
+
+
+// ---- staged leading steps, compute, fold --------------------------------------------------------------------------
+// Bounded spin (kWaitLimitNs) on the completion of phase `parity` of `bar` (non-blocking test).
+__device__ __forceinline__ bool mbar_spin(uint64_t *bar, unsigned parity) {
+    const uint32_t a = smem_addr(bar);
+    unsigned long long start = 0;
+    for (unsigned i = 0;; ++i) {
+        uint32_t done;
+        asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(done)
+                     : "r"(a), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        if ((i & 1023u) == 1023u) {
+            const unsigned long long now = global_ns();
+            if (start == 0) start = now;
+            else if (now - start > kWaitLimitNs) return false;
         }
-        const GemvMemberArgs &M0 = unit_member(a, it.unit);
-        const int pair = a.unit_pair[it.unit];
-        const unsigned t = it.item - a.item_start[it.unit];
-        const unsigned R = M0.w.rt, C = M0.w.ct, cs = res_stride(C);
-        const unsigned r0 = t * R, nr = min(R, M0.w.rows - r0);
-        const uint32_t res = smem_addr((b ? P.res[1] : P.res[0]));
-        if (!a.dbg) {
-            const bool last = it.k + 1 == M0.w.kc;
-            if (lane < nr) {
-                acc0 = fold_terms(acc0, res + lane * cs * 4, C);
-                if (pair >= 0) acc1 = fold_terms(acc1, res + (R + lane) * cs * 4, C);
-                if (last) {
-                    const unsigned gr = M0.w.row0 + r0 + lane;
-                    if (pair >= 0) write_row(a.m[pair], gr, acc1, acc0);
-                    else write_row(M0, gr, acc0, 0.0f);
-                    acc0 = acc1 = 0.0f;
+    }
+}
+
+// Weights of the first steps of a CTA's first panel, staged in shared memory by one bulk copy (per matrix) issued
+// with the x loads: [A: k steps][B: k steps (pairs)].
+struct Staging {
+    const uint8_t *base;  // A's first staged step
+    unsigned k;           // staged steps (0: none)
+    uint32_t b_off;       // offset of B's part
+};
+
+template <unsigned FMT>
+__device__ __forceinline__ void load_step_smem(Step<FMT> &v, const uint8_t *tile, unsigned lane) {
+    v.q0 = reinterpret_cast<const uint4 *>(tile)[lane];
+    if (FMT == 8) {
+        v.q1 = reinterpret_cast<const uint4 *>(tile + 512)[lane];
+        v.d = reinterpret_cast<const uint16_t *>(tile + 1024)[lane];
+    } else if (FMT == 2) {
+        v.d = reinterpret_cast<const uint16_t *>(tile + 512)[lane];
+    } else {
+        v.d = reinterpret_cast<const uint32_t *>(tile + 512)[lane];
+    }
+}
+
+// Warp w: steps w, w + 8, ... of one panel, block terms into the term buffers (row s = step s, 32 floats). FA alone
+// (FB == 0) or the SwiGLU pair g (FA) / u (FB) over the same rows and steps. U steps in flight; staged steps come
+// from shared memory. False if the wait for the staged steps gave up.
+template <unsigned FA, unsigned FB, unsigned U>
+__device__ __forceinline__ bool compute_steps(const GemvArgs &a, const GemvMemberArgs &MA, const GemvMemberArgs &MB,
+                                              unsigned pnl, const XSmem &xs, unsigned warp, unsigned lane,
+                                              uint64_t pol, float *term_a, float *term_b, const Staging &stg,
+                                              uint64_t *stage_bar) {
+    const MatrixView &w = MA.w;
+    const unsigned J = w.ct, S = w.kc, nb = a.cols / 32;
+    const unsigned j = lane & (J - 1u), lrow = pnl * w.rt + lane / J;
+    const unsigned TA = w.tile_bytes, TB = FB ? MB.w.tile_bytes : 0u;
+    const uint8_t *ta = w.base + size_t(pnl) * S * TA;
+    const uint8_t *tb = FB ? MB.w.base + size_t(pnl) * S * TB : nullptr;
+    constexpr unsigned FB_ = FB ? FB : FA;
+    constexpr unsigned NW = kPanelWarps;
+    const unsigned n_my = S > warp ? (S - warp + NW - 1) / NW : 0u;
+    // this warp's steps i < i_g are staged (step warp + 8 i < k), the rest stream from global memory
+    const unsigned i_g = min(n_my, stg.k > warp ? (stg.k - warp + NW - 1) / NW : 0u);
+    int32_t *dbg = a.dbg && lrow < w.rows ? a.dbg + size_t(w.row0 + lrow) * nb : nullptr;
+    auto step = [&](const Step<FA> &ca, const Step<FB_> &cb, unsigned i) {
+        const unsigned s = warp + NW * i;
+        const unsigned b = s * J + j, bc = b < nb ? b : 0u;
+        const XBlock x = load_xblock(xs, bc);
+        int sumi;
+        term_a[s * 32 + lane] = block_term<FA>(ca, x, sumi);
+        if (dbg && b < nb) dbg[b] = sumi;
+        if (FB) {
+            int su;
+            term_b[s * 32 + lane] = block_term<FB_>(cb, x, su);
+        }
+    };
+    Step<FA> ba[U];
+    Step<FB_> bb[U];
+#pragma unroll
+    for (unsigned k = 0; k < U; ++k) {
+        const unsigned i = i_g + k;
+        if (i < n_my) {
+            load_step<FA>(ba[k], ta + (warp + NW * i) * TA, lane, pol);
+            if (FB) load_step<FB_>(bb[k], tb + (warp + NW * i) * TB, lane, pol);
+        }
+    }
+    const bool ok = i_g == 0 || mbar_spin(stage_bar, 0);
+    for (unsigned i = 0; ok && i < i_g; ++i) {
+        const unsigned s = warp + NW * i;
+        Step<FA> ca;
+        Step<FB_> cb;
+        load_step_smem<FA>(ca, stg.base + s * TA, lane);
+        if (FB) load_step_smem<FB_>(cb, stg.base + stg.b_off + s * TB, lane);
+        step(ca, cb, i);
+    }
+    for (unsigned i0 = i_g; ok && i0 < n_my; i0 += U) {
+#pragma unroll
+        for (unsigned k = 0; k < U; ++k) {
+            const unsigned i = i0 + k;
+            if (i < n_my) {
+                step(ba[k], bb[k], i);  // then the slot takes step i + U
+                if (i + U < n_my) {
+                    const unsigned s2 = warp + NW * (i + U);
+                    load_step<FA>(ba[k], ta + s2 * TA, lane, pol);
+                    if (FB) load_step<FB_>(bb[k], tb + s2 * TB, lane, pol);
                 }
             }
-            if (last) write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, lane);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&P.rempty[b]);
-        ++seq;
-        tile_next(a, it);
     }
+    return ok;
+}
+
+// Row r's terms in block order, sum += term from 0: the CPU's sequential FP32 sum (gemvq_ref.h:248-262). The term
+// of block k of row r sits at terms[32 (k / J) + r J + k % J]; 16 terms are loaded ahead of their 16 additions.
+__device__ __forceinline__ float fold_row(const float *terms, unsigned r, unsigned J, unsigned nb) {
+    const float *t = terms + r * J;
+    const unsigned jl = __ffs(J) - 1, jm = J - 1;
+    float acc = 0.0f;
+    unsigned k = 0;
+#pragma unroll 2
+    for (; k + 16 <= nb; k += 16) {
+        float v[16];
+#pragma unroll
+        for (unsigned e = 0; e < 16; ++e) {
+            const unsigned kk = k + e;
+            v[e] = t[((kk >> jl) << 5) + (kk & jm)];
+        }
+#pragma unroll
+        for (unsigned e = 0; e < 16; ++e) acc = fadd(acc, v[e]);
+    }
+    for (; k < nb; ++k) acc = fadd(acc, t[((k >> jl) << 5) + (k & jm)]);
+    return acc;
+}
+
+// One launch serves the units of one format combination: FA alone (FB == 0) or SwiGLU pairs FA / FB. Clusters
+// of kXCluster CTAs share the x preparation.
+//   shared memory: [x image][terms A][terms B (pairs)][staging mbarrier, u sums][staged steps]
+template <unsigned FA, unsigned FB, unsigned U>
+__global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThreads, 3)
+    gemv_q8_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char *p = smem;
+    const QImage X = carve_qimage(p, a.cols);
+    p += align128(qimage_bytes(a.cols));
+    float *term_a = reinterpret_cast<float *>(p), *term_b = reinterpret_cast<float *>(p + (FB ? a.term_bytes : 0u));
+    p += (FB ? 2u : 1u) * a.term_bytes;
+    uint64_t *stage_bar = reinterpret_cast<uint64_t *>(p);
+    float *usum = reinterpret_cast<float *>(p + 128);  // 32 floats
+    p += 256;
+    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const unsigned total = a.item_start[a.n_units];
+    if (threadIdx.x == 0) {
+        mbar_init(stage_bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    // the first steps of the first panel into shared memory: one bulk copy per matrix, issued once the x loads are
+    // on their way (so they are not queued behind the copies)
+    Staging stg{p, 0u, 0u};
+    unsigned u0 = 0, pnl0 = 0;
+    if (blockIdx.x < total && a.n_stages) {
+        u0 = unit_of(a, blockIdx.x);
+        pnl0 = blockIdx.x - a.item_start[u0];
+        const MatrixView &g = unit_member(a, u0).w;
+        stg.k = min(a.n_stages, g.kc);
+        stg.b_off = stg.k * g.tile_bytes;
+    }
+    auto issue_staging = [&]() {
+        if (threadIdx.x != 0 || stg.k == 0) return;
+        const uint64_t pol = evict_first_policy();
+        const MatrixView &g = unit_member(a, u0).w;
+        const MatrixView *v = FB ? &a.m[a.unit_pair[u0]].w : nullptr;
+        const unsigned bytes_b = v ? stg.k * v->tile_bytes : 0u;
+        mbar_expect_tx(stage_bar, stg.b_off + bytes_b);
+        bulk_copy(p, g.base + size_t(pnl0) * g.kc * g.tile_bytes, stg.b_off, stage_bar, pol);
+        if (v) bulk_copy(p + stg.b_off, v->base + size_t(pnl0) * v->kc * v->tile_bytes, bytes_b, stage_bar, pol);
+    };
+    pdl_launch_dependents();  // the next kernel may start as SMs free up
+    pdl_wait();
+    if (a.qin) {
+        issue_staging();
+        load_qimage(a, X);
+    } else if (a.xq) {
+        issue_staging();
+        load_xq(a, X, FA == 3 ? 1u : 0u);
+    } else {
+        prepare_x_cluster(a, X, FA == 3 ? 1u : 0u, issue_staging);
+    }
+    // the rest of the first panel (and the next one) into L2, in step order
+    if (threadIdx.x == 0 && blockIdx.x < total) prefetch_panel(a, blockIdx.x, stg.k);
+    if (threadIdx.x == 32) prefetch_panel(a, blockIdx.x + gridDim.x, 0);
+    const unsigned n = a.cols, nb = n / 32;
+    const XSmem xs{reinterpret_cast<const uint4 *>(X.q), reinterpret_cast<const uint4 *>(X.q + n / 2), X.meta};
+    const uint64_t pol = evict_first_policy();
+    bool failed = false;
+    unsigned np = 0;
+    for (unsigned it = blockIdx.x; it < total; it += gridDim.x, ++np) {
+        if (threadIdx.x == 0 && np) prefetch_panel(a, it + gridDim.x, 0);
+        const unsigned u = unit_of(a, it), pnl = it - a.item_start[u];
+        const GemvMemberArgs &MA = unit_member(a, u);
+        const GemvMemberArgs &MB = FB ? a.m[a.unit_pair[u]] : MA;
+        const MatrixView &w = MA.w;
+        const unsigned P = w.rt, lrow = pnl * P + lane;
+        const bool mine = lane < P && lrow < w.rows;
+        const GemvMemberArgs &OUT = FB ? MB : MA;
+        float res = 0.0f;  // residual of the row, loaded before the steps (off the tail)
+        if (warp == 0 && mine && OUT.epi == EpiAdd && !a.dbg) res = OUT.res[w.row0 + lrow];
+        const Staging none{nullptr, 0u, 0u};
+        if (!compute_steps<FA, FB, U>(a, MA, MB, pnl, xs, warp, lane, pol, term_a, term_b, np == 0 ? stg : none,
+                                      stage_bar)) {
+            failed = true;
+            if (lane == 0 && a.err) atomicExch(a.err, 1u);
+        }
+        if (__syncthreads_or(failed)) break;
+        if (!a.dbg) {
+            if (FB && warp == 1 && lane < P) usum[lane] = fold_row(term_b, lane, w.ct, nb);
+            if (FB) __syncthreads();
+            if (warp == 0) {
+                const unsigned out_member = FB ? unsigned(a.unit_pair[u]) : a.unit_member[u];
+                if (a.qout && out_member == a.qout_member && P == 32) {
+                    // this panel is block pnl of the next pass's x: every lane holds a row (rows % 32 == 0)
+                    const float acc = fold_row(term_a, lane, w.ct, nb);
+                    const float val = FB ? row_value(MB, w.row0 + lrow, usum[lane], acc)
+                                         : row_value(MA, w.row0 + lrow, acc, 0.0f, &res);
+                    OUT.y[w.row0 + lrow] = val;
+                    write_image_block(a.qout, OUT.total_rows, pnl, val, lane, a.qout_act);
+                } else if (mine) {
+                    const float acc = fold_row(term_a, lane, w.ct, nb);
+                    if (FB) write_row(MB, w.row0 + lrow, usum[lane], acc);
+                    else write_row(MA, w.row0 + lrow, acc, 0.0f, &res);
+                }
+                const unsigned end = min((pnl + 1) * P, w.rows);
+                if (end == w.rows) write_padding(OUT, w.row0 + end, lane);
+            }
+        }
+        __syncthreads();  // the term buffers are reused by the next panel
+    }
+    // a staging copy that no warp waited for (a failure): let it land before the CTA exits
+    if (threadIdx.x == 0 && stg.k && failed) mbar_spin(stage_bar, 0);
+}
+
+using GemvKernel = void (*)(GemvArgs);
+
+// The kernel of a format combination (fb = 0: single members), or null.
+static GemvKernel q8_kernel_for(unsigned fa, unsigned fb) {
+    if (fb == 0) {
+        if (fa == 8) return gemv_q8_kernel<8, 0, 4>;
+        if (fa == 2) return gemv_q8_kernel<2, 0, 6>;
+        if (fa == 3) return gemv_q8_kernel<3, 0, 6>;
+    } else {
+        if (fa == 8 && fb == 8) return gemv_q8_kernel<8, 8, 2>;
+        if (fa == 2 && fb == 2) return gemv_q8_kernel<2, 2, 3>;
+        if (fa == 8 && fb == 2) return gemv_q8_kernel<8, 2, 2>;
+        if (fa == 2 && fb == 8) return gemv_q8_kernel<2, 8, 2>;
+        if (fa == 3 && fb == 3) return gemv_q8_kernel<3, 3, 3>;
+    }
+    return nullptr;
 }
 
 __global__ void __launch_bounds__(256) quantize_kernel(const QuantArgs a) {
@@ -222,37 +609,65 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantArgs a) {
     for (unsigned i = threadIdx.x; i < nbs; i += blockDim.x) a.b[i] = X.b[i];
 }
 
-// Shared memory plan of a Q8 pass (see PassSmem): stage = the largest unit tile (x2 for a pair), results = the
-// largest R x stride terms (x2 for a pair); as many stages as fit two CTAs per SM.
+// Shared memory of a Q8 pass: the x image (split halves), the term buffers of one panel (two for a pair), the
+// staging mbarrier and the u sums, and as many staged leading steps of the first panel as keep three CTAs per SM.
 void plan_gemv_q8(GemvArgs &a, size_t &smem) {
-    unsigned stage = 0, res = 0;
+    a.wraw = 0;
+    a.res_bytes = 0;
+    unsigned steps = 0, stage_step_bytes = 0;
+    bool pair = false;
     for (unsigned u = 0; u < a.n_units; ++u) {
-        const MatrixView &w = a.m[a.unit_member[u]].w;
-        const bool pair = a.unit_pair[u] >= 0;
-        const unsigned sb = pair ? pair_offset(w.tile_bytes) + w.tile_bytes : w.tile_bytes;
-        stage = stage > sb ? stage : sb;
-        const unsigned rb = (pair ? 2u : 1u) * w.rt * res_stride(w.ct) * 4u;
-        res = res > rb ? res : rb;
+        const MatrixView &g = a.m[a.unit_member[u]].w;
+        steps = steps > g.kc ? steps : g.kc;
+        unsigned sb = g.tile_bytes;
+        if (a.unit_pair[u] >= 0) {
+            pair = true;
+            sb += a.m[a.unit_pair[u]].w.tile_bytes;
+        }
+        stage_step_bytes = stage_step_bytes > sb ? stage_step_bytes : sb;
     }
-    a.stage_bytes = (stage + 127u) & ~127u;
-    a.res_bytes = (res + 127u) & ~127u;
-    const bool norm_w = (a.norm_mode & 8u) && !(a.norm_mode & 2u) && !a.xq;
-    a.wraw = norm_w && a.cols <= 4096 ? 1u : 0u;
-    unsigned ns = kMaxStages;
-    while (ns > 2 && pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, a.cols, a.wraw, 0) > 113 * 1024) --ns;
-    a.n_stages = ns;
-    smem = pass_smem_bytes(ns, a.stage_bytes, a.res_bytes, a.cols, a.wraw, 0);
+    a.term_bytes = unsigned(align128(size_t(steps) * 128));
+    const size_t fixed = align128(qimage_bytes(a.cols)) + (pair ? 2u : 1u) * size_t(a.term_bytes) + 256;
+    // staged leading steps: what is left of a third of the SM's shared memory (three CTAs per SM)
+    const size_t per_cta = 227 * 1024 / 3 - 1024;
+    const size_t room = per_cta > fixed ? per_cta - fixed : 0;
+    a.n_stages = stage_step_bytes ? unsigned(std::min<size_t>(room / stage_step_bytes, steps)) : 0u;
+    a.stage_bytes = unsigned(align128(size_t(a.n_stages) * stage_step_bytes));
+    smem = fixed + a.stage_bytes;
 }
 
-cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(gemv_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        attr_set = true;
+unsigned gemv_q8_warps_per_cta() { return kPanelWarps; }
+
+bool gemv_q8_supported(unsigned fa, unsigned fb) { return q8_kernel_for(fa, fb) != nullptr; }
+
+// CTAs of the kernel of (fa, fb) with `smem` bytes of shared memory that are resident at once on the GPU (whole
+// clusters of kXCluster).
+unsigned gemv_q8_resident_ctas(unsigned fa, unsigned fb, size_t smem, cudaStream_t st) {
+    const GemvKernel k = q8_kernel_for(fa, fb);
+    if (!k) return kXCluster;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kXCluster * 148);
+    cfg.blockDim = dim3(kPanelThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters < 1) {
+        cudaGetLastError();
+        clusters = 1;
     }
+    return unsigned(clusters) * kXCluster;
+}
+
+unsigned gemv_q8_cluster() { return kXCluster; }
+
+cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned fa, unsigned fb, unsigned grid, size_t smem, cudaStream_t st,
+                           bool pdl) {
+    const GemvKernel k = q8_kernel_for(fa, fb);
+    if (!k) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kPassThreads);
+    cfg.blockDim = dim3(kPanelThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -260,7 +675,7 @@ cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned grid, size_t smem, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_q8_kernel, a);
+    return cudaLaunchKernelEx(&cfg, k, a);
 }
 
 cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st) {

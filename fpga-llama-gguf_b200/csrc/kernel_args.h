@@ -29,6 +29,8 @@ struct GemvMemberArgs {
 };
 
 constexpr unsigned kMaxUnits = 4;
+// bytes of a quantized x image of up to 16384 values (quants + meta words)
+constexpr unsigned kQImageBytes = 16384 + 16384 / 32 * 16;
 
 struct GemvArgs {
     const float *x = nullptr;     // act + x_off (or the deferred norm's x)
@@ -55,6 +57,15 @@ struct GemvArgs {
     unsigned wraw = 0;            // the norm weight is staged in shared memory next to x
     unsigned *err = nullptr;      // set when a bounded wait runs out
     int32_t *dbg = nullptr;       // debug: per-block integer sums of member 0 (no y written)
+    // Q8_0-family pass: bytes of one matrix's block terms of a panel in shared memory (steps x 32 floats)
+    unsigned term_bytes = 0;
+    // quantized x images in the GEMV shared-memory layout ([quants: two runs of 16-byte halves][one 16-byte meta
+    // word per 32-block]): qin, this pass's x (written by the previous pass); qout, the image of member
+    // qout_member's y for the next pass (32-row panels: one block per panel)
+    const uint8_t *qin = nullptr;
+    uint8_t *qout = nullptr;
+    unsigned qout_member = 0;
+    unsigned qout_act = 0;        // 0 Q8_0, 1 Q8_1 (the next pass's activation type)
 };
 
 // Quantize x (optionally through the RMSNORM arithmetic) to scratch: the same device code as the GEMV prologue.

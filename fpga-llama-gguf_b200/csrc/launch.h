@@ -41,8 +41,13 @@ struct AttnArgs {
 
 // fill in the shared-memory plan of a pass (stages, result buffers) and return its dynamic shared memory
 void plan_gemv_q8(GemvArgs &a, size_t &smem);
+unsigned gemv_q8_warps_per_cta();
+bool gemv_q8_supported(unsigned fa, unsigned fb);
+unsigned gemv_q8_resident_ctas(unsigned fa, unsigned fb, size_t smem, cudaStream_t st);
+unsigned gemv_q8_cluster();
 void plan_gemv_kq(GemvArgs &a, size_t &smem);
-cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned fa, unsigned fb, unsigned grid, size_t smem, cudaStream_t st,
+                           bool pdl);
 cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
 cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,

@@ -146,29 +146,48 @@ DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sm
     default: return L;
     }
     if (rows == 0 || L.blocks == 0) return L;
+    if (f == 2 || f == 3 || f == 8) {
+        // Panels of P rows (one per CTA of a pass), streamed as steps of 32 units (P rows x J = 32 / P blocks; the
+        // last step of a panel is zero-padded when J does not divide the blocks). P: the largest for which the
+        // panels fill between half and all of the CTA slots of the GPU (one wave), with at most 15% padding;
+        // matrices too large for one wave take P = 32, too small ones the smallest P (most panels).
+        const unsigned slots = (sms ? sms : 148u) * kPanelCtasPerSm;
+        auto panels = [&](unsigned P) { return (rows + P - 1) / P; };
+        auto padded_ok = [&](unsigned P) {
+            const unsigned J = 32u / P;
+            return double((L.blocks + J - 1) / J * J) <= 1.15 * double(L.blocks);
+        };
+        unsigned P = 0;
+        for (unsigned p = 32; p >= 1 && !P; p /= 2)
+            if (2 * panels(p) >= slots && panels(p) <= slots && padded_ok(p)) P = p;
+        if (!P && panels(32) > slots) P = 32;
+        if (!P)
+            for (unsigned p = 32; p >= 1; p /= 2)
+                if (padded_ok(p)) P = p;
+        if (!P) P = 1;
+        L.rt = P;
+        L.ct = 32u / P;
+        L.kc = (L.blocks + L.ct - 1) / L.ct;
+        L.n_rt = (rows + P - 1) / P;
+        L.qs_part = 32u * L.qb;
+        L.dm_part = 32u * L.db;
+        L.dd_part = 0;
+        L.tile_bytes = L.qs_part + L.dm_part;
+        L.total = (size_t(L.n_rt) * L.kc * L.tile_bytes + 255) & ~size_t(255);
+        return L;
+    }
     const unsigned ub = L.qb + L.db + L.dd;
-    const size_t target = (f == 13 || f == 14) ? kTileTargetK : kTileTarget;
-    // R: rows per tile such that the matrix splits into about one tile per CTA of a pass (two CTAs per SM), so
-    // every CTA of a pass streams the same bytes; at most 32 (one fold lane per row)
+    const size_t target = kTileTargetK;
+    // K-quants: R rows per tile such that the matrix splits into about one tile per CTA of a pass (two CTAs per
+    // SM), at most 32 (one fold lane per row); C the largest divisor of the row's super-blocks within the target.
     const unsigned ctas = 2u * (sms ? sms : 148u);
     unsigned R = (rows + ctas - 1) / ctas;
     R = R < 1 ? 1 : (R > 32 ? 32 : R);
-    // C: Q8_0-family tiles take a power of two <= 32 blocks (lane = (row, block) in the compute warps; a lane's x
-    // block stays in registers for the whole tile); K-quant tiles the largest divisor of the row's super-blocks.
-    // Both within the tile target.
     unsigned C = 1;
-    if (f == 13 || f == 14) {
-        for (unsigned c = L.blocks; c >= 1; --c) {
-            if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
-        }
-        while (R > 1 && size_t(R) * C * ub > target) --R;
-    } else {
-        for (unsigned c = 32; c >= 4; c /= 2) {
-            if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
-        }
-        if (C == 1) C = 4;  // cols is a multiple of 128: 4 always divides the blocks
-        while (R > 1 && size_t(R) * C * ub > target) --R;
+    for (unsigned c = L.blocks; c >= 1; --c) {
+        if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
     }
+    while (R > 1 && size_t(R) * C * ub > target) --R;
     L.rt = R;
     L.ct = C;
     L.kc = L.blocks / C;
@@ -190,7 +209,8 @@ BlockAt block_at(const DeviceLayout &L, unsigned r, unsigned b) {
     const unsigned t = r / L.rt, rr = r % L.rt, k = b / L.ct, cc = b % L.ct;
     const size_t tile = (size_t(t) * L.kc + k) * L.tile_bytes;
     const size_t i = size_t(rr) * L.ct + cc;
-    return {tile + i * L.qb, tile + L.qs_part + i * L.db, tile + L.qs_part + L.dm_part + i * L.dd};
+    const bool q8 = L.format == 2 || L.format == 3 || L.format == 8;
+    return {tile + i * (q8 ? 16u : L.qb), tile + L.qs_part + i * L.db, tile + L.qs_part + L.dm_part + i * L.dd};
 }
 }  // namespace
 
@@ -203,10 +223,13 @@ void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, cons
         const uint8_t *row = gguf + size_t(row_begin + r) * rb;
         for (unsigned b = 0; b < L.blocks; ++b) {
             const BlockAt a = block_at(L, r, b);
-            if (f == 2 || f == 8) {
-                const unsigned bb = f == 2 ? 18 : 34;
-                std::memcpy(dst + a.dm, row + size_t(b) * bb, 2);
-                std::memcpy(dst + a.qs, row + size_t(b) * bb + 2, L.qb);
+            if (f == 2) {
+                std::memcpy(dst + a.dm, row + size_t(b) * 18, 2);
+                std::memcpy(dst + a.qs, row + size_t(b) * 18 + 2, 16);
+            } else if (f == 8) {  // quant halves 512 bytes apart (32 units x 16 bytes)
+                std::memcpy(dst + a.dm, row + size_t(b) * 34, 2);
+                std::memcpy(dst + a.qs, row + size_t(b) * 34 + 2, 16);
+                std::memcpy(dst + a.qs + 512, row + size_t(b) * 34 + 18, 16);
             } else if (f == 3) {
                 std::memcpy(dst + a.dm, row + size_t(b) * 20, 4);
                 std::memcpy(dst + a.qs, row + size_t(b) * 20 + 4, 16);
@@ -232,10 +255,13 @@ void unpack_row(const uint8_t *dev, const DeviceLayout &L, unsigned r, uint8_t *
     uint8_t lo[256], hi[256];
     for (unsigned b = 0; b < L.blocks; ++b) {
         const BlockAt a = block_at(L, r, b);
-        if (f == 2 || f == 8) {
-            const unsigned bb = f == 2 ? 18 : 34;
-            std::memcpy(out + size_t(b) * bb, dev + a.dm, 2);
-            std::memcpy(out + size_t(b) * bb + 2, dev + a.qs, L.qb);
+        if (f == 2) {
+            std::memcpy(out + size_t(b) * 18, dev + a.dm, 2);
+            std::memcpy(out + size_t(b) * 18 + 2, dev + a.qs, 16);
+        } else if (f == 8) {
+            std::memcpy(out + size_t(b) * 34, dev + a.dm, 2);
+            std::memcpy(out + size_t(b) * 34 + 2, dev + a.qs, 16);
+            std::memcpy(out + size_t(b) * 34 + 18, dev + a.qs + 512, 16);
         } else if (f == 3) {
             std::memcpy(out + size_t(b) * 20, dev + a.dm, 4);
             std::memcpy(out + size_t(b) * 20 + 4, dev + a.qs, 16);

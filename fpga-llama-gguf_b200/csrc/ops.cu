@@ -118,19 +118,19 @@ __global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *i
         return;
     }
     const unsigned r = row - w.row0;
-    const unsigned QB = w.format == 2 ? 16u : 32u;
     for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < cols; e += gridDim.x * blockDim.x) {
         const unsigned b = e / 32, j = e % 32;
-        // tiled layout: tile (r / R, b / C), item (r % R) * C + b % C
+        // panel layout: tile (r / P, b / C), unit (r % P) * C + b % C; 16 quant bytes per unit (Q8_0: two
+        // halves 512 bytes apart), then the 32 FP16 scales
         const uint8_t *tile = w.base + (size_t(r / w.rt) * w.kc + b / w.ct) * w.tile_bytes;
         const unsigned i = (r % w.rt) * w.ct + b % w.ct;
         const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(tile + w.qs_part + i * 2));
         int q;
         if (w.format == 2) {
-            const uint8_t byte = tile[i * QB + (j & 15)];
+            const uint8_t byte = tile[i * 16 + (j & 15)];
             q = int(j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
         } else {
-            q = int(int8_t(tile[i * QB + j]));
+            q = int(int8_t(tile[(j / 16) * 512 + i * 16 + (j & 15)]));
         }
         y[e] = fmul(float(q), d);
     }

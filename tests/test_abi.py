@@ -39,14 +39,22 @@ def test_repack_roundtrip_keeps_bits(b2, synth, fmt, cols, rows):
         assert np.unpackbits(dev).sum() == np.unpackbits(w).sum()
 
 
-def test_layout_tiles_balance_the_sms(b2):
-    # about one row tile per CTA (two CTAs per SM), so every CTA of a pass streams the same bytes
-    for rows, cols, fmt in [(9216, 2560, 2), (2560, 9216, 8), (6144, 2560, 2), (2048, 2560, 2)]:
+def test_layout_panels_fill_the_warps(b2):
+    # Q8_0 family: tiles of 32 units (P rows x 32 / P blocks, one warp step); P the largest whose panels (one per
+    # CTA) fill between half and all of the 3 x 148 CTA slots, with at most 15% padding
+    for rows, cols, fmt, P in [(9216, 2560, 8, 32), (2560, 9216, 8, 8), (9216, 2560, 2, 32), (4096, 2560, 2, 16),
+                               (151936, 2560, 2, 32), (300, 512, 3, 2), (1024, 2560, 2, 4)]:
         lay = b2.layout(rows, cols, fmt)
-        assert 2 * 148 * 0.9 <= lay["row_tiles"] <= 2 * 148, (rows, lay)
-        assert lay["tile_bytes"] <= 12288
+        qb, db = {2: (16, 2), 8: (32, 2), 3: (16, 4)}[fmt]
+        assert lay["rows_per_tile"] == P and lay["rows_per_tile"] * lay["blocks_per_tile"] == 32, (rows, lay)
+        assert lay["tile_bytes"] == 32 * (qb + db)
+        assert lay["tiles_per_row_tile"] == -(-cols // 32 // lay["blocks_per_tile"])
+        assert lay["row_tiles"] == -(-rows // P)
+    # K-quants: about one row tile per CTA of a pass (two per SM), tiles within 16 KB
     lay = b2.layout(65520, 2560, 14)
     assert lay["rows_per_tile"] == 32 and lay["tile_bytes"] <= 16384
+    lay = b2.layout(9216, 2560, 13)
+    assert 2 * 148 * 0.9 <= lay["row_tiles"] <= 2 * 148 and lay["tile_bytes"] <= 16384
 
 
 def test_device_bytes_and_row_bytes(b2):

@@ -150,6 +150,34 @@ def test_fused_ffn_block_config1(ctx, b2, synth, orc):
     assert np.array_equal(_bits(got[XIN:XN]), _bits(ref[XIN:XN]))
 
 
+@pytest.mark.parametrize("chain", ["q8_0-to-q4_0", "q4_0-add-to-q4_1"])
+def test_gemv_chain_hands_over_quantized_x(ctx, b2, synth, orc, chain):
+    """A GEMV pass whose output is the next GEMV pass's whole x (32-row panels, no deferred norm) writes that pass's
+    quantized x itself; the chain stays bit-exact against the CPU path (no exp in it). The Q4_1 consumer takes a
+    Q8_1 image (with the s terms)."""
+    ctx.reset_weights()
+    r = rng(49, 0 if chain == "q8_0-to-q4_0" else 1)
+    H, F, K = 2560, 9216, 1024
+    if chain == "q8_0-to-q4_0":
+        ws = _weights_and_list(b2, synth, ctx, [(8, F, H), (2, H, F)], r)
+        h1, h2 = list(ws)
+        X, Y1, Y2 = 0, H, H + F
+        act = np.zeros(Y2 + H, np.float32)
+        act[X:X + H] = synth.activation(r, H)
+        cl = b2.cmd_list(b2.gemv(8, F, H, h1, X, Y1), b2.gemv(2, H, F, h2, Y1, Y2))
+    else:
+        ws = _weights_and_list(b2, synth, ctx, [(2, F, H), (3, K, F)], r)
+        h1, h2 = list(ws)
+        X, R, Y1, Y2 = 0, H, H + F, H + 2 * F
+        act = np.zeros(Y2 + K, np.float32)
+        act[X:X + H] = synth.activation(r, H)
+        act[R:R + F] = synth.activation(r, F)
+        cl = b2.cmd_list(b2.gemv(2, F, H, h1, X, Y1, b2.GEMV_ADD), b2.add(F, Y1, R, Y1), b2.gemv(3, K, F, h2, Y1, Y2))
+    st, passes = b2.plan(cl)
+    assert st == 0 and sum(p["kind"] == "gemv" for p in passes) == 2
+    _compare_list(ctx, orc, cl, ws, act, act.size)
+
+
 def test_q6k_output_head_config2(ctx, b2, synth, orc):
     """The Q6_K output head [151936 x 2560]: GEMV commands hold at most 65536 rows (reference MAX_ROWS), so the head
     goes in 65520-row pieces as the reference backend emits it (ggml-xrt.cpp:133-139, 1536-1554) — here three
