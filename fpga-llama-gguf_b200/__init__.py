@@ -182,6 +182,7 @@ def lib() -> ctypes.CDLL:
         "b200q_plan": (I, [P, U, P, U, ctypes.POINTER(U)]),
         "b200q_debug_quantize": (I, [P, U, SZ, U, U32, ctypes.c_float, U, P, P, P]),
         "b200q_debug_block_sums": (I, [P, P, P]),
+        "b200q_quantize_noalloc": (I, [I, P, U, U, P, ctypes.c_float, U, P, P, P, P, ctypes.c_char_p, U]),
         "b200q_comm_unique_id": (I, [P]),
         "b200q_comm_init": (I, [P, I, I, P]),
         "b200q_comm_world": (I, [P]),
@@ -203,7 +204,8 @@ EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream",
             "b200q_weights_reset", "b200q_act_write", "b200q_act_read", "b200q_act_fill", "b200q_state_write",
             "b200q_state_read", "b200q_kv_write", "b200q_run", "b200q_run_async", "b200q_graph_create",
             "b200q_graph_launch", "b200q_graph_launch_many", "b200q_graph_destroy", "b200q_graph_kernel_count", "b200q_plan",
-            "b200q_debug_quantize", "b200q_debug_block_sums", "b200q_comm_unique_id", "b200q_comm_init",
+            "b200q_debug_quantize", "b200q_debug_block_sums", "b200q_quantize_noalloc", "b200q_comm_unique_id",
+            "b200q_comm_init",
             "b200q_comm_world", "b200q_layout", "b200q_repack_host", "b200q_unpack_row_host"]
 
 
@@ -254,6 +256,31 @@ def plan(cmds: np.ndarray, max_passes: int = 256):
     passes = [dict(first=p.first_cmd, count=p.n_cmds, kind=PASS_KINDS.get(p.kind, "?"), members=p.n_members,
                    fused_norm=bool(p.fused_norm)) for p in infos[: min(n.value, max_passes)]]
     return st, passes
+
+
+NOALLOC_MAX_N = 16384
+
+
+def quantize_noalloc(device: int, x_ptr: int, n: int, fmt: int, norm_w_ptr: int | None = None, eps: float = 0.0,
+                     norm_flags: int = 0, stream: int | None = None):
+    """b200q_quantize_noalloc: n device floats at x_ptr quantized as a GEMV pass of format `fmt` would, without a
+    context and without allocating device memory (n <= NOALLOC_MAX_N). Returns (q, scales, bsums) as
+    Context.debug_quantize does."""
+    q = np.zeros(n, dtype=np.int8)
+    act = 2 if fmt in (Q5_K, Q6_K) else (1 if fmt == Q4_1 else 0)
+    if act == 2:
+        scales = np.zeros(max(n // 256, 1), dtype=np.float32)
+        bs = np.zeros(max(n // 16, 1), dtype=np.int32)
+    else:
+        scales = np.zeros(max(n // 32, 1) * (2 if act == 1 else 1), dtype=np.uint16)
+        bs = np.zeros(max(n // 32, 1), dtype=np.int32)
+    err = ctypes.create_string_buffer(256)
+    rc = lib().b200q_quantize_noalloc(device, x_ptr, n, fmt, norm_w_ptr, eps, norm_flags, stream,
+                                      q.ctypes.data_as(ctypes.c_void_p), scales.ctypes.data_as(ctypes.c_void_p),
+                                      bs.ctypes.data_as(ctypes.c_void_p), err, len(err))
+    if rc != 0:
+        raise B200QError(rc, err.value.decode() or ERR.get(rc, str(rc)))
+    return q, scales, bs
 
 
 def gguf_row_bytes(cols: int, fmt: int) -> int:

@@ -232,6 +232,26 @@ B200Q_API int b200q_debug_quantize(b200q_ctx *ctx, unsigned format, size_t x_off
  * mins sum (0 for Q6_K); Q4_1: rows x cols/32). */
 B200Q_API int b200q_debug_block_sums(b200q_ctx *ctx, const uint32_t cmd[8], int32_t *out);
 
+/* ---- the activation quantizer without a context and without allocation -------------------------------------
+ * No counterpart in the reference (its quantizer runs inside the FPGA kernel, gemvqc16.cpp).
+ * b200q_quantize_noalloc quantizes n device floats exactly as b200q_debug_quantize does (the same kernel and
+ * arithmetic, the same output layout in host memory), for callers that hold no b200q context and may not allocate
+ * device memory: a host runtime whose device memory is all reserved up front by its own pool, or a diagnostic path
+ * that runs after an allocation failed. It allocates nothing. Its scratch is a fixed array in device memory carried
+ * by the library (one per device), so n is limited to B200Q_NOALLOC_MAX_N; larger n is rejected with B200Q_ERR_ARG.
+ *   x, norm_w: device pointers on `device` (norm_w NULL: no deferred RMSNORM; else eps and norm_flags as in
+ *   RMSNORM); stream: a cudaStream_t of that device (NULL: the legacy default stream), synchronized before the call
+ *   returns; q / scales / bsums: host memory as in b200q_debug_quantize (NULL: not copied); err_msg: receives the
+ *   reason of a failure (may be NULL).
+ * The first call on a device looks up the scratch address (cudaGetSymbolAddress, which may initialize the CUDA
+ * context): make it before any stream capture. Nothing in the scratch needs to start at zero. Calls on the same
+ * device that overlap (from other threads, or on other streams before the previous one returned) share the scratch
+ * and race: the library serializes calls within one process, other processes must not share a device this way. */
+#define B200Q_NOALLOC_MAX_N 16384
+B200Q_API int b200q_quantize_noalloc(int device, const float *x, unsigned n, unsigned format, const float *norm_w,
+                                     float norm_eps, unsigned norm_flags, void *stream, int8_t *q, void *scales,
+                                     int32_t *bsums, char *err_msg, unsigned err_len);
+
 /* ---- multi-GPU (one process per GPU, NCCL over NVLink) ------------------------------------------------------- */
 #define B200Q_UNIQUE_ID_BYTES 128
 B200Q_API int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]);
