@@ -131,6 +131,23 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def profiled_traffic(kernel: str):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "gemv_q8_config1_full.txt")
+    try:
+        lines = open(path).read().splitlines()
+    except OSError:
+        return None
+    for i, ln in enumerate(lines):
+        if ln.startswith(f"--- {kernel}:"):
+            for nxt in lines[i + 1:]:
+                if nxt.startswith("---"):
+                    break
+                if nxt.strip().startswith("traffic_bytes_per_launch:"):
+                    return int(nxt.split(":")[1].split()[0])
+    return None
+
+
 def measured_peak():
     try:
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"], "measured"
@@ -294,11 +311,7 @@ def main():
                 "kernel": "gemv_q8_kernel (deferred RMSNorm + Q8_0 gate/up pair + SwiGLU)",
                 "algorithmic_bytes_per_launch": ru_bytes, "us_per_launch": round(ru_ms * 1e3, 3),
                 "peak_kind": peak_kind}
-    try:
-        prof = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
-        roofline["traffic"] = prof.get("gemv_q8_kernel_gate_up")
-    except Exception:
-        pass
+    roofline["traffic"] = profiled_traffic("gemv_q8_kernel<8, 8, 2>")
 
     # end to end through the public API with host buffers: x in (pinned), one token through the stack, y out
     xin = torch.from_numpy(x).pin_memory().numpy()
