@@ -510,14 +510,15 @@ int stamp(b200q_ctx *c, bool on, unsigned cmd, unsigned kind) {
     return 0;
 }
 
-// Pass p's GEMV output that pass q (the next pass) reads as its whole x: pass p can write q's quantized x image
-// itself (one Q8_0/Q8_1 block per 32-row panel, from the values it writes), so q skips its x preparation. Needs:
-// q a Q8_0-family GEMV pass without a deferred norm reading exactly one member's y; that member and its SwiGLU
-// partner in 32-row panels, unsharded, with a plain / SwiGLU / residual-ADD writer. Returns the member index or -1.
-int link_image(const b200q_ctx *c, const Pass &p, const Pass &q) {
-    if (p.kind != PassKind::Gemv || q.kind != PassKind::Gemv || q.from_nd || q.prequant) return -1;
-    const unsigned qact = act_type(q.m[0].format);
-    if (qact == 2) return -1;
+// Pass p's GEMV output that pass q (the next pass that launches work) reads as its whole x: pass p writes q's
+// quantized x image itself, one block per 32-row panel from the values its fold warps store, so q skips its x
+// preparation. Needs: q a Q8_0-family GEMV pass without a deferred norm, reading exactly one member's y; that member
+// (and its SwiGLU partner) unsharded, in 32-row panels, with a plain / SwiGLU / residual-ADD writer. (For a deferred
+// norm the scale needs the whole y first; quantizing it at the end of p costs p's tail more than q's own x
+// preparation, which overlaps q's weight staging.) Returns the member index or -1.
+int link_image(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link) {
+    if (p.kind != PassKind::Gemv || q.kind != PassKind::Gemv || q.prequant || q.from_nd) return -1;
+    if (act_type(q.m[0].format) == 2) return -1;
     for (unsigned i = 0; i < p.n_members; ++i) {
         const Member &m = p.m[i];
         if (m.epi == EpiSwigluG || m.epi == EpiConv) continue;
@@ -529,6 +530,8 @@ int link_image(const b200q_ctx *c, const Pass &p, const Pass &q) {
             if (!w || w->rt != 32 || w->row_begin != 0 || w->row_end != w->rows || act_type(w->format) == 2)
                 return -1;
         }
+        link.out_member = i;
+        link.out_act = act_type(q.m[0].format);
         return int(i);
     }
     return -1;
@@ -546,7 +549,7 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     unsigned img_turn = 0;
     for (size_t pi = 0; pi < plan.passes.size(); ++pi) {
         const Pass &p = plan.passes[pi];
-        if (p.kind != PassKind::Gemv) img_in = nullptr;
+        if (p.kind != PassKind::Gemv && !(p.kind == PassKind::Nop && !p.nd_store)) img_in = nullptr;
         if ((rc = stamp(c, tr, p.first, 0))) return rc;
         const bool is_pass = p.kind == PassKind::Gemv || p.kind == PassKind::Gdn;
         if (is_pass && (rc = stamp(c, tr, p.first, 1))) return rc;
@@ -556,15 +559,12 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
             ImageLink link;
             if (img_in) link.in = img_in;
             img_in = nullptr;
-            if (pi + 1 < plan.passes.size()) {
-                const int mi = link_image(c, p, plan.passes[pi + 1]);
-                if (mi >= 0) {
-                    link.out = c->qimg[img_turn];
-                    link.out_member = unsigned(mi);
-                    link.out_act = act_type(plan.passes[pi + 1].m[0].format);
-                    img_in = c->qimg[img_turn];
-                    img_turn ^= 1u;
-                }
+            size_t qi = pi + 1;  // the next pass that launches work (a deferred RMSNORM's own pass launches none)
+            while (qi < plan.passes.size() && plan.passes[qi].kind == PassKind::Nop && !plan.passes[qi].nd_store) ++qi;
+            if (qi < plan.passes.size() && link_image(c, p, plan.passes[qi], link) >= 0) {
+                link.out = c->qimg[img_turn];
+                img_in = c->qimg[img_turn];
+                img_turn ^= 1u;
             }
             rc = exec_gemv(c, p.m, p.n_members, p.x_off, p.cols, p.from_nd, p.nd, p.prequant, nullptr, nullptr, link);
         }

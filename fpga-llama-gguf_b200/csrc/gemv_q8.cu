@@ -72,6 +72,48 @@ struct XBlock {
     int bsum;
 };
 
+// ---- the RMSNORM scale of x, in the order both quantizer paths use ------------------------------------------------
+// Thread t of a CTA owns values 16 (t & 1) .. +15 of block 128 r + t / 2 in round r (the values it quantizes); it adds
+// their FP32 squares in FP64 in order, rounds in order; then a shuffle tree over the warp, then the warps in order.
+// The reference adds the same FP64 terms left to right; both round to the same FP32 mean unless the exact sum lies
+// within ~1e-13 (relative) of an FP32 rounding boundary.
+__device__ __forceinline__ double sumsq16(const float4 (&v)[4]) {
+    double acc = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc += double(fmul(v[i].x, v[i].x));
+        acc += double(fmul(v[i].y, v[i].y));
+        acc += double(fmul(v[i].z, v[i].z));
+        acc += double(fmul(v[i].w, v[i].w));
+    }
+    return acc;
+}
+
+// The 16 values of thread t in round r (zeros past the end); cg: read through L2 only.
+__device__ __forceinline__ void load16(const float *x, unsigned n, unsigned r, bool cg, float4 (&v)[4]) {
+    const unsigned b = r * (kPanelThreads / 2) + threadIdx.x / 2, h = threadIdx.x & 1u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (b < n / 32) {
+            const float4 *p = reinterpret_cast<const float4 *>(x + b * 32 + h * 16) + i;
+            v[i] = cg ? __ldcg(p) : *p;
+        }
+    }
+}
+
+// Completes the sum from each thread's partial (every thread of the CTA calls it) and returns the RMSNORM scale.
+__device__ __forceinline__ float norm_scale(double acc, unsigned n, float eps, unsigned l2, double *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
+    __syncthreads();
+    double sum = 0.0;
+    for (unsigned w = 0; w < kPanelWarps; ++w) sum += red[w];
+    if (l2) return fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sum)), eps));
+    return fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(sum, double(n))), eps)));
+}
+
 struct XSmem {
     const uint4 *q0, *q1, *meta;
 };
@@ -205,7 +247,7 @@ __device__ __forceinline__ void prepare_x_cluster(const GemvArgs &a, const QImag
     const unsigned n = a.cols, nb = n / 32, rank = cluster_rank();
     const unsigned per = (nb + kXCluster - 1) / kXCluster, b0 = rank * per, b1 = min(nb, b0 + per);
     const bool norm = (a.norm_mode & 8u) != 0, weighted = (a.norm_mode & 2u) == 0;
-    const unsigned t = threadIdx.x, h = t & 1u, b = b0 + (t >> 1), warp = t / 32, lane = t % 32;
+    const unsigned t = threadIdx.x, h = t & 1u, b = b0 + (t >> 1);
     const bool live = b < b1;
     float v[16], w16[16];
 #pragma unroll
@@ -218,40 +260,18 @@ __device__ __forceinline__ void prepare_x_cluster(const GemvArgs &a, const QImag
         v[4 * i] = xv.x, v[4 * i + 1] = xv.y, v[4 * i + 2] = xv.z, v[4 * i + 3] = xv.w;
         w16[4 * i] = wv.x, w16[4 * i + 1] = wv.y, w16[4 * i + 2] = wv.z, w16[4 * i + 3] = wv.w;
     }
-    // the whole x for the RMSNORM sum: the first kNormPre float4 per thread are requested before the hook
-    constexpr unsigned kNormPre = 2;
-    float4 nv[kNormPre];
-#pragma unroll
-    for (unsigned k = 0; k < kNormPre; ++k) {
-        const unsigned i = t + k * kPanelThreads;
-        nv[k] = norm && i < n / 4 ? ldg_act4(a.x + i * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    // the whole x for the RMSNORM sum (canonical order); the first round is requested before the hook
+    float4 nv[4];
+    if (norm) load16(a.x, n, 0, false, nv);
     after_loads();
     float scale = 1.0f;
     if (norm) {
-        double acc = 0.0;
-#pragma unroll
-        for (unsigned k = 0; k < kNormPre; ++k) {
-            acc += double(fmul(nv[k].x, nv[k].x));
-            acc += double(fmul(nv[k].y, nv[k].y));
-            acc += double(fmul(nv[k].z, nv[k].z));
-            acc += double(fmul(nv[k].w, nv[k].w));
+        double acc = sumsq16(nv);
+        for (unsigned r = 1; r * (kPanelThreads / 2) < nb; ++r) {
+            load16(a.x, n, r, false, nv);
+            acc += sumsq16(nv);
         }
-        for (unsigned i = t + kNormPre * kPanelThreads; i < n / 4; i += kPanelThreads) {
-            const float4 u = ldg_act4(a.x + i * 4);
-            acc += double(fmul(u.x, u.x));
-            acc += double(fmul(u.y, u.y));
-            acc += double(fmul(u.z, u.z));
-            acc += double(fmul(u.w, u.w));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) X.red[warp] = acc;
-        __syncthreads();
-        double sum = 0.0;
-        for (unsigned w = 0; w < kPanelWarps; ++w) sum += X.red[w];
-        if (a.norm_mode & 1u) scale = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sum)), a.norm_eps));
-        else scale = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(sum, double(n))), a.norm_eps)));
+        scale = norm_scale(acc, n, a.norm_eps, a.norm_mode & 1u, X.red);
     }
     float amax = 0.0f;
 #pragma unroll
@@ -296,12 +316,26 @@ __device__ __forceinline__ void load_xq(const GemvArgs &a, const QImage &X, unsi
     __syncthreads();
 }
 
-// Copy of an x image written by the previous pass (same layout as the shared-memory image: quants, then meta).
-__device__ __forceinline__ void load_qimage(const GemvArgs &a, const QImage &X) {
+// Copy of an x image written by the previous pass (same layout as the shared-memory image: quants, then meta). The
+// loads go out before the hook (the weight staging copy), so they are not queued behind it.
+template <class Hook>
+__device__ __forceinline__ void load_qimage(const GemvArgs &a, const QImage &X, Hook after_loads) {
     const unsigned n = a.cols, words = (n + n / 32 * 16) / 16;
     const uint4 *src = reinterpret_cast<const uint4 *>(a.qin);
     uint4 *dst = reinterpret_cast<uint4 *>(X.q);
-    for (unsigned i = threadIdx.x; i < words; i += kPanelThreads) dst[i] = src[i];
+    constexpr unsigned kPre = (kQImageBytes / 16 + kPanelThreads - 1) / kPanelThreads;
+    uint4 v[kPre];
+#pragma unroll
+    for (unsigned k = 0; k < kPre; ++k) {
+        const unsigned i = threadIdx.x + k * kPanelThreads;
+        if (i < words) v[k] = __ldcg(src + i);
+    }
+    after_loads();
+#pragma unroll
+    for (unsigned k = 0; k < kPre; ++k) {
+        const unsigned i = threadIdx.x + k * kPanelThreads;
+        if (i < words) dst[i] = v[k];
+    }
     __syncthreads();
 }
 
@@ -483,8 +517,7 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
         mbar_fence_init();
     }
     __syncthreads();
-    // the first steps of the first panel into shared memory: one bulk copy per matrix, issued once the x loads are
-    // on their way (so they are not queued behind the copies)
+    // the first steps of the first panel into shared memory: one bulk copy per matrix
     Staging stg{p, 0u, 0u};
     unsigned u0 = 0, pnl0 = 0;
     if (blockIdx.x < total && a.n_stages) {
@@ -505,15 +538,16 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
         if (v) bulk_copy(p + stg.b_off, v->base + size_t(pnl0) * v->kc * v->tile_bytes, bytes_b, stage_bar, pol);
     };
     pdl_launch_dependents();  // the next kernel may start as SMs free up
+    // weights never change within a list: a CTA that is resident before the previous kernel completes starts its
+    // staging copy now, so HBM streams while that kernel finishes
+    issue_staging();
     pdl_wait();
     if (a.qin) {
-        issue_staging();
-        load_qimage(a, X);
+        load_qimage(a, X, [] {});
     } else if (a.xq) {
-        issue_staging();
         load_xq(a, X, FA == 3 ? 1u : 0u);
     } else {
-        prepare_x_cluster(a, X, FA == 3 ? 1u : 0u, issue_staging);
+        prepare_x_cluster(a, X, FA == 3 ? 1u : 0u, [] {});
     }
     // the rest of the first panel (and the next one) into L2, in step order
     if (threadIdx.x == 0 && blockIdx.x < total) prefetch_panel(a, blockIdx.x, stg.k);

@@ -150,15 +150,37 @@ def test_fused_ffn_block_config1(ctx, b2, synth, orc):
     assert np.array_equal(_bits(got[XIN:XN]), _bits(ref[XIN:XN]))
 
 
-@pytest.mark.parametrize("chain", ["q8_0-to-q4_0", "q4_0-add-to-q4_1"])
+CHAINS = ["q8_0-to-q4_0", "q4_0-add-to-q4_1", "p8-to-q8_0", "q8_0-norm-to-q4_0", "q4_0-l2norm-to-q4_1"]
+
+
+@pytest.mark.parametrize("chain", CHAINS)
 def test_gemv_chain_hands_over_quantized_x(ctx, b2, synth, orc, chain):
-    """A GEMV pass whose output is the next GEMV pass's whole x (32-row panels, no deferred norm) writes that pass's
-    quantized x itself; the chain stays bit-exact against the CPU path (no exp in it). The Q4_1 consumer takes a
-    Q8_1 image (with the s terms)."""
+    """A GEMV pass whose output is the next GEMV pass's whole x writes that pass's quantized x itself when its output
+    rows are in 32-row panels (the first two chains; a Q4_1 consumer takes a Q8_1 image, with the s terms); outputs
+    in smaller panels, and outputs the next pass reads through a deferred RMSNORM (weighted, and L2 without weight),
+    are quantized by the next pass. Every chain stays bit-exact against the CPU path (no exp in it)."""
     ctx.reset_weights()
-    r = rng(49, 0 if chain == "q8_0-to-q4_0" else 1)
+    r = rng(49, CHAINS.index(chain))
     H, F, K = 2560, 9216, 1024
-    if chain == "q8_0-to-q4_0":
+    if chain == "p8-to-q8_0":  # [2560 x 9216] is laid out in 8-row panels
+        ws = _weights_and_list(b2, synth, ctx, [(8, H, F), (8, K, H)], r)
+        h1, h2 = list(ws)
+        X, Y1, Y2 = 0, F, F + H
+        act = np.zeros(Y2 + K, np.float32)
+        act[X:X + F] = synth.activation(r, F)
+        cl = b2.cmd_list(b2.gemv(8, H, F, h1, X, Y1), b2.gemv(8, K, H, h2, Y1, Y2))
+    elif chain in ("q8_0-norm-to-q4_0", "q4_0-l2norm-to-q4_1"):
+        f1, f2, flags = (8, 2, b2.NORM_DEFER) if chain == "q8_0-norm-to-q4_0" else (2, 3, b2.NORM_DEFER | 1 | 2)
+        ws = _weights_and_list(b2, synth, ctx, [(f1, H, F), (f2, K, H)], r)
+        h1, h2 = list(ws)
+        X, R, Y1, G, XN, Y2 = 0, F, F + H, F + 2 * H, F + 3 * H, F + 4 * H
+        act = np.zeros(Y2 + K, np.float32)
+        act[X:X + F] = synth.activation(r, F)
+        act[R:R + H] = synth.activation(r, H)
+        act[G:G + H] = r.normal(1, 0.1, H).astype(np.float32)
+        cl = b2.cmd_list(b2.gemv(f1, H, F, h1, X, Y1, b2.GEMV_ADD), b2.add(H, Y1, R, Y1),
+                         b2.rmsnorm(H, Y1, G, XN, 1e-6, flags=flags), b2.gemv(f2, K, H, h2, XN, Y2))
+    elif chain == "q8_0-to-q4_0":
         ws = _weights_and_list(b2, synth, ctx, [(8, F, H), (2, H, F)], r)
         h1, h2 = list(ws)
         X, Y1, Y2 = 0, H, H + F
@@ -176,6 +198,30 @@ def test_gemv_chain_hands_over_quantized_x(ctx, b2, synth, orc, chain):
     st, passes = b2.plan(cl)
     assert st == 0 and sum(p["kind"] == "gemv" for p in passes) == 2
     _compare_list(ctx, orc, cl, ws, act, act.size)
+
+
+def test_two_layer_ffn_stack(ctx, b2, synth, orc):
+    """Two config-1 FFN blocks in one list, the second reading the residual the first wrote through its deferred
+    RMSNORM (each gate+up pass hands its down pass the quantized SwiGLU output)."""
+    ctx.reset_weights()
+    r = rng(55)
+    H, F = 2560, 9216
+    ws = _weights_and_list(b2, synth, ctx, [(8, F, H), (8, F, H), (8, H, F)] * 2, r)
+    hs = list(ws)
+    R0, GAIN, XN, FF, R1 = 0, H, 2 * H, 4 * H, 4 * H + F
+    act = np.zeros(R1 + H, np.float32)
+    act[R0:R0 + H] = synth.activation(r, H)
+    act[GAIN:GAIN + H] = r.normal(1, 0.1, H).astype(np.float32)
+    cmds = []
+    for layer, (xin, out) in enumerate(((R0, R1), (R1, R0))):
+        hg, hu, hd = hs[3 * layer:3 * layer + 3]
+        cmds += [b2.rmsnorm(H, xin, GAIN, XN, 1e-6, flags=b2.NORM_DEFER),
+                 b2.gemv(8, F, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(8, F, H, hu, XN, FF),
+                 b2.gemv(8, H, F, hd, FF, out, b2.GEMV_ADD), b2.add(H, out, xin, out)]
+    cl = b2.cmd_list(*cmds)
+    got, ref = _compare_list(ctx, orc, cl, ws, act, act.size, exact=False)
+    rel = np.abs(got[R0:R0 + H] - ref[R0:R0 + H]) / np.maximum(np.abs(ref[R0:R0 + H]), 1e-30)
+    assert rel.max() <= 1e-4, rel.max()
 
 
 def test_q6k_output_head_config2(ctx, b2, synth, orc):
