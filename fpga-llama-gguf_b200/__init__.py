@@ -114,8 +114,9 @@ def gdn(hv: int, hk: int, q: int, k: int, v: int, g: int, beta: int, y: int, src
     return cmd_list(*slots)
 
 
-def attn(n_head: int, n_kv: int, head_dim: int, q: int, k: int, v: int, y: int, pos: int, slot: int) -> np.ndarray:
-    return cmd(OP_ATTN, n_head | (n_kv << 8) | ((head_dim // 16) << 16), q, k, v, y, pos, slot)
+def attn(n_head: int, n_kv: int, head_dim: int, q: int, k: int, v: int, y: int, pos_off: int, slot: int) -> np.ndarray:
+    """ATTN extension; the token position is read from act[pos_off] (uint32 bits)."""
+    return cmd(OP_ATTN, n_head | (n_kv << 8) | ((head_dim // 16) << 16), q, k, v, y, pos_off, slot)
 
 
 def argmax(n: int, x: int, y: int) -> np.ndarray:

@@ -474,10 +474,11 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         t.n_head = cmd[1] & 0xffu;
         t.n_kv_head = (cmd[1] >> 8) & 0xffu;
         t.head_dim = (cmd[1] >> 16) * 16u;
-        t.pos = cmd[6];
         t.kv_ctx = c->kv_ctx;
         t.y = A + cmd[5];
+        t.status = c->dstatus;
         std::vector<Range> w{{t.y, size_t(t.n_head) * t.head_dim}};
+        t.pos = snap_if(c, A + cmd[6], 1, w, nullptr, rc);
         t.q = snap_if(c, A + cmd[2], size_t(t.n_head) * t.head_dim, w, nullptr, rc);
         t.k = snap_if(c, A + cmd[3], size_t(t.n_kv_head) * t.head_dim, w, nullptr, rc);
         t.v = snap_if(c, A + cmd[4], size_t(t.n_kv_head) * t.head_dim, w, nullptr, rc);
@@ -615,6 +616,7 @@ int check_device_status(b200q_ctx *c) {
         const unsigned zero[2] = {0, 0};
         CUDA_TRY(c, cudaMemcpy(c->dstatus, zero, sizeof(zero), cudaMemcpyHostToDevice));
         if (st[1]) return set_err(c, B200Q_ERR_TIMEOUT, "a pass gave up waiting for its weight tiles (bounded wait)");
+        if (st[0] & 2u) return set_err(c, B200Q_ERR_ARG, "ATTN: the position in act is outside the KV slot");
         return set_err(c, B200Q_ERR_ARG, "GET_ROW: the row index in act is outside the matrix");
     }
     return 0;

@@ -1,6 +1,7 @@
 // Decode attention over an F16 KV cache (extension opcode 12). The reference leaves the attention core on the CPU
 // (ggml F16 path); this kernel runs it on the GPU so a whole token stays on the device: the token's k and v are
-// stored into the cache (F16, round to nearest even) at position pos, then per query head
+// stored into the cache (F16, round to nearest even) at position pos (read from act, so a replayed graph serves
+// every token; outside the slot: nothing is written and the status word says so), then per query head
 // scores_t = (q . k_t) * scale over t = 0..pos, softmax with the maximum subtracted, y = sum_t p_t v_t / sum_t p_t.
 // GQA: query head h reads KV head h / (n_head / n_kv_head). One CTA per query head; FP32 sums (tolerance-checked
 // against the CPU oracle, which sums in FP64).
@@ -14,12 +15,17 @@ constexpr unsigned kAttnThreads = 256;
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     extern __shared__ float sm[];
     float *qsh = sm;               // head_dim
-    float *p = sm + a.head_dim;    // pos + 1 scores
+    float *p = sm + a.head_dim;    // pos + 1 scores (room for kv_ctx)
     __shared__ float redf[32];
     pdl_wait();
+    const unsigned pos = __float_as_uint(*a.pos);
+    if (pos >= a.kv_ctx) {
+        if (blockIdx.x == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, 2u);
+        return;
+    }
     const unsigned h = blockIdx.x, group = a.n_head / a.n_kv_head, kvh = h / group, hd = a.head_dim;
-    const unsigned T = a.pos + 1, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = kAttnThreads / 32;
-    const size_t kv_row = (size_t(kvh) * a.kv_ctx + a.pos) * hd;
+    const unsigned T = pos + 1, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = kAttnThreads / 32;
+    const size_t kv_row = (size_t(kvh) * a.kv_ctx + pos) * hd;
     for (unsigned e = threadIdx.x; e < hd; e += kAttnThreads) {
         qsh[e] = a.q[size_t(h) * hd + e];
         if (h % group == 0) {
@@ -33,7 +39,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     for (unsigned t = warp; t < T; t += nw) {
         float s = 0.0f;
         for (unsigned e = lane; e < hd; e += 32) {
-            const float kv = t == a.pos ? half_bits_to_float(float_to_half_bits(a.k[size_t(kvh) * hd + e]))
+            const float kv = t == pos ? half_bits_to_float(float_to_half_bits(a.k[size_t(kvh) * hd + e]))
                                         : half_bits_to_float(kc[size_t(t) * hd + e]);
             s = fmaf(qsh[e], kv, s);
         }
@@ -66,7 +72,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     for (unsigned e = threadIdx.x; e < hd; e += kAttnThreads) {
         float acc = 0.0f;
         for (unsigned t = 0; t < T; ++t) {
-            const float vv = t == a.pos ? half_bits_to_float(float_to_half_bits(a.v[size_t(kvh) * hd + e]))
+            const float vv = t == pos ? half_bits_to_float(float_to_half_bits(a.v[size_t(kvh) * hd + e]))
                                         : half_bits_to_float(vc[size_t(t) * hd + e]);
             acc = fmaf(p[t], vv, acc);
         }
@@ -83,7 +89,7 @@ cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_head);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = sizeof(float) * (a.head_dim + a.pos + 1);
+    cfg.dynamicSmemBytes = sizeof(float) * (a.head_dim + a.kv_ctx);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -32,7 +32,9 @@ struct GdnArgs {
 };
 
 struct AttnArgs {
-    unsigned n_head = 0, n_kv_head = 0, head_dim = 0, pos = 0, kv_ctx = 0;
+    unsigned n_head = 0, n_kv_head = 0, head_dim = 0, kv_ctx = 0;
+    const float *pos = nullptr;                     // the token position (uint32 bits)
+    unsigned *status = nullptr;                     // bit 1 set when the position is outside the slot
     const float *q = nullptr, *k = nullptr, *v = nullptr;
     float *y = nullptr;
     uint16_t *kcache = nullptr, *vcache = nullptr;  // [n_kv_head][kv_ctx][head_dim] F16 each

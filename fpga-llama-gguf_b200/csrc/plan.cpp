@@ -395,10 +395,11 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
         } else if (op == 12) {
             // ---- ATTN extension
             const unsigned nh = cmd[1] & 0xffu, nkv = (cmd[1] >> 8) & 0xffu, hd = (cmd[1] >> 16) * 16u;
-            const unsigned pos = cmd[6], slot = cmd[7];
+            const unsigned slot = cmd[7];
             const size_t slot_bytes = size_t(nkv) * lim.kv_ctx * hd * 2 * 2;
             if (nh == 0 || nkv == 0 || nh % nkv || hd == 0 || hd > 512 || cmd[2] % 16 || cmd[3] % 16 || cmd[4] % 16 ||
-                cmd[5] % 16 || pos >= lim.kv_ctx || !C.act(cmd[2], size_t(nh) * hd) || !C.act(cmd[3], size_t(nkv) * hd) ||
+                cmd[5] % 16 || cmd[6] % 16 || lim.kv_ctx == 0 || !C.act(cmd[6], 1) ||
+                !C.act(cmd[2], size_t(nh) * hd) || !C.act(cmd[3], size_t(nkv) * hd) ||
                 !C.act(cmd[4], size_t(nkv) * hd) || !C.act(cmd[5], size_t(nh) * hd) ||
                 (size_t(slot) + 1) * slot_bytes > lim.kv_bytes) {
                 reject(c, "invalid ATTN");

@@ -61,8 +61,10 @@ extern "C" {
 #define B200Q_OP_ROPE 10u
 #define B200Q_OP_TRACE 11u
 /* extensions (no reference counterpart; see the feature word 3 bits below) */
-/* [12, n_head | n_kv_head << 8 | (head_dim / 16) << 16, q_off, k_off, v_off, y_off, pos, slot]: stores this token's
- * k, v (F16) at position pos of KV slot `slot`, then y = softmax(q K^T / sqrt(head_dim)) V over positions 0..pos */
+/* [12, n_head | n_kv_head << 8 | (head_dim / 16) << 16, q_off, k_off, v_off, y_off, pos_off, slot]: pos = act[pos_off]
+ * (uint32 bits, so a replayed graph reads each token's position from act); stores this token's k, v (F16) at
+ * position pos of KV slot `slot`, then y = softmax(q K^T / sqrt(head_dim)) V over positions 0..pos. A pos outside the
+ * slot writes nothing and makes b200q_run / b200q_synchronize return B200Q_ERR_ARG. */
 #define B200Q_OP_ATTN 12u
 /* [13, n, x_off, y_off, 0, 0, 0, 0]: y[0] = first index of the maximum (uint32 bits), y[1] = the maximum */
 #define B200Q_OP_ARGMAX 13u
@@ -145,8 +147,10 @@ B200Q_API void *b200q_kv_device_ptr(b200q_ctx *ctx);
 B200Q_API void b200q_features(uint32_t out[3]);
 
 /* One-time repack + upload of a GGUF matrix (rows x cols, row-major GGUF blocks; format a B200Q_Q* id). The bits
- * of every scale and quant stay as they are; only their arrangement changes (scales and quants in separate
- * row-major regions; K-quant quant fields permuted within each super-block).
+ * of every scale and quant stay as they are; only their arrangement changes: Q4_0 / Q4_1 / Q8_0 rows are cut into
+ * panels of P rows (P from the matrix shape) whose quants are interleaved 16 bytes per (row, block) step and whose
+ * scales follow each 32-block tile; Q5_K / Q6_K matrices are cut into tiles of R rows x up to 16384 columns with
+ * the quant fields permuted within each super-block. b200q_layout() reports the arrangement.
  * block_cols: 0, or 256 for a matrix that a GDN_WITH_OUT step consumes (accepted for list compatibility; the
  * device layout is the same). *w_off receives the handle for GEMV words 4/5. In a row-sharded context (after
  * b200q_comm_init) only this rank's row slice is kept. */

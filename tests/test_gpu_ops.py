@@ -163,7 +163,8 @@ def test_attention_argmax_getrow(ctx, b2, synth, orc):
     he = ctx.upload(emb, 100, 256, 2, flags=b2.UPLOAD_REPLICATE)
     act[12800:12800 + 300] = r.normal(0, 1, 300)
     act[13312] = np.array([37], np.uint32).view(np.float32)[0]
-    cl = b2.cmd_list(b2.attn(nh, nkv, hd, Q, K, V, YY, 512, 0), b2.argmax(300, 12800, 13120),
+    act[13440] = np.array([512], np.uint32).view(np.float32)[0]  # the token position
+    cl = b2.cmd_list(b2.attn(nh, nkv, hd, Q, K, V, YY, 13440, 0), b2.argmax(300, 12800, 13120),
                      b2.get_row(2, 256, he, 13312, 13376))
     got, ref, _, _ = _run_both(ctx, orc, cl, act, ws={he: (emb.reshape(-1), 100, 256, 2)}, kv_ctx=kv_ctx, kv=kv)
     rel = np.abs(got[YY:YY + nh * hd] - ref[YY:YY + nh * hd]) / np.maximum(np.abs(ref[YY:YY + nh * hd]), 1e-3)
