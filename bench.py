@@ -198,6 +198,72 @@ def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
                       f"each, gemvq_ref.h generic path, {cores} threads"}
 
 
+def decode_bench(b2, torch, dist, dev: int, world: int, rank: int, shape, label: str, tokens: int, warm: int,
+                 max_over_ranks, barrier):
+    """Batch-1 greedy decode of the synthetic hybrid model: `tokens` tokens at positions prefill ..
+    prefill + tokens - 1, each one stream-ordered record write (position + RoPE row, page-locked), the replay of the
+    token's lists (one CUDA Graph each) and a stream-ordered read of the argmax token; the device chains the tokens
+    (ARGMAX -> next GET_ROW). Timed with CUDA events on the context stream (max over ranks); then the same loop with
+    the host waiting for every token (a host-side sampler's pattern), wall clock."""
+    import fpga_llama_gguf_b200.decode as D
+    t_setup = time.perf_counter()
+    m = D.HybridDecoder(shape)
+    ctx = b2.Context(device=dev, **m.context_config(world))
+    if world > 1:
+        obj = [b2.Context.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.comm_init(world, rank, obj[0])
+    m.load(ctx)
+    graphs = [ctx.graph(cl) for cl in m.token_lists()]
+    setup_s = time.perf_counter() - t_setup
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+    n = max(tokens, warm)
+    rec = torch.empty((n, D.RECORD), dtype=torch.float32).pin_memory()
+    rec.copy_(torch.from_numpy(np.stack([m.record(shape.prefill + t) for t in range(n)])))
+    out = torch.zeros((n, 2), dtype=torch.float32).pin_memory()
+    row = D.RECORD * 4
+
+    def run(k: int):
+        for t in range(k):
+            ctx.write_async(m.L.REC, rec.data_ptr() + t * row, D.RECORD)
+            ctx.launch_many(graphs, len(graphs))
+            ctx.read_async(m.L.TOK, out.data_ptr() + t * 8, 2)
+
+    run(warm)
+    ctx.synchronize()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    run(tokens)
+    end.record(stream)
+    end.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / tokens)
+    toks = [int(v) for v in out[:tokens, 0].numpy().view(np.uint32)]
+    barrier()
+    # host waits for each token before the next (synchronous write, replay, synchronous read)
+    n_sync = min(tokens, 32)
+    t0 = time.perf_counter()
+    for t in range(n_sync):
+        ctx.write(m.L.REC, rec[t].numpy())
+        ctx.launch_many(graphs, len(graphs))
+        ctx.read(m.L.TOK, 2)
+    ms_sync = max_over_ranks((time.perf_counter() - t0) / n_sync * 1e3)
+    kernels = sum(g.kernels for g in graphs)
+    for g in graphs:
+        g.close()
+    ctx.close()
+    bpt = shape.bytes_per_token()
+    peak, peak_kind = measured_peak()
+    return {"model": label, "tokens": tokens, "positions": f"{shape.prefill}..{shape.prefill + tokens - 1}",
+            "tokens_per_s": round(1e3 / ms, 2), "ms_per_token": round(ms, 4),
+            "tokens_per_s_host_synced": round(1e3 / ms_sync, 2), "bytes_per_token": bpt,
+            "hbm_gbs": round(bpt / (ms * 1e-3) / 1e9, 1),
+            "frac_of_peak": round(bpt / (ms * 1e-3) / 1e9 / (peak * world), 4), "peak_kind": peak_kind,
+            "roofline_tokens_per_s": round(peak * world * 1e9 / bpt, 1), "lists_per_token": len(graphs),
+            "kernels_per_token": kernels, "h2d_bytes_per_token": row, "d2h_bytes_per_token": 8,
+            "first_tokens": toks[:8], "scaling": "strong", "setup_s": round(setup_s, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -205,6 +271,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--decode", default="4b,9b", help="synthetic decode models to run after the GEMV stack "
+                    "(comma list of 4b, 9b; empty for none)")
+    ap.add_argument("--decode-tokens", type=int, default=128)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -338,6 +407,16 @@ def main():
     for g in (stack, ru):
         g.close()
     ctx.close()
+
+    decode = {}
+    import fpga_llama_gguf_b200.decode as D
+    shapes = {"4b": (D.SHAPE_4B, "4B-like: 24 GDN + 8 gated GQA layers, hidden 2560, FFN 9216, vocab 151936, Q4_0 + "
+                                 "Q6_K head, 512-token F16 KV"),
+              "9b": (D.SHAPE_9B, "9B-like: as 4B-like with hidden 4096, FFN 12288")}
+    for key in [k for k in args.decode.split(",") if k]:
+        shape, label = shapes[key]
+        decode[key] = decode_bench(b2, torch, dist, dev, world, rank, shape, label, args.decode_tokens,
+                                   max(3, min(args.warmup, 16)), max_over_ranks, barrier)
     if dist:
         dist.destroy_process_group()
     if rank == 0:
@@ -348,7 +427,8 @@ def main():
                 "config": dict(config, l2=f"{n_layers} layers with distinct weights per step "
                                                              f"({n_layers * per_layer >> 20} MiB per GPU > 3x L2)",
                                frac_of_peak=round(value / peak, 4)),
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+                "decode": decode}
         print(json.dumps(line), flush=True)
     return 0
 

@@ -170,6 +170,8 @@ def lib() -> ctypes.CDLL:
         "b200q_act_write": (I, [P, SZ, P, SZ]),
         "b200q_act_read": (I, [P, SZ, P, SZ]),
         "b200q_act_fill": (I, [P, SZ, ctypes.c_float, SZ]),
+        "b200q_act_write_async": (I, [P, SZ, P, SZ]),
+        "b200q_act_read_async": (I, [P, SZ, P, SZ]),
         "b200q_state_write": (I, [P, SZ, P, SZ]),
         "b200q_state_read": (I, [P, SZ, P, SZ]),
         "b200q_kv_write": (I, [P, SZ, P, SZ]),
@@ -202,7 +204,8 @@ def lib() -> ctypes.CDLL:
 EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream", "b200q_synchronize",
             "b200q_act_device_ptr", "b200q_state_device_ptr", "b200q_kv_device_ptr", "b200q_features",
             "b200q_upload_weight", "b200q_upload_weight_ex", "b200q_weight_device_bytes", "b200q_gguf_row_bytes",
-            "b200q_weights_reset", "b200q_act_write", "b200q_act_read", "b200q_act_fill", "b200q_state_write",
+            "b200q_weights_reset", "b200q_act_write", "b200q_act_read", "b200q_act_fill", "b200q_act_write_async",
+            "b200q_act_read_async", "b200q_state_write",
             "b200q_state_read", "b200q_kv_write", "b200q_run", "b200q_run_async", "b200q_graph_create",
             "b200q_graph_launch", "b200q_graph_launch_many", "b200q_graph_destroy", "b200q_graph_kernel_count", "b200q_plan",
             "b200q_debug_quantize", "b200q_debug_block_sums", "b200q_quantize_noalloc", "b200q_comm_unique_id",
@@ -255,7 +258,8 @@ def plan(cmds: np.ndarray, max_passes: int = 256):
     st = lib().b200q_plan(c.ctypes.data_as(ctypes.c_void_p), len(c) // CMD_WORDS, infos, max_passes,
                           ctypes.byref(n))
     passes = [dict(first=p.first_cmd, count=p.n_cmds, kind=PASS_KINDS.get(p.kind, "?"), members=p.n_members,
-                   fused_norm=bool(p.fused_norm)) for p in infos[: min(n.value, max_passes)]]
+                   fused_norm=bool(p.fused_norm), stored_norm=p.fused_norm == 2)
+              for p in infos[: min(n.value, max_passes)]]
     return st, passes
 
 
@@ -286,6 +290,11 @@ def quantize_noalloc(device: int, x_ptr: int, n: int, fmt: int, norm_w_ptr: int 
 
 def gguf_row_bytes(cols: int, fmt: int) -> int:
     return int(lib().b200q_gguf_row_bytes(cols, fmt))
+
+
+def weight_device_bytes(rows: int, cols: int, fmt: int) -> int:
+    """Device bytes of one uploaded matrix (its repacked layout), before the arena's 256-byte rounding."""
+    return int(lib().b200q_weight_device_bytes(rows, cols, fmt))
 
 
 class Graph:
@@ -359,6 +368,10 @@ class Context:
     def act_ptr(self) -> int:
         return int(lib().b200q_act_device_ptr(self.h))
 
+    @property
+    def kv_ptr(self) -> int:
+        return int(lib().b200q_kv_device_ptr(self.h) or 0)
+
     def synchronize(self):
         self._check(lib().b200q_synchronize(self.h))
 
@@ -387,6 +400,15 @@ class Context:
         out = np.empty(n, dtype=np.float32)
         self._check(lib().b200q_act_read(self.h, off, out.ctypes.data_as(ctypes.c_void_p), n))
         return out
+
+    def write_async(self, off: int, host_ptr: int, n: int) -> None:
+        """Stream-ordered copy of n floats at host_ptr (page-locked memory for no wait) into act[off:]; the buffer
+        must stay untouched until synchronize()."""
+        self._check(lib().b200q_act_write_async(self.h, off, host_ptr, n))
+
+    def read_async(self, off: int, host_ptr: int, n: int) -> None:
+        """Stream-ordered copy of act[off:off + n] to host_ptr; valid after synchronize()."""
+        self._check(lib().b200q_act_read_async(self.h, off, host_ptr, n))
 
     def fill(self, off: int, value: float, n: int) -> None:
         self._check(lib().b200q_act_fill(self.h, off, value, n))

@@ -71,6 +71,9 @@ bool load_nccl(std::string &err) {
 
 constexpr size_t kSnapFloats = size_t(1) << 20;  // snapshot scratch (overlapping in/out ranges)
 constexpr unsigned kMaxTraceEvents = 4096;
+// device words after the status words: per-KV-head chunk counters of ATTN, the ARGMAX combine slot
+constexpr unsigned kSyncAttnWord = 256, kSyncArgmaxWord = 512;
+constexpr size_t kAttnPartFloats = size_t(1) << 22;  // ATTN chunk outputs (16 MiB)
 
 }  // namespace
 
@@ -99,6 +102,7 @@ struct b200q_ctx {
     float *snap = nullptr;
     size_t snap_used = 0;
     unsigned *dstatus = nullptr;
+    float *attn_part = nullptr;
     unsigned long long *tstamps = nullptr;
     uint32_t *ttags = nullptr;
     std::vector<uint32_t> host_tags;
@@ -487,9 +491,23 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         t.kcache = c->kv + size_t(cmd[7]) * slot_elems * 2;
         t.vcache = t.kcache + slot_elems;
         t.scale = 1.0f / std::sqrt(float(t.head_dim));
+        t.chunk = attn_chunk(c->kv_ctx, t.n_kv_head, unsigned(c->sms));
+        t.max_chunks = (c->kv_ctx + t.chunk - 1) / t.chunk;
+        if (size_t(t.n_head) * t.max_chunks * (t.head_dim + 2) > kAttnPartFloats)
+            return set_err(c, B200Q_ERR_ARG, "ATTN: n_head x kv_ctx x head_dim too large for the chunk buffer");
+        if (attn_smem_bytes(t.n_head, t.n_kv_head, t.head_dim, t.chunk, t.max_chunks) > 200 * 1024)
+            return set_err(c, B200Q_ERR_ARG, "ATTN: the chunk does not fit in shared memory");
+        t.part = c->attn_part;
+        t.counters = c->dstatus + kSyncAttnWord;
+        t.err = c->dstatus + 1;
         CUDA_TRY(c, launch_attn(t, c->stream, c->pdl));
     } else if (p.op == 13) {
-        CUDA_TRY(c, launch_argmax(A + cmd[2], cmd[1], A + cmd[3], c->stream, c->pdl));
+        std::vector<Range> w{{A + cmd[3], 2}};
+        const float *x = snap_if(c, A + cmd[2], cmd[1], w, nullptr, rc);
+        if (rc) return rc;
+        CUDA_TRY(c, launch_argmax(x, cmd[1], A + cmd[3],
+                                  reinterpret_cast<unsigned long long *>(c->dstatus + kSyncArgmaxWord),
+                                  c->dstatus + kSyncArgmaxWord + 2, c->stream, c->pdl));
     } else if (p.op == 14) {
         const WeightInfo *w = find_w(c, uint64_t(cmd[3]) | (uint64_t(cmd[4]) << 32));
         if (!w) return set_err(c, B200Q_ERR_ARG, "GET_ROW: unknown weight");
@@ -675,6 +693,7 @@ int b200q_create(const b200q_config *cfg, b200q_ctx **out) {
     if (c->kv_bytes) {
         if ((e = cudaMalloc(&c->kv, c->kv_bytes)) != cudaSuccess) return fail(e, "kv");
         cudaMemset(c->kv, 0, c->kv_bytes);
+        if ((e = cudaMalloc(&c->attn_part, kAttnPartFloats * sizeof(float))) != cudaSuccess) return fail(e, "attn");
     }
     const size_t scratch = kMaxCols + 4 * (kMaxCols / 16) * 4 + kMaxCols * 4 + kSnapFloats * 4 + 4096 +
                            kMaxTraceEvents * 12;
@@ -721,6 +740,7 @@ void b200q_destroy(b200q_ctx *c) {
     cudaFree(c->act);
     cudaFree(c->state);
     cudaFree(c->kv);
+    cudaFree(c->attn_part);
     cudaFree(c->xq);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -820,12 +840,29 @@ int b200q_act_read(b200q_ctx *c, size_t off, float *dst, size_t n) {
     return 0;
 }
 
+int b200q_act_write_async(b200q_ctx *c, size_t off, const float *src, size_t n) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!src || off > c->act_floats || n > c->act_floats - off) return set_err(c, B200Q_ERR_ARG, "act_write range");
+    CUDA_TRY(c, cudaMemcpyAsync(c->act + off, src, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    return 0;
+}
+
+int b200q_act_read_async(b200q_ctx *c, size_t off, float *dst, size_t n) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!dst || off > c->act_floats || n > c->act_floats - off) return set_err(c, B200Q_ERR_ARG, "act_read range");
+    CUDA_TRY(c, cudaMemcpyAsync(dst, c->act + off, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    return 0;
+}
+
 int b200q_act_fill(b200q_ctx *c, size_t off, float value, size_t n) {
     int rc = check_ctx(c);
     if (rc) return rc;
     if (off > c->act_floats || n > c->act_floats - off) return set_err(c, B200Q_ERR_ARG, "act_fill range");
     std::vector<float> v(n, value);
-    CUDA_TRY(c, cudaMemcpy(c->act + off, v.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+    CUDA_TRY(c, cudaMemcpyAsync(c->act + off, v.data(), n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
     return 0;
 }
 
@@ -961,7 +998,7 @@ int b200q_plan(const uint32_t *cmds, unsigned n_cmds, b200q_pass_info *passes, u
             o.kind = uint32_t(p.kind);
             o.n_members = p.kind == PassKind::Gemv ? p.n_members
                                                    : (p.kind == PassKind::Gdn ? unsigned(p.gdn_with_gemv) + unsigned(p.gdn_with_out) : 0u);
-            o.fused_norm = p.from_nd ? 1u : 0u;
+            o.fused_norm = p.from_nd ? (p.nd.materialize ? 2u : 1u) : 0u;
         }
         ++k;
     }

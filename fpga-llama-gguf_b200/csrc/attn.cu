@@ -3,81 +3,223 @@
 // stored into the cache (F16, round to nearest even) at position pos (read from act, so a replayed graph serves
 // every token; outside the slot: nothing is written and the status word says so), then per query head
 // scores_t = (q . k_t) * scale over t = 0..pos, softmax with the maximum subtracted, y = sum_t p_t v_t / sum_t p_t.
-// GQA: query head h reads KV head h / (n_head / n_kv_head). One CTA per query head; FP32 sums (tolerance-checked
-// against the CPU oracle, which sums in FP64).
+// GQA: query head h reads KV head h / (n_head / n_kv_head).
+//
+// Split over positions (flash decoding): CTA (chunk, kv head) takes positions [chunk * C, chunk * C + C) for all G
+// query heads of its KV head, so each K/V row is read once per token. The chunk's K and V rows are contiguous in the
+// cache: two bulk copies bring them into shared memory. The CTA writes its chunk's maximum m, sum l and unnormalised
+// output o per query head; the last CTA of a KV head to finish (counter in the sync words, reset by that CTA) merges
+// the chunks: y = sum_c w_c o_c with w_c = e^(m_c - M) / sum_c e^(m_c - M) l_c. Chunks past pos exit at once. Only
+// the CTA that holds pos touches row pos: it uses the token's k / v (rounded to F16) for it and stores them after
+// its copies landed. FP32 sums (tolerance-checked against the CPU oracle, which sums in FP64).
 #include "launch.h"
+#include "pipeline.cuh"
 #include "quant.cuh"
 
 namespace b200q {
 
-constexpr unsigned kAttnThreads = 256;
+constexpr unsigned kAttnThreads = 256, kAttnWarps = kAttnThreads / 32, kAttnMaxGroup = 16;
+
+__device__ __forceinline__ void half8_to_float(uint4 u, float *f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = half_bits_to_float(uint16_t(w[i] & 0xffffu));
+        f[2 * i + 1] = half_bits_to_float(uint16_t(w[i] >> 16));
+    }
+}
+
+struct AttnSmem {
+    uint16_t *k, *v;  // [C][hd] F16 rows of the chunk
+    float *q;         // [G][hd]
+    float *p;         // [G][C] scores, then probabilities
+    float *ml;        // [G][2] chunk maximum and sum
+    float *w;         // [G][max_chunks] merge weights (last CTA)
+};
+
+__device__ __forceinline__ AttnSmem attn_smem(unsigned char *base, unsigned G, unsigned hd, unsigned C,
+                                              unsigned max_chunks) {
+    AttnSmem S;
+    S.k = reinterpret_cast<uint16_t *>(base);
+    S.v = S.k + size_t(C) * hd;
+    S.q = reinterpret_cast<float *>(S.v + size_t(C) * hd);
+    S.p = S.q + G * hd;
+    S.ml = S.p + G * C;
+    S.w = S.ml + 2 * G;
+    (void)max_chunks;
+    return S;
+}
 
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
-    extern __shared__ float sm[];
-    float *qsh = sm;               // head_dim
-    float *p = sm + a.head_dim;    // pos + 1 scores (room for kv_ctx)
-    __shared__ float redf[32];
+    extern __shared__ __align__(128) unsigned char attn_sm[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ unsigned last_s, ok_s;
+    const unsigned G = a.n_head / a.n_kv_head, hd = a.head_dim, C = a.chunk, nvec = hd / 8;
+    const AttnSmem S = attn_smem(attn_sm, G, hd, C, a.max_chunks);
     pdl_wait();
     const unsigned pos = __float_as_uint(*a.pos);
     if (pos >= a.kv_ctx) {
-        if (blockIdx.x == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, 2u);
+        if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, 2u);
         return;
     }
-    const unsigned h = blockIdx.x, group = a.n_head / a.n_kv_head, kvh = h / group, hd = a.head_dim;
-    const unsigned T = pos + 1, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = kAttnThreads / 32;
-    const size_t kv_row = (size_t(kvh) * a.kv_ctx + pos) * hd;
-    for (unsigned e = threadIdx.x; e < hd; e += kAttnThreads) {
-        qsh[e] = a.q[size_t(h) * hd + e];
-        if (h % group == 0) {
-            a.kcache[kv_row + e] = float_to_half_bits(a.k[size_t(kvh) * hd + e]);
-            a.vcache[kv_row + e] = float_to_half_bits(a.v[size_t(kvh) * hd + e]);
+    const unsigned T = pos + 1, chunk = blockIdx.x, kvh = blockIdx.y, c0 = chunk * C;
+    if (c0 >= T) return;
+    const unsigned n_chunks = (T + C - 1) / C, cn = T - c0 < C ? T - c0 : C;
+    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const size_t row0 = size_t(kvh) * a.kv_ctx + c0;  // first cache row of the chunk
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        const unsigned bytes = cn * hd * 2;
+        mbar_expect_tx(&bar, 2 * bytes);
+        const uint64_t pol = evict_first_policy();
+        bulk_copy(S.k, a.kcache + row0 * hd, bytes, &bar, pol);
+        bulk_copy(S.v, a.vcache + row0 * hd, bytes, &bar, pol);
+    }
+    for (unsigned e = threadIdx.x; e < G * hd; e += kAttnThreads) S.q[e] = a.q[size_t(kvh) * G * hd + e];
+    if (threadIdx.x == 0) {
+        ok_s = mbar_wait(&bar, 0);
+        if (!ok_s) {
+            if (a.err) atomicExch(a.err, 1u);
+            mbar_wait(&bar, 0);  // let the copies land before the CTA exits
         }
     }
     __syncthreads();
-    const uint16_t *kc = a.kcache + size_t(kvh) * a.kv_ctx * hd;
-    const uint16_t *vc = a.vcache + size_t(kvh) * a.kv_ctx * hd;
-    for (unsigned t = warp; t < T; t += nw) {
-        float s = 0.0f;
-        for (unsigned e = lane; e < hd; e += 32) {
-            const float kv = t == pos ? half_bits_to_float(float_to_half_bits(a.k[size_t(kvh) * hd + e]))
-                                        : half_bits_to_float(kc[size_t(t) * hd + e]);
-            s = fmaf(qsh[e], kv, s);
+    if (!ok_s) return;
+    if (pos < c0 + cn) {  // this CTA holds the new row: use it, then store it in the cache
+        const size_t r = size_t(pos - c0) * hd;
+        for (unsigned e = threadIdx.x; e < hd; e += kAttnThreads) {
+            const uint16_t kb = float_to_half_bits(a.k[size_t(kvh) * hd + e]);
+            const uint16_t vb = float_to_half_bits(a.v[size_t(kvh) * hd + e]);
+            S.k[r + e] = kb;
+            S.v[r + e] = vb;
+            a.kcache[(row0 + pos - c0) * hd + e] = kb;
+            a.vcache[(row0 + pos - c0) * hd + e] = vb;
+        }
+    }
+    __syncthreads();
+    // scores: warp w takes rows w, w + 8, ...; lanes split the row in 8-value vectors
+    for (unsigned i = warp; i < cn; i += kAttnWarps) {
+        float acc[kAttnMaxGroup];
+#pragma unroll
+        for (unsigned g = 0; g < kAttnMaxGroup; ++g) acc[g] = 0.0f;
+        for (unsigned vec = lane; vec < nvec; vec += 32) {
+            float k8[8];
+            half8_to_float(reinterpret_cast<const uint4 *>(S.k + size_t(i) * hd)[vec], k8);
+#pragma unroll
+            for (unsigned g = 0; g < kAttnMaxGroup; ++g) {
+                if (g < G) {
+                    const float4 qa = reinterpret_cast<const float4 *>(S.q + g * hd)[2 * vec];
+                    const float4 qb = reinterpret_cast<const float4 *>(S.q + g * hd)[2 * vec + 1];
+                    acc[g] = fmaf(qa.x, k8[0], acc[g]);
+                    acc[g] = fmaf(qa.y, k8[1], acc[g]);
+                    acc[g] = fmaf(qa.z, k8[2], acc[g]);
+                    acc[g] = fmaf(qa.w, k8[3], acc[g]);
+                    acc[g] = fmaf(qb.x, k8[4], acc[g]);
+                    acc[g] = fmaf(qb.y, k8[5], acc[g]);
+                    acc[g] = fmaf(qb.z, k8[6], acc[g]);
+                    acc[g] = fmaf(qb.w, k8[7], acc[g]);
+                }
+            }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) p[t] = s * a.scale;
-    }
-    __syncthreads();
-    float mx = -INFINITY;
-    for (unsigned t = threadIdx.x; t < T; t += kAttnThreads) mx = fmaxf(mx, p[t]);
-    mx = warp_max(mx);
-    if (lane == 0) redf[warp] = mx;
-    __syncthreads();
-    mx = redf[0];
-    for (unsigned w = 1; w < nw; ++w) mx = fmaxf(mx, redf[w]);
-    __syncthreads();
-    float sum = 0.0f;
-    for (unsigned t = threadIdx.x; t < T; t += kAttnThreads) {
-        const float e = expf(p[t] - mx);
-        p[t] = e;
-        sum += e;
-    }
+        for (unsigned g = 0; g < kAttnMaxGroup; ++g) {
+            if (g < G) {
+                float s = acc[g];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) redf[warp] = sum;
-    __syncthreads();
-    sum = 0.0f;
-    for (unsigned w = 0; w < nw; ++w) sum += redf[w];
-    const float inv = 1.0f / sum;
-    for (unsigned e = threadIdx.x; e < hd; e += kAttnThreads) {
-        float acc = 0.0f;
-        for (unsigned t = 0; t < T; ++t) {
-            const float vv = t == pos ? half_bits_to_float(float_to_half_bits(a.v[size_t(kvh) * hd + e]))
-                                        : half_bits_to_float(vc[size_t(t) * hd + e]);
-            acc = fmaf(p[t], vv, acc);
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (lane == 0) S.p[g * C + i] = s * a.scale;
+            }
         }
-        a.y[size_t(h) * hd + e] = acc * inv;
     }
+    __syncthreads();
+    // chunk softmax statistics: warp w takes query heads w, w + 8, ...
+    for (unsigned g = warp; g < G; g += kAttnWarps) {
+        float mx = -INFINITY;
+        for (unsigned i = lane; i < cn; i += 32) mx = fmaxf(mx, S.p[g * C + i]);
+        mx = warp_max(mx);
+        float sum = 0.0f;
+        for (unsigned i = lane; i < cn; i += 32) {
+            const float e = expf(S.p[g * C + i] - mx);
+            S.p[g * C + i] = e;
+            sum += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            S.ml[2 * g] = mx;
+            S.ml[2 * g + 1] = sum;
+        }
+    }
+    __syncthreads();
+    // unnormalised chunk output: item (g, vec) per thread
+    const size_t part_stride = size_t(hd) + 2;
+    for (unsigned it = threadIdx.x; it < G * nvec; it += kAttnThreads) {
+        const unsigned g = it / nvec, vec = it % nvec;
+        float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (unsigned i = 0; i < cn; ++i) {
+            float v8[8];
+            half8_to_float(reinterpret_cast<const uint4 *>(S.v + size_t(i) * hd)[vec], v8);
+            const float p = S.p[g * C + i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = fmaf(p, v8[j], o[j]);
+        }
+        float *dst = a.part + (size_t(kvh * G + g) * a.max_chunks + chunk) * part_stride;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[vec * 8 + j] = o[j];
+        if (vec == 0) {
+            dst[hd] = S.ml[2 * g];
+            dst[hd + 1] = S.ml[2 * g + 1];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned done = atomicAdd(a.counters + kvh, 1u);
+        last_s = done == n_chunks - 1;
+        if (last_s) a.counters[kvh] = 0;  // every other chunk has counted: ready for the next launch
+    }
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    // merge weights per (query head, chunk): warp g reduces over the chunks
+    for (unsigned g = warp; g < G; g += kAttnWarps) {
+        const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride;
+        float M = -INFINITY;
+        for (unsigned c = lane; c < n_chunks; c += 32) M = fmaxf(M, __ldcg(base + c * part_stride + hd));
+        M = warp_max(M);
+        float L = 0.0f;
+        for (unsigned c = lane; c < n_chunks; c += 32) {
+            const float e = expf(__ldcg(base + c * part_stride + hd) - M);
+            S.w[g * a.max_chunks + c] = e;
+            L = fmaf(e, __ldcg(base + c * part_stride + hd + 1), L);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = 1.0f / L;
+        for (unsigned c = lane; c < n_chunks; c += 32) S.w[g * a.max_chunks + c] *= inv;
+    }
+    __syncthreads();
+    for (unsigned it = threadIdx.x; it < G * hd; it += kAttnThreads) {
+        const unsigned g = it / hd, e = it % hd;
+        const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride + e;
+        const float *w = S.w + g * a.max_chunks;
+        float y = 0.0f;
+#pragma unroll 4
+        for (unsigned c = 0; c < n_chunks; ++c) y = fmaf(w[c], __ldcg(base + c * part_stride), y);
+        a.y[size_t(kvh * G + g) * hd + e] = y;
+    }
+}
+
+unsigned attn_chunk(unsigned kv_ctx, unsigned n_kv_head, unsigned sms) {
+    // about one CTA per SM over the whole slot, at least 16 positions per CTA
+    const unsigned per = (kv_ctx * n_kv_head + sms - 1) / sms;
+    return per <= 16 ? 16u : (per + 15) / 16 * 16;
+}
+
+size_t attn_smem_bytes(unsigned n_head, unsigned n_kv_head, unsigned head_dim, unsigned chunk, unsigned max_chunks) {
+    const size_t G = n_head / n_kv_head;
+    return 2 * size_t(chunk) * head_dim * 2 + sizeof(float) * (G * head_dim + G * chunk + 2 * G + G * max_chunks);
 }
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl) {
@@ -87,9 +229,9 @@ cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl) {
         attr_set = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_head);
+    cfg.gridDim = dim3(a.max_chunks, a.n_kv_head);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = sizeof(float) * (a.head_dim + a.kv_ctx);
+    cfg.dynamicSmemBytes = attn_smem_bytes(a.n_head, a.n_kv_head, a.head_dim, a.chunk, a.max_chunks);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -39,6 +39,10 @@ struct AttnArgs {
     float *y = nullptr;
     uint16_t *kcache = nullptr, *vcache = nullptr;  // [n_kv_head][kv_ctx][head_dim] F16 each
     float scale = 0.0f;
+    unsigned chunk = 16, max_chunks = 0;            // positions per CTA; CTAs per KV head (kv_ctx / chunk)
+    float *part = nullptr;      // [n_head][max_chunks][head_dim + 2] chunk outputs, maximum, sum
+    unsigned *counters = nullptr;  // [n_kv_head] finished chunks (zero between launches)
+    unsigned *err = nullptr;       // set when a bounded wait for the chunk copies ran out
 };
 
 // fill in the shared-memory plan of a pass (stages, result buffers) and return its dynamic shared memory
@@ -59,11 +63,14 @@ cudaError_t launch_conv(const float *x, const float *w, float *y, const float *s
                         unsigned use_silu, cudaStream_t st, bool pdl);
 cudaError_t launch_rope(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows,
                         cudaStream_t st, bool pdl);
-cudaError_t launch_argmax(const float *x, unsigned n, float *y, cudaStream_t st, bool pdl);
+cudaError_t launch_argmax(const float *x, unsigned n, float *y, unsigned long long *slot, unsigned *counter,
+                          cudaStream_t st, bool pdl);
 cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx, float *y, unsigned *status,
                            cudaStream_t st, bool pdl);
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
+unsigned attn_chunk(unsigned kv_ctx, unsigned n_kv_head, unsigned sms);
+size_t attn_smem_bytes(unsigned n_head, unsigned n_kv_head, unsigned head_dim, unsigned chunk, unsigned max_chunks);
 cudaError_t launch_trace_stamp(unsigned long long *slot, cudaStream_t st);
 cudaError_t launch_trace_write(const unsigned long long *stamps, const uint32_t *tags, unsigned n_events,
                                float *log, cudaStream_t st);

@@ -83,29 +83,53 @@ __global__ void rope_kernel(const float *x, const float *cs, float *y, unsigned 
 }
 
 // ---- ARGMAX (extension): first index of the maximum ---------------------------------------------------------------
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *x, unsigned n, float *y) {
-    __shared__ float bv[32];
-    __shared__ unsigned bi[32];
+// Order-preserving key of a float (NaN lowest, so it never wins) packed with the complement of the index: the
+// largest packed value is the largest value at its first index.
+__device__ __forceinline__ unsigned long long argmax_key(float v, unsigned i) {
+    const unsigned u = v == 0.0f ? 0u : __float_as_uint(v);  // -0 and +0 compare equal
+    const unsigned key = isnan(v) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+    return (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - i);
+}
+
+// Each CTA reduces a strided share of x to one packed key and folds it into the combine slot with a 64-bit
+// atomicMax; the last CTA to finish (counter) writes the result and clears slot and counter for the next launch.
+// Like a scalar scan with `>` from index 0: a NaN at index 0 keeps index 0, other NaNs are skipped.
+__global__ void __launch_bounds__(256) argmax_kernel(const float *x, unsigned n, float *y, unsigned long long *slot,
+                                                     unsigned *counter) {
+    __shared__ unsigned long long red[8];
+    __shared__ bool last_s;
     pdl_wait();
-    float best = -INFINITY;
-    unsigned idx = 0xffffffffu;
-    for (unsigned i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = x[i];
-        if (v > best || (idx == 0xffffffffu)) { best = v; idx = i; }
+    unsigned long long best = 0;
+    const unsigned n4 = n / 4, stride = gridDim.x * blockDim.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 v = __ldg(x4 + i);
+        best = max(best, argmax_key(v.x, 4 * i));
+        best = max(best, argmax_key(v.y, 4 * i + 1));
+        best = max(best, argmax_key(v.z, 4 * i + 2));
+        best = max(best, argmax_key(v.w, 4 * i + 3));
     }
+    for (unsigned i = 4 * n4 + blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        best = max(best, argmax_key(x[i], i));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const unsigned oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
-    }
-    if (threadIdx.x % 32 == 0) { bv[threadIdx.x / 32] = best; bi[threadIdx.x / 32] = idx; }
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (unsigned w = 1; w < (blockDim.x + 31) / 32; ++w)
-            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
-        y[0] = __uint_as_float(idx);
-        y[1] = best;
+        for (unsigned w = 1; w < blockDim.x / 32; ++w) best = max(best, red[w]);
+        atomicMax(slot, best);
+        __threadfence();
+        last_s = atomicAdd(counter, 1u) == gridDim.x - 1;
+        if (last_s) {
+            __threadfence();
+            const unsigned long long r = atomicExch(slot, 0ull);
+            *counter = 0;
+            unsigned idx = 0xffffffffu - unsigned(r & 0xffffffffu);
+            if (isnan(x[0]) || r == 0) idx = 0;  // NaN first (or every value NaN): index 0, as the scan keeps it
+            const float v = x[idx];
+            y[0] = __uint_as_float(idx);
+            y[1] = v;
+        }
     }
 }
 
@@ -181,10 +205,14 @@ cudaError_t launch_rope(const float *x, const float *cs, float *y, unsigned n_di
     return cudaLaunchKernelEx(&cfg, rope_kernel, x, cs, y, n_dims, ne0, rows);
 }
 
-cudaError_t launch_argmax(const float *x, unsigned n, float *y, cudaStream_t st, bool pdl) {
+cudaError_t launch_argmax(const float *x, unsigned n, float *y, unsigned long long *slot, unsigned *counter,
+                          cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(1024), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, argmax_kernel, x, n, y);
+    const unsigned per_cta = 256 * 4 * 4;  // about four float4 per thread
+    unsigned grid = (n + per_cta - 1) / per_cta;
+    grid = grid < 1 ? 1 : (grid > 148 ? 148 : grid);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, x, n, y, slot, counter);
 }
 
 cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx, float *y, unsigned *status,

@@ -150,6 +150,7 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
     Ctx C{cmds, n_cmds, lim, plan};
     DeferredNorm nd;
     int nd_pass = -1;          // index of the deferred RMSNORM's Nop pass
+    bool nd_dirty = false;     // a pass after the deferred RMSNORM wrote its x or weight
     std::vector<std::pair<size_t, size_t>> writes;
     unsigned c = 0;
     auto reject = [&](unsigned idx, const char *why) {
@@ -263,6 +264,7 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
                 nd.eps = bits_to_float(cmd[5]);
                 nd.cmd = c;
                 nd_pass = int(plan.passes.size());
+                nd_dirty = false;
             } else {
                 p.kind = PassKind::Elementwise;
             }
@@ -397,7 +399,7 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
             const unsigned nh = cmd[1] & 0xffu, nkv = (cmd[1] >> 8) & 0xffu, hd = (cmd[1] >> 16) * 16u;
             const unsigned slot = cmd[7];
             const size_t slot_bytes = size_t(nkv) * lim.kv_ctx * hd * 2 * 2;
-            if (nh == 0 || nkv == 0 || nh % nkv || hd == 0 || hd > 512 || cmd[2] % 16 || cmd[3] % 16 || cmd[4] % 16 ||
+            if (nh == 0 || nkv == 0 || nh % nkv || nh / nkv > 16 || hd == 0 || hd > 512 || cmd[2] % 16 || cmd[3] % 16 || cmd[4] % 16 ||
                 cmd[5] % 16 || cmd[6] % 16 || lim.kv_ctx == 0 || !C.act(cmd[6], 1) ||
                 !C.act(cmd[2], size_t(nh) * hd) || !C.act(cmd[3], size_t(nkv) * hd) ||
                 !C.act(cmd[4], size_t(nkv) * hd) || !C.act(cmd[5], size_t(nh) * hd) ||
@@ -434,17 +436,22 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
             break;
         }
         p.count = advance;
-        // a write to the deferred norm's x or weight before its consumers: store the norm at its command instead
+        // A consumer of the deferred norm computes it from x and the weight as they are when it runs. When x or the
+        // weight changes between the RMSNORM and a consumer (a write by an earlier pass, or by the consumer itself,
+        // whose CTAs write while others still read), the norm is stored at its command and consumers read that row.
+        // Writes after the last consumer cost nothing.
         if (nd.valid && nd_pass >= 0 && p.kind != PassKind::Nop) {
             pass_writes(p, writes);
-            for (const auto &w : writes) {
-                if (ranges_meet(w.first, w.second, nd.x_off, nd.n) ||
-                    ((nd.flags & 2u) == 0 && ranges_meet(w.first, w.second, nd.w_off, nd.n))) {
-                    nd.materialize = true;
-                    plan.passes[size_t(nd_pass)].nd_store = true;
-                    plan.passes[size_t(nd_pass)].nd = nd;
-                }
+            bool hits = false;
+            for (const auto &w : writes)
+                hits = hits || ranges_meet(w.first, w.second, nd.x_off, nd.n) ||
+                       ((nd.flags & 2u) == 0 && ranges_meet(w.first, w.second, nd.w_off, nd.n));
+            if (p.kind == PassKind::Gemv && p.from_nd && (nd_dirty || hits)) {
+                nd.materialize = true;
+                plan.passes[size_t(nd_pass)].nd_store = true;
+                plan.passes[size_t(nd_pass)].nd = nd;
             }
+            nd_dirty = nd_dirty || hits;
         }
         if (p.kind == PassKind::Nop && op == 2) p.nd = nd;
         plan.passes.push_back(p);

@@ -64,7 +64,8 @@ extern "C" {
 /* [12, n_head | n_kv_head << 8 | (head_dim / 16) << 16, q_off, k_off, v_off, y_off, pos_off, slot]: pos = act[pos_off]
  * (uint32 bits, so a replayed graph reads each token's position from act); stores this token's k, v (F16) at
  * position pos of KV slot `slot`, then y = softmax(q K^T / sqrt(head_dim)) V over positions 0..pos. A pos outside the
- * slot writes nothing and makes b200q_run / b200q_synchronize return B200Q_ERR_ARG. */
+ * slot writes nothing and makes b200q_run / b200q_synchronize return B200Q_ERR_ARG. At most 16 query heads per KV
+ * head, head_dim <= 512. */
 #define B200Q_OP_ATTN 12u
 /* [13, n, x_off, y_off, 0, 0, 0, 0]: y[0] = first index of the maximum (uint32 bits), y[1] = the maximum */
 #define B200Q_OP_ARGMAX 13u
@@ -175,6 +176,11 @@ B200Q_API int b200q_act_fill(b200q_ctx *ctx, size_t off, float value, size_t n);
 B200Q_API int b200q_state_write(b200q_ctx *ctx, size_t row, const float *src, size_t rows);
 B200Q_API int b200q_state_read(b200q_ctx *ctx, size_t row, float *dst, size_t rows);
 B200Q_API int b200q_kv_write(b200q_ctx *ctx, size_t byte_off, const void *src, size_t bytes);
+/* Stream-ordered act copies for a per-token loop: enqueued on the context stream behind the lists already launched,
+ * no wait. The host buffer must stay untouched (write) or unread (read) until b200q_synchronize() returns; page-locked
+ * host memory makes the copy asynchronous, pageable memory may make the call wait. */
+B200Q_API int b200q_act_write_async(b200q_ctx *ctx, size_t off, const float *src, size_t n);
+B200Q_API int b200q_act_read_async(b200q_ctx *ctx, size_t off, float *dst, size_t n);
 
 /* Run one command list (reference gemvqc16 contract, see the top of this header); synchronous: returns once the
  * GPU finished the list. n_cmds = 0 writes the feature words into act[0..2]. */
@@ -200,7 +206,8 @@ typedef struct b200q_pass_info {
     uint32_t n_cmds;      /* commands the pass consumes */
     uint32_t kind;        /* B200Q_PASS_* */
     uint32_t n_members;   /* GEMVs in the pass */
-    uint32_t fused_norm;  /* 1: the GEMVs quantize a deferred RMSNORM's row */
+    uint32_t fused_norm;  /* 1: the GEMVs quantize a deferred RMSNORM's row, computed in the pass; 2: the row stored at
+                           * the RMSNORM command (its x or weight changes before this pass) */
 } b200q_pass_info;
 #define B200Q_PASS_GEMV 1u
 #define B200Q_PASS_ELEMENTWISE 2u

@@ -898,7 +898,7 @@ ORC_API int orc_run_list(float *act, size_t act_floats, float *state, size_t sta
             unsigned pos = 0xffffffffu;
             if (in_act(&M, c[6], 1)) memcpy(&pos, &M.act[c[6]], 4);
             const size_t slot_elems = (size_t)nkv * kv_ctx * hd; /* K, then V */
-            if (nh == 0 || nkv == 0 || nh % nkv || hd == 0 || hd > 512 || c[2] % 16 || c[3] % 16 || c[4] % 16 ||
+            if (nh == 0 || nkv == 0 || nh % nkv || nh / nkv > 16 || hd == 0 || hd > 512 || c[2] % 16 || c[3] % 16 || c[4] % 16 ||
                 c[5] % 16 || c[6] % 16 || pos >= kv_ctx || !in_act(&M, c[2], (size_t)nh * hd) || !in_act(&M, c[3], (size_t)nkv * hd) ||
                 !in_act(&M, c[4], (size_t)nkv * hd) || !in_act(&M, c[5], (size_t)nh * hd) ||
                 ((size_t)slot + 1) * slot_elems * 2 * sizeof(uint16_t) > kv_bytes) {

@@ -150,6 +150,27 @@ def test_fused_ffn_block_config1(ctx, b2, synth, orc):
     assert np.array_equal(_bits(got[XIN:XN]), _bits(ref[XIN:XN]))
 
 
+def test_deferred_norm_of_a_row_that_changes_before_its_consumer(ctx, b2, synth, orc):
+    """RMSNORM (deferred) of x, then an ADD that rewrites x, then the GEMV that reads the norm: the norm is the one of
+    x at the RMSNORM command (stored there), as the reference's on-chip row is."""
+    ctx.reset_weights()
+    r = rng(56)
+    H, R = 2560, 2048
+    ws = _weights_and_list(b2, synth, ctx, [(2, R, H)], r)
+    (h,) = list(ws)
+    XIN, GAIN, OTHER, XN, Y = 0, H, 2 * H, 3 * H, 4 * H
+    act = np.zeros(Y + R, np.float32)
+    act[XIN:XIN + H] = synth.activation(r, H)
+    act[GAIN:GAIN + H] = r.normal(1, 0.1, H).astype(np.float32)
+    act[OTHER:OTHER + H] = synth.activation(r, H)
+    cl = b2.cmd_list(b2.rmsnorm(H, XIN, GAIN, XN, 1e-6, flags=b2.NORM_DEFER), b2.add(H, XIN, OTHER, XIN),
+                     b2.gemv(2, R, H, h, XN, Y))
+    st, passes = b2.plan(cl)
+    assert st == 0 and passes[-1]["stored_norm"]
+    got, ref = _compare_list(ctx, orc, cl, ws, act, act.size, exact=True)
+    assert np.array_equal(_bits(got[Y:Y + R]), _bits(ref[Y:Y + R]))
+
+
 CHAINS = ["q8_0-to-q4_0", "q4_0-add-to-q4_1", "p8-to-q8_0", "q8_0-norm-to-q4_0", "q4_0-l2norm-to-q4_1"]
 
 

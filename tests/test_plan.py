@@ -118,3 +118,23 @@ def test_random_lists_status_matches_oracle(b2, synth, orc):
         assert st_plan == st_orc, (trial, cl.reshape(-1, 8))
         agree += 1
     assert agree == 400
+
+
+def test_deferred_norm_stored_only_when_x_changes_before_a_consumer(b2):
+    """A deferred RMSNORM is computed inside its consumer GEMV pass unless its x or weight changes between the
+    command and a consumer (an earlier pass, or the consumer itself writing them): then it is stored at the
+    command. Writes after the last consumer (the residual ADD of a layer) leave it fused."""
+    g = b2.gemv
+    norm = b2.rmsnorm(256, X, 256, 512, 1e-6, flags=b2.NORM_DEFER)
+    cases = {
+        "write after the consumer": (b2.cmd_list(norm, g(2, 64, 256, 1000, 512, Y), b2.add(256, X, Z, X)), False),
+        "x written before": (b2.cmd_list(norm, b2.add(256, X, Z, X), g(2, 64, 256, 1000, 512, Y)), True),
+        "weight written before": (b2.cmd_list(norm, b2.add(256, 256, Z, 256), g(2, 64, 256, 1000, 512, Y)), True),
+        "consumer writes x": (b2.cmd_list(norm, g(2, 64, 256, 1000, 512, X)), True),
+        "unrelated write": (b2.cmd_list(norm, b2.add(256, Z, Z, Z + 256), g(2, 64, 256, 1000, 512, Y)), False),
+    }
+    for name, (cl, stored) in cases.items():
+        st, passes = b2.plan(cl)
+        assert st == 0, name
+        gp = [p for p in passes if p["kind"] == "gemv"][0]
+        assert gp["fused_norm"] and gp["stored_norm"] == stored, name
