@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     const unsigned G = a.n_head / a.n_kv_head, hd = a.head_dim, C = a.chunk, nvec = hd / 8;
     const AttnSmem S = attn_smem(attn_sm, G, hd, C, a.max_chunks);
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     const unsigned pos = __float_as_uint(*a.pos);
     if (pos >= a.kv_ctx) {
         if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, 2u);

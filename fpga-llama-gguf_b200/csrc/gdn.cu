@@ -5,30 +5,36 @@
 // optionally with q/k L2-normalized per head (RMSNORM with flags 3), the gates beta = sigmoid(beta),
 // g = softplus(g + dt) * a, and the gated output (RMSNORM(y) * w) * silu(z) per head.
 //
-// One CTA per value head, one thread per state row: the thread holds its 128-float row in registers for the whole
-// step (read once, written once) and sums both dot products in index order with IEEE-rounded FP32 adds, the CPU
-// reference's order, so the new state and y match it bit for bit whenever exp() does.
+// One cluster of 4 CTAs per value head, 32 state rows per CTA, one thread per state row: the thread holds its
+// 128-float row in registers for the whole step (read once, written once) and sums both dot products in index
+// order with IEEE-rounded FP32 adds, the CPU reference's order, so the new state and y match it bit for bit
+// whenever exp() does. The per-head sums of squares (L2 of q and k, RMS of y) are taken as four 32-value
+// shuffle-tree sums added in row order; each CTA forms the q / k sums itself and the y sum from the four CTAs'
+// parts, exchanged through distributed shared memory.
 #include "launch.h"
+#include "pipeline.cuh"
 #include "quant.cuh"
 
 namespace b200q {
 
-__device__ __forceinline__ double cta128_sum(double v, double *red) {
+constexpr unsigned kGdnSplit = 4;  // CTAs per head (one cluster), 32 state rows each
+
+__device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    __syncthreads();
-    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
-    __syncthreads();
-    return ((red[0] + red[1]) + red[2]) + red[3];
+    return v;
 }
 
-__global__ void __launch_bounds__(128) gdn_kernel(const GdnArgs a) {
+__global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(32) gdn_kernel(const GdnArgs a) {
     __shared__ float qs[128], ks[128];
-    __shared__ double red[4];
+    __shared__ double ysum[kGdnSplit];  // part p of the head's sum of y^2, written by CTA p into every CTA
     __shared__ float gate[2];
+    cluster_arrive_relaxed();
     pdl_wait();
-    const unsigned h = blockIdx.x, kh = h % a.hk, j = threadIdx.x;
-    // state row of this thread: issue the loads first (the state is not written by earlier commands' other rows)
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    const unsigned part = cluster_rank(), h = blockIdx.x / kGdnSplit, kh = h % a.hk, lane = threadIdx.x;
+    const unsigned j = part * 32 + lane;
+    // state row of this thread: issue the loads first
     const float4 *src = reinterpret_cast<const float4 *>(a.state_in + (size_t(h) * 128 + j) * 128);
     float row[128];
 #pragma unroll
@@ -39,16 +45,33 @@ __global__ void __launch_bounds__(128) gdn_kernel(const GdnArgs a) {
         row[4 * i + 2] = v.z;
         row[4 * i + 3] = v.w;
     }
-    float qv = a.q[kh * 128 + j], kv = a.k[kh * 128 + j];
-    if (a.l2) {  // 1 / fmaxf(sqrtf(float(sum x^2)), eps), x * scale (gemvq_ref.h:309-324 with flags 3)
-        const double sq = cta128_sum(double(fmul(qv, qv)), red);
-        const double sk = cta128_sum(double(fmul(kv, kv)), red);
-        qv = fmul(qv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sq)), a.l2_eps)));
-        kv = fmul(kv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sk)), a.l2_eps)));
+    float qv[kGdnSplit], kv[kGdnSplit];
+#pragma unroll
+    for (unsigned w = 0; w < kGdnSplit; ++w) {
+        qv[w] = a.q[kh * 128 + 32 * w + lane];
+        kv[w] = a.k[kh * 128 + 32 * w + lane];
     }
-    qs[j] = qv;
-    ks[j] = kv;
-    if (j == 0) {
+    if (a.l2) {  // 1 / fmaxf(sqrtf(float(sum x^2)), eps), x * scale (gemvq_ref.h:309-324 with flags 3)
+        double sq = 0.0, sk = 0.0;
+#pragma unroll
+        for (unsigned w = 0; w < kGdnSplit; ++w) {
+            sq = w == 0 ? warp_sum_d(double(fmul(qv[w], qv[w]))) : sq + warp_sum_d(double(fmul(qv[w], qv[w])));
+            sk = w == 0 ? warp_sum_d(double(fmul(kv[w], kv[w]))) : sk + warp_sum_d(double(fmul(kv[w], kv[w])));
+        }
+        const float iq = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sq)), a.l2_eps));
+        const float ik = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sk)), a.l2_eps));
+#pragma unroll
+        for (unsigned w = 0; w < kGdnSplit; ++w) {
+            qv[w] = fmul(qv[w], iq);
+            kv[w] = fmul(kv[w], ik);
+        }
+    }
+#pragma unroll
+    for (unsigned w = 0; w < kGdnSplit; ++w) {
+        qs[32 * w + lane] = qv[w];
+        ks[32 * w + lane] = kv[w];
+    }
+    if (lane == 0) {
         float g = a.g[h], b = a.beta[h];
         if (a.dt) {  // gemvqc_gdn.h:265-280: g = softplus(g + dt) * a, beta = sigmoid(beta)
             g = fmul(softplus_f32(fadd(g, a.dt[h])), a.a[h]);
@@ -57,7 +80,7 @@ __global__ void __launch_bounds__(128) gdn_kernel(const GdnArgs a) {
         gate[0] = exp_f32(g);
         gate[1] = b;
     }
-    __syncthreads();
+    __syncwarp();
     const float decay = gate[0], beta = gate[1];
     float dot = 0.0f;
 #pragma unroll
@@ -76,8 +99,12 @@ __global__ void __launch_bounds__(128) gdn_kernel(const GdnArgs a) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) dst[i] = make_float4(row[4 * i], row[4 * i + 1], row[4 * i + 2], row[4 * i + 3]);
     float yv = fmul(out, a.scale);
+    cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
     if (a.z) {  // (y * rms scale) * w, then silu(z) * that (RMSNORM + SILU_MUL, gemvqc_gdn.h:284-346)
-        const double s = cta128_sum(double(fmul(yv, yv)), red);
+        const double mine = warp_sum_d(double(fmul(yv, yv)));
+        if (lane < kGdnSplit) st_cluster_f64(peer_smem(smem_addr(&ysum[part]), lane), mine);
+        cluster_sync();
+        const double s = ((ysum[0] + ysum[1]) + ysum[2]) + ysum[3];
         const float sc = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(s, 128.0)), a.rms_eps)));
         const float nv = fmul(fmul(yv, sc), a.wn[j]);
         yv = fmul(silu_f32(a.z[h * 128 + j]), nv);
@@ -87,8 +114,8 @@ __global__ void __launch_bounds__(128) gdn_kernel(const GdnArgs a) {
 
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.hv);
-    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3(a.hv * kGdnSplit);
+    cfg.blockDim = dim3(32);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

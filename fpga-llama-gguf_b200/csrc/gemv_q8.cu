@@ -194,25 +194,6 @@ __device__ __forceinline__ void prefetch_panel(const GemvArgs &a, unsigned item,
 }
 
 // ---- x preparation, split over a cluster of kXCluster CTAs ---------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Address of the same shared-memory offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t peer_smem(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
-    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-                 "r"(v.w)
-                 : "memory");
-}
 __device__ __forceinline__ float4 ldg_act4(const float *p) {
     return *reinterpret_cast<const float4 *>(p);
 }
@@ -624,6 +605,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const XImage X = carve_ximage(smem, a.n);
     pdl_wait();
+    pdl_launch_dependents();
     quantize_cta(a.x, a.n, a.act, a.norm_w, a.norm_eps, a.norm_mode, X);
     for (unsigned i = threadIdx.x; i < a.n / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(a.q)[i] = reinterpret_cast<const uint4 *>(X.q)[i];

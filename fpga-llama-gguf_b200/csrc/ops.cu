@@ -14,6 +14,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
     __shared__ double red[32];
     __shared__ float scale_s;
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     const float *xr = x + size_t(blockIdx.x) * stride;
     float *yr = y + size_t(blockIdx.x) * n;
     const float s = cta_norm_scale(xr, n, eps, flags & 1u, red, &scale_s);
@@ -26,6 +27,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
 // ---- ADD / MUL / SILU_MUL / UNARY ---------------------------------------------------------------------------------
 __global__ void ew_kernel(const EwArgs a) {
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < a.n; e += gridDim.x * blockDim.x) {
         const size_t ai = a.row ? size_t(e / a.row) * a.stride + e % a.row : e;
         const float av = a.a[ai];
@@ -46,6 +48,7 @@ __global__ void ew_kernel(const EwArgs a) {
 __global__ void conv_kernel(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
                             unsigned use_silu) {
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= ch) return;
     const float s0 = s_src[3 * c], s1 = s_src[3 * c + 1], s2 = s_src[3 * c + 2], xv = x[c];
@@ -63,6 +66,7 @@ __global__ void conv_kernel(const float *x, const float *w, float *y, const floa
 // ---- ROPE, NEOX pairing --------------------------------------------------------------------------------------------
 __global__ void rope_kernel(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows) {
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     const unsigned half = n_dims / 2;
     const unsigned per_row = half + (ne0 - n_dims);
     for (unsigned t = blockIdx.x * blockDim.x + threadIdx.x; t < rows * per_row; t += gridDim.x * blockDim.x) {
@@ -99,6 +103,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *x, unsigned n,
     __shared__ unsigned long long red[8];
     __shared__ bool last_s;
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     unsigned long long best = 0;
     const unsigned n4 = n / 4, stride = gridDim.x * blockDim.x;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
@@ -136,6 +141,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *x, unsigned n,
 // ---- GET_ROW (extension): one dequantized row, index read from act (ggml dequantize_row_q4_0 / q8_0) -------------
 __global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *idx_f, float *y, unsigned *status) {
     pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     const unsigned row = __float_as_uint(*idx_f);
     if (row < w.row0 || row >= w.row0 + w.rows) {
         if (blockIdx.x == 0 && threadIdx.x == 0 && status) atomicExch(status, 1u);
