@@ -112,6 +112,14 @@ struct b200q_ctx {
     std::string err;
     int world = 1, rank = 0;
     nccl_comm comm = nullptr;
+    // row-sharded passes without a collective: the peers' act and sync words (IPC-mapped), this rank's sync words,
+    // the next free sync slot of the list and the wait not yet handed to a kernel
+    bool peer_ok = false;
+    float *peer_act[kMaxPeers] = {};
+    unsigned *peer_sync[kMaxPeers] = {};
+    unsigned *sync = nullptr;  // kSyncWords: ready and data words per (slot, rank), CTA and launch counts per slot
+    unsigned slot_next = 0;
+    PeerWait pending;          // sharded launches whose rows no kernel has waited for yet
     bool pdl = true;
     unsigned launches = 0;  // kernels launched by the last executed list
     std::mutex mu;
@@ -172,6 +180,21 @@ struct Range {
     size_t n;
 };
 
+// The wait for the peers' rows of the last sharded pass, handed to the next kernel launched (which waits for them
+// after its wait on the previous kernel); every kernel after it is ordered behind it.
+PeerWait take_wait(b200q_ctx *c) {
+    PeerWait w = c->pending;
+    c->pending.n = 0;
+    return w;
+}
+// ... or as a kernel of its own, before a copy (or the end of the list) that no kernel covers
+int flush_wait(b200q_ctx *c) {
+    if (c->pending.n == 0) return 0;
+    CUDA_TRY(c, launch_peer_wait(take_wait(c), c->stream, c->pdl));
+    ++c->launches;
+    return 0;
+}
+
 // An input that a kernel of the same launch writes with a different element mapping: copy it first.
 const float *snap_if(b200q_ctx *c, const float *in, size_t n, const std::vector<Range> &writes, const float *same_ok,
                      int &rc) {
@@ -182,6 +205,7 @@ const float *snap_if(b200q_ctx *c, const float *in, size_t n, const std::vector<
         hit = true;
     }
     if (!hit) return in;
+    if ((rc = flush_wait(c))) return in;
     if (c->snap_used + n > kSnapFloats) {
         rc = set_err(c, B200Q_ERR_NOMEM, "snapshot scratch full");
         return in;
@@ -286,6 +310,7 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
         q.d = c->xd;
         q.s = c->xs;
         q.b = c->xb;
+        q.pw = take_wait(c);
         CUDA_TRY(c, launch_quantize(q, c->stream));
         ++c->launches;
         a.xq = c->xq;
@@ -307,10 +332,36 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
     a.n_units = u;
     a.item_start[u] = items;
     a.err = c->dstatus + 1;
+    const unsigned slot0 = c->slot_next;
+    // a launch with sharded members takes a sync slot (peer stores, ready / data flags)
+    auto take_slot = [&](GemvArgs &g) -> int {
+        if (!shard || dbg || !c->peer_ok) return 0;
+        bool any = false;
+        for (unsigned k = 0; k < g.n_units; ++k) {
+            const int pk = g.unit_pair[k];
+            const GemvMemberArgs &out = g.m[pk >= 0 ? unsigned(pk) : g.unit_member[k]];
+            any = any || out.w.rows != out.total_rows;
+        }
+        if (!any) return 0;
+        if (c->slot_next >= kSyncSlots) return set_err(c, B200Q_ERR_ARG, "too many sharded GEMV launches in a list");
+        PeerSync &ps = g.ps;
+        ps.act = c->act;
+        for (int r = 0; r < c->world; ++r) {
+            ps.peer_act[r] = c->peer_act[r];
+            ps.peer_sync[r] = c->peer_sync[r];
+        }
+        ps.sync = c->sync;
+        ps.world = unsigned(c->world);
+        ps.rank = unsigned(c->rank);
+        ps.slot = c->slot_next++;
+        return 0;
+    };
     size_t smem = 0;
     if (kq) {
         plan_gemv_kq(a, smem);
         const unsigned grid = std::min(items, unsigned(c->sms) * (smem <= 113 * 1024 ? 2u : 1u));
+        if ((rc = take_slot(a))) return rc;
+        a.pw = take_wait(c);
         CUDA_TRY(c, launch_gemv_kq(a, grid, smem, c->stream, c->pdl));
         ++c->launches;
     } else {
@@ -346,11 +397,21 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
             // whole clusters (the x preparation is split over a cluster's CTAs)
             const unsigned cl = gemv_q8_cluster();
             const unsigned grid = std::min((gi + cl - 1) / cl * cl, gemv_q8_resident_ctas(fa, fb, smem, c->stream));
+            if ((rc = take_slot(g))) return rc;
+            g.pw = take_wait(c);
             CUDA_TRY(c, launch_gemv_q8(g, fa, fb, grid, smem, c->stream, c->pdl));
             ++c->launches;
         }
     }
-    if (shard && !dbg) {
+    if (shard && !dbg && c->peer_ok) {
+        // every launch stored its sharded rows into the peers: the next kernel waits for theirs
+        c->pending.sync = c->sync;
+        c->pending.slot0 = slot0;
+        c->pending.n = c->slot_next - slot0;
+        c->pending.world = unsigned(c->world);
+        c->pending.rank = unsigned(c->rank);
+        c->pending.err = c->dstatus + 1;
+    } else if (shard && !dbg) {
         for (unsigned i = 0; i < nm; ++i) {
             const GemvMemberArgs &g = a.m[i];
             if (g.epi == EpiSwigluG || g.w.rows == mem[i].rows) continue;
@@ -376,6 +437,7 @@ int exec_elementwise(b200q_ctx *c, const Pass &p) {
         const float *wt = (cmd[7] & 2u) ? nullptr : snap_if(c, A + cmd[3], n, w, nullptr, rc);
         if (rc) return rc;
         CUDA_TRY(c, launch_rmsnorm(x, wt, y, n, rows, xs, *reinterpret_cast<const float *>(&cmd[5]), cmd[7] & 3u,
+                                   take_wait(c),
                                    c->stream, c->pdl));
         break;
     }
@@ -394,6 +456,7 @@ int exec_elementwise(b200q_ctx *c, const Pass &p) {
         e.a = snap_if(c, A + cmd[2], span, w, e.row ? nullptr : e.y, rc);
         if (!unary) e.b = snap_if(c, A + cmd[3], e.n, w, e.y, rc);
         if (rc) return rc;
+        e.pw = take_wait(c);
         CUDA_TRY(c, launch_ew(e, c->stream, c->pdl));
         break;
     }
@@ -405,7 +468,7 @@ int exec_elementwise(b200q_ctx *c, const Pass &p) {
         const float *wt = snap_if(c, A + cmd[3], size_t(4) * ch, w, nullptr, rc);
         const float *ss = snap_if(c, A + cmd[5], size_t(3) * ch, w, sd, rc);
         if (rc) return rc;
-        CUDA_TRY(c, launch_conv(x, wt, y, ss, sd, ch, cmd[7] & 1u, c->stream, c->pdl));
+        CUDA_TRY(c, launch_conv(x, wt, y, ss, sd, ch, cmd[7] & 1u, take_wait(c), c->stream, c->pdl));
         break;
     }
     case 10: {  // ROPE
@@ -415,7 +478,7 @@ int exec_elementwise(b200q_ctx *c, const Pass &p) {
         const float *x = snap_if(c, A + cmd[2], size_t(ne0) * rows, w, y, rc);
         const float *cs = snap_if(c, A + cmd[3], nd, w, nullptr, rc);
         if (rc) return rc;
-        CUDA_TRY(c, launch_rope(x, cs, y, nd, ne0, rows, c->stream, c->pdl));
+        CUDA_TRY(c, launch_rope(x, cs, y, nd, ne0, rows, take_wait(c), c->stream, c->pdl));
         break;
     }
     default: return set_err(c, B200Q_ERR_ARG, "unexpected element-wise opcode %u", p.op);
@@ -454,6 +517,7 @@ int exec_gdn(b200q_ctx *c, const Pass &p) {
         g.a = snap_if(c, A + ext2[1], g.hv, w, nullptr, rc);
     }
     if (rc) return rc;
+    g.pw = take_wait(c);
     CUDA_TRY(c, launch_gdn(g, c->stream, c->pdl));
     ++c->launches;
     DeferredNorm none;
@@ -500,6 +564,7 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         t.part = c->attn_part;
         t.counters = c->dstatus + kSyncAttnWord;
         t.err = c->dstatus + 1;
+        t.pw = take_wait(c);
         CUDA_TRY(c, launch_attn(t, c->stream, c->pdl));
     } else if (p.op == 13) {
         std::vector<Range> w{{A + cmd[3], 2}};
@@ -507,7 +572,7 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         if (rc) return rc;
         CUDA_TRY(c, launch_argmax(x, cmd[1], A + cmd[3],
                                   reinterpret_cast<unsigned long long *>(c->dstatus + kSyncArgmaxWord),
-                                  c->dstatus + kSyncArgmaxWord + 2, c->stream, c->pdl));
+                                  c->dstatus + kSyncArgmaxWord + 2, take_wait(c), c->stream, c->pdl));
     } else if (p.op == 14) {
         const WeightInfo *w = find_w(c, uint64_t(cmd[3]) | (uint64_t(cmd[4]) << 32));
         if (!w) return set_err(c, B200Q_ERR_ARG, "GET_ROW: unknown weight");
@@ -515,7 +580,7 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         std::vector<Range> wr{{y, cmd[2]}};
         const float *idx = snap_if(c, A + cmd[5], 1, wr, nullptr, rc);
         if (rc) return rc;
-        CUDA_TRY(c, launch_get_row(view_of(c, *w), cmd[2], idx, y, c->dstatus, c->stream, c->pdl));
+        CUDA_TRY(c, launch_get_row(view_of(c, *w), cmd[2], idx, y, c->dstatus, take_wait(c), c->stream, c->pdl));
     }
     ++c->launches;
     return 0;
@@ -560,6 +625,8 @@ int link_image(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link
 int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
     c->launches = 0;
+    c->slot_next = 0;
+    c->pending.n = 0;
     c->n_events = 0;
     c->host_tags.clear();
     const bool tr = plan.has_trace;
@@ -595,7 +662,7 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
             if (p.nd_store) {  // a deferred RMSNORM whose x or weight changes before its GEMVs: store its row now
                 const DeferredNorm &nd = p.nd;
                 CUDA_TRY(c, launch_rmsnorm(c->act + nd.x_off, c->act + nd.w_off, c->ndrow, nd.n, 1, nd.n, nd.eps,
-                                           nd.flags, c->stream, c->pdl));
+                                           nd.flags, take_wait(c), c->stream, c->pdl));
                 ++c->launches;
             }
             break;
@@ -603,6 +670,8 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
         if (rc) return rc;
         if (is_pass && (rc = stamp(c, tr, p.first, 2))) return rc;
     }
+    // the last sharded pass's rows from the peers are in act before the list ends
+    if ((rc = flush_wait(c))) return rc;
     if (tr) {
         const unsigned end_c = plan.status ? unsigned(plan.status - 1) : n_cmds;
         if ((rc = stamp(c, tr, end_c, 0))) return rc;
@@ -633,7 +702,7 @@ int check_device_status(b200q_ctx *c) {
     if (st[0] | st[1]) {
         const unsigned zero[2] = {0, 0};
         CUDA_TRY(c, cudaMemcpy(c->dstatus, zero, sizeof(zero), cudaMemcpyHostToDevice));
-        if (st[1]) return set_err(c, B200Q_ERR_TIMEOUT, "a pass gave up waiting for its weight tiles (bounded wait)");
+        if (st[1]) return set_err(c, B200Q_ERR_TIMEOUT, "a bounded wait ran out (weight tiles, or a peer GPU's rows)");
         if (st[0] & 2u) return set_err(c, B200Q_ERR_ARG, "ATTN: the position in act is outside the KV slot");
         return set_err(c, B200Q_ERR_ARG, "GET_ROW: the row index in act is outside the matrix");
     }
@@ -734,6 +803,11 @@ void b200q_destroy(b200q_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    for (unsigned p = 0; p < kMaxPeers; ++p) {
+        if (c->peer_act[p]) cudaIpcCloseMemHandle(c->peer_act[p]);
+        if (c->peer_sync[p]) cudaIpcCloseMemHandle(c->peer_sync[p]);
+    }
+    cudaFree(c->sync);
     if (c->comm && g_nccl.comm_destroy) g_nccl.comm_destroy(c->comm);
     cudaFree(c->warena);
     cudaFree(c->qimg[0]);
@@ -1098,6 +1172,40 @@ int b200q_unpack_row_host(const void *dev, unsigned rows, unsigned cols, unsigne
     return 0;
 }
 
+namespace {
+// Map every peer's act and flag words into this process (CUDA IPC; the handles travel through one NCCL all-gather).
+int setup_peers(b200q_ctx *c) {
+    const size_t words = kSyncWords;
+    CUDA_TRY(c, cudaMalloc(&c->sync, words * sizeof(unsigned)));
+    CUDA_TRY(c, cudaMemset(c->sync, 0, words * sizeof(unsigned)));
+    cudaIpcMemHandle_t mine[2];
+    CUDA_TRY(c, cudaIpcGetMemHandle(&mine[0], c->act));
+    CUDA_TRY(c, cudaIpcGetMemHandle(&mine[1], c->sync));
+    static_assert(sizeof(mine) % sizeof(float) == 0, "handles travel as floats");
+    const size_t n = sizeof(mine) / sizeof(float);
+    float *dev = nullptr;
+    CUDA_TRY(c, cudaMalloc(&dev, sizeof(mine) * (size_t(c->world) + 1)));
+    CUDA_TRY(c, cudaMemcpy(dev, mine, sizeof(mine), cudaMemcpyHostToDevice));
+    const int r = g_nccl.all_gather(dev, dev + n, n, kNcclFloat32, c->comm, c->stream);
+    std::vector<cudaIpcMemHandle_t> all(2 * size_t(c->world));
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), dev + n, sizeof(mine) * size_t(c->world), cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (r != 0) return set_err(c, B200Q_ERR_COMM, "ncclAllGather of the IPC handles: %d", r);
+    if (e != cudaSuccess) return set_err(c, B200Q_ERR_CUDA, "IPC handle exchange: %s", cudaGetErrorString(e));
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        void *pa = nullptr, *pf = nullptr;
+        CUDA_TRY(c, cudaIpcOpenMemHandle(&pa, all[2 * size_t(p)], cudaIpcMemLazyEnablePeerAccess));
+        CUDA_TRY(c, cudaIpcOpenMemHandle(&pf, all[2 * size_t(p) + 1], cudaIpcMemLazyEnablePeerAccess));
+        c->peer_act[p] = static_cast<float *>(pa);
+        c->peer_sync[p] = static_cast<unsigned *>(pf);
+    }
+    c->peer_ok = true;
+    return 0;
+}
+}  // namespace
+
 int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]) {
     std::string err;
     if (!id || !load_nccl(err)) return B200Q_ERR_COMM;
@@ -1121,6 +1229,10 @@ int b200q_comm_init(b200q_ctx *c, int world, int rank, const uint8_t id[B200Q_UN
     if (r != 0) return set_err(c, B200Q_ERR_COMM, "ncclCommInitRank: %d", r);
     c->world = world;
     c->rank = rank;
+    // outputs exchanged by peer stores (B200Q_PEER=1) or by an NCCL all-gather per sharded member (default: at the
+    // sizes measured so far the peer path's per-pass synchronisation costs more than the all-gather)
+    const char *pe = getenv("B200Q_PEER");
+    if (world <= int(kMaxPeers) && pe && pe[0] == '1') return setup_peers(c);
     return 0;
 }
 

@@ -13,6 +13,7 @@
 // the CTA that holds pos touches row pos: it uses the token's k / v (rounded to F16) for it and stores them after
 // its copies landed. FP32 sums (tolerance-checked against the CPU oracle, which sums in FP64).
 #include "launch.h"
+#include "peer.cuh"
 #include "pipeline.cuh"
 #include "quant.cuh"
 
@@ -58,6 +59,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     const AttnSmem S = attn_smem(attn_sm, G, hd, C, a.max_chunks);
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(a.pw);
     const unsigned pos = __float_as_uint(*a.pos);
     if (pos >= a.kv_ctx) {
         if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, 2u);

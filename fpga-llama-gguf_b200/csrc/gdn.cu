@@ -12,6 +12,7 @@
 // shuffle-tree sums added in row order; each CTA forms the q / k sums itself and the y sum from the four CTAs'
 // parts, exchanged through distributed shared memory.
 #include "launch.h"
+#include "peer.cuh"
 #include "pipeline.cuh"
 #include "quant.cuh"
 
@@ -32,6 +33,7 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(32) gdn_kern
     cluster_arrive_relaxed();
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(a.pw);
     const unsigned part = cluster_rank(), h = blockIdx.x / kGdnSplit, kh = h % a.hk, lane = threadIdx.x;
     const unsigned j = part * 32 + lane;
     // state row of this thread: issue the loads first

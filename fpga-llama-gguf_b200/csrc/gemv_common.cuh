@@ -13,6 +13,7 @@
 // copies it started).
 #pragma once
 #include "kernel_args.h"
+#include "peer.cuh"
 #include "pipeline.cuh"
 #include "plan.h"
 #include "quant.cuh"
@@ -91,11 +92,13 @@ __device__ __forceinline__ float row_value(const GemvMemberArgs &M, unsigned gr,
     }
 }
 
+// ps (multi-GPU): the rows of a sharded member (its local rows are fewer than its total rows) also go to the peers.
 __device__ __forceinline__ void write_row(const GemvMemberArgs &M, unsigned gr, float v, float g,
-                                          const float *res_pre = nullptr) {
+                                          const float *res_pre = nullptr, const PeerSync *ps = nullptr) {
+    const PeerSync *pp = (ps && M.w.rows != M.total_rows) ? ps : nullptr;
     switch (M.epi) {
-    case EpiSwigluU: M.y[gr] = row_value(M, gr, v, g); break;
-    case EpiAdd: M.y[gr] = row_value(M, gr, v, g, res_pre); break;
+    case EpiSwigluU: peer_store(pp, M.y + gr, row_value(M, gr, v, g)); break;
+    case EpiAdd: peer_store(pp, M.y + gr, row_value(M, gr, v, g, res_pre)); break;
     case EpiConv: {
         const float s0 = M.cs[3 * gr], s1 = M.cs[3 * gr + 1], s2 = M.cs[3 * gr + 2];
         float sum = 0.0f;
@@ -103,22 +106,24 @@ __device__ __forceinline__ void write_row(const GemvMemberArgs &M, unsigned gr, 
         sum = fadd(sum, fmul(s1, M.cw[4 * gr + 1]));
         sum = fadd(sum, fmul(s2, M.cw[4 * gr + 2]));
         sum = fadd(sum, fmul(v, M.cw[4 * gr + 3]));
-        M.y[gr] = M.csilu ? silu_f32(sum) : sum;
-        M.cd[3 * gr] = s1;
-        M.cd[3 * gr + 1] = s2;
-        M.cd[3 * gr + 2] = v;
+        peer_store(pp, M.y + gr, M.csilu ? silu_f32(sum) : sum);
+        peer_store(pp, M.cd + 3 * gr, s1);
+        peer_store(pp, M.cd + 3 * gr + 1, s2);
+        peer_store(pp, M.cd + 3 * gr + 2, v);
         break;
     }
-    default: M.y[gr] = v; break;
+    default: peer_store(pp, M.y + gr, v); break;
     }
 }
 
 // Zero padding of y up to a multiple of 16 rows (the reference writes y rounded up to 16 floats), by the CTA that
 // writes the matrix's last row.
-__device__ __forceinline__ void write_padding(const GemvMemberArgs &OUT, unsigned end_row, unsigned lane) {
+__device__ __forceinline__ void write_padding(const GemvMemberArgs &OUT, unsigned end_row, unsigned lane,
+                                              const PeerSync *ps = nullptr) {
     if (end_row == OUT.total_rows && OUT.epi != EpiConv && OUT.epi != EpiAdd) {
         const unsigned pad = round16(end_row) - end_row;
-        if (lane < pad) OUT.y[end_row + lane] = 0.0f;
+        const PeerSync *pp = (ps && OUT.w.rows != OUT.total_rows) ? ps : nullptr;
+        if (lane < pad) peer_store(pp, OUT.y + end_row + lane, 0.0f);
     }
 }
 

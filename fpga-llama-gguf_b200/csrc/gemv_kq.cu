@@ -203,6 +203,8 @@ __device__ __forceinline__ float kq_final(const KqAcc &A) {
     return s;
 }
 
+// PEERS: a row-sharded multi-GPU launch (rows also stored into the peers, ready / data flags).
+template <bool PEERS>
 __global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const PassSmem P = carve_pass(smem, a);
@@ -218,6 +220,10 @@ __global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const __grid_c
         return;
     }
     pdl_wait();
+    if (a.pw.n) {  // rows of earlier sharded launches: wait for the peers' (the x warps only; warp 0 streams)
+        if (threadIdx.x == 32) peer_wait_rows(a.pw);
+        named_sync_x();
+    }
     prepare_x(a, P, X, 2);
     bool need5 = false, need6 = false;
     for (unsigned i = 0; i < a.n_members; ++i) {
@@ -257,6 +263,14 @@ __global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const __grid_c
         return;
     }
     // fold (warp 1)
+    constexpr bool peers = PEERS;
+    if (peers && blockIdx.x == 0 && lane == 0) peer_announce(a.ps);
+    const PeerSync *ps = nullptr;  // set once every peer has reached this launch (before the first store)
+    if (peers) {
+        const bool ok = __shfl_sync(0xffffffffu, lane == 0 ? peer_wait_ready(a.ps) : false, 0);
+        if (ok) ps = &a.ps;
+        else if (lane == 0 && a.err) atomicExch(a.err, 1u);
+    }
     KqAcc A0, A1;
     kq_reset(A0);
     kq_reset(A1);
@@ -279,18 +293,22 @@ __global__ void __launch_bounds__(kPassThreads, 2) gemv_kq_kernel(const __grid_c
                 if (pair >= 0) kq_fold(A1, rec + size_t(R + lane) * C * kRecWords, C, it.k, a.m[pair].w.format, X);
                 if (last) {
                     const unsigned gr = M0.w.row0 + r0 + lane;
-                    if (pair >= 0) write_row(a.m[pair], gr, kq_final(A1), kq_final(A0));
-                    else write_row(M0, gr, kq_final(A0), 0.0f);
+                    if (pair >= 0) write_row(a.m[pair], gr, kq_final(A1), kq_final(A0), nullptr, ps);
+                    else write_row(M0, gr, kq_final(A0), 0.0f, nullptr, ps);
                     kq_reset(A0);
                     kq_reset(A1);
                 }
             }
-            if (last) write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, lane);
+            if (last) write_padding(pair >= 0 ? a.m[pair] : M0, M0.w.row0 + r0 + nr, lane, ps);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&P.rempty[b]);
         ++seq;
         tile_next(a, it);
+    }
+    if (peers) {  // this CTA's rows are in every peer: count it; the last CTA raises the data flags
+        __syncwarp();
+        if (lane == 0) peer_signal(a.ps, gridDim.x);
     }
 }
 
@@ -318,7 +336,8 @@ void plan_gemv_kq(GemvArgs &a, size_t &smem) {
 cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl) {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(gemv_kq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(gemv_kq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(gemv_kq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_set = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -331,7 +350,8 @@ cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kq_kernel, a);
+    return a.ps.world > 1 ? cudaLaunchKernelEx(&cfg, gemv_kq_kernel<true>, a)
+                          : cudaLaunchKernelEx(&cfg, gemv_kq_kernel<false>, a);
 }
 
 }  // namespace b200q

@@ -479,7 +479,9 @@ __device__ __forceinline__ float fold_row(const float *terms, unsigned r, unsign
 // One launch serves the units of one format combination: FA alone (FB == 0) or SwiGLU pairs FA / FB. Clusters
 // of kXCluster CTAs share the x preparation.
 //   shared memory: [x image][terms A][terms B (pairs)][staging mbarrier, u sums][staged steps]
-template <unsigned FA, unsigned FB, unsigned U>
+// PEERS: a row-sharded multi-GPU launch (rows also stored into the peers, ready / data flags); a separate
+// instantiation so single-GPU launches carry none of it.
+template <unsigned FA, unsigned FB, unsigned U, bool PEERS>
 __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThreads, 3)
     gemv_q8_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -523,6 +525,9 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
     // staging copy now, so HBM streams while that kernel finishes
     issue_staging();
     pdl_wait();
+    constexpr bool peers = PEERS;
+    if (peers && blockIdx.x == 0 && threadIdx.x == 0) peer_announce(a.ps);
+    peer_wait_rows_cta(a.pw);
     if (a.qin) {
         load_qimage(a, X, [] {});
     } else if (a.xq) {
@@ -537,6 +542,7 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
     const XSmem xs{reinterpret_cast<const uint4 *>(X.q), reinterpret_cast<const uint4 *>(X.q + n / 2), X.meta};
     const uint64_t pol = evict_first_policy();
     bool failed = false;
+    const PeerSync *ps = nullptr;  // set once every peer has reached this launch (before the first store)
     unsigned np = 0;
     for (unsigned it = blockIdx.x; it < total; it += gridDim.x, ++np) {
         if (threadIdx.x == 0 && np) prefetch_panel(a, it + gridDim.x, 0);
@@ -560,6 +566,11 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
             if (FB && warp == 1 && lane < P) usum[lane] = fold_row(term_b, lane, w.ct, nb);
             if (FB) __syncthreads();
             if (warp == 0) {
+                if (peers && np == 0) {
+                    const bool ok = __shfl_sync(0xffffffffu, lane == 0 ? peer_wait_ready(a.ps) : false, 0);
+                    if (ok) ps = &a.ps;
+                    else if (lane == 0 && a.err) atomicExch(a.err, 1u);
+                }
                 const unsigned out_member = FB ? unsigned(a.unit_pair[u]) : a.unit_member[u];
                 if (a.qout && out_member == a.qout_member && P == 32) {
                     // this panel is block pnl of the next pass's x: every lane holds a row (rows % 32 == 0)
@@ -570,35 +581,43 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
                     write_image_block(a.qout, OUT.total_rows, pnl, val, lane, a.qout_act);
                 } else if (mine) {
                     const float acc = fold_row(term_a, lane, w.ct, nb);
-                    if (FB) write_row(MB, w.row0 + lrow, usum[lane], acc);
-                    else write_row(MA, w.row0 + lrow, acc, 0.0f, &res);
+                    if (FB) write_row(MB, w.row0 + lrow, usum[lane], acc, nullptr, ps);
+                    else write_row(MA, w.row0 + lrow, acc, 0.0f, &res, ps);
                 }
                 const unsigned end = min((pnl + 1) * P, w.rows);
-                if (end == w.rows) write_padding(OUT, w.row0 + end, lane);
+                if (end == w.rows) write_padding(OUT, w.row0 + end, lane, ps);
             }
         }
         __syncthreads();  // the term buffers are reused by the next panel
     }
     // a staging copy that no warp waited for (a failure): let it land before the CTA exits
     if (threadIdx.x == 0 && stg.k && failed) mbar_spin(stage_bar, 0);
+    if (peers && warp == 0) {  // this CTA's rows are in every peer: count it; the last CTA raises the data flags
+        __syncwarp();
+        if (lane == 0) peer_signal(a.ps, gridDim.x);
+    }
 }
 
 using GemvKernel = void (*)(GemvArgs);
 
 // The kernel of a format combination (fb = 0: single members), or null.
-static GemvKernel q8_kernel_for(unsigned fa, unsigned fb) {
+template <bool PEERS>
+static GemvKernel q8_kernel_of(unsigned fa, unsigned fb) {
     if (fb == 0) {
-        if (fa == 8) return gemv_q8_kernel<8, 0, 4>;
-        if (fa == 2) return gemv_q8_kernel<2, 0, 6>;
-        if (fa == 3) return gemv_q8_kernel<3, 0, 6>;
+        if (fa == 8) return gemv_q8_kernel<8, 0, 4, PEERS>;
+        if (fa == 2) return gemv_q8_kernel<2, 0, 6, PEERS>;
+        if (fa == 3) return gemv_q8_kernel<3, 0, 6, PEERS>;
     } else {
-        if (fa == 8 && fb == 8) return gemv_q8_kernel<8, 8, 2>;
-        if (fa == 2 && fb == 2) return gemv_q8_kernel<2, 2, 3>;
-        if (fa == 8 && fb == 2) return gemv_q8_kernel<8, 2, 2>;
-        if (fa == 2 && fb == 8) return gemv_q8_kernel<2, 8, 2>;
-        if (fa == 3 && fb == 3) return gemv_q8_kernel<3, 3, 3>;
+        if (fa == 8 && fb == 8) return gemv_q8_kernel<8, 8, 2, PEERS>;
+        if (fa == 2 && fb == 2) return gemv_q8_kernel<2, 2, 3, PEERS>;
+        if (fa == 8 && fb == 2) return gemv_q8_kernel<8, 2, 2, PEERS>;
+        if (fa == 2 && fb == 8) return gemv_q8_kernel<2, 8, 2, PEERS>;
+        if (fa == 3 && fb == 3) return gemv_q8_kernel<3, 3, 3, PEERS>;
     }
     return nullptr;
+}
+static GemvKernel q8_kernel_for(unsigned fa, unsigned fb, bool peers = false) {
+    return peers ? q8_kernel_of<true>(fa, fb) : q8_kernel_of<false>(fa, fb);
 }
 
 __global__ void __launch_bounds__(256) quantize_kernel(const QuantArgs a) {
@@ -606,6 +625,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantArgs a) {
     const XImage X = carve_ximage(smem, a.n);
     pdl_wait();
     pdl_launch_dependents();
+    peer_wait_rows_cta(a.pw);
     quantize_cta(a.x, a.n, a.act, a.norm_w, a.norm_eps, a.norm_mode, X);
     for (unsigned i = threadIdx.x; i < a.n / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(a.q)[i] = reinterpret_cast<const uint4 *>(X.q)[i];
@@ -679,8 +699,10 @@ unsigned gemv_q8_cluster() { return kXCluster; }
 
 cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned fa, unsigned fb, unsigned grid, size_t smem, cudaStream_t st,
                            bool pdl) {
-    const GemvKernel k = q8_kernel_for(fa, fb);
+    const bool peers = a.ps.world > 1;
+    const GemvKernel k = q8_kernel_for(fa, fb, peers);
     if (!k) return cudaErrorInvalidValue;
+    if (peers) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kPanelThreads);

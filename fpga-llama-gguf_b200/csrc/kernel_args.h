@@ -28,6 +28,38 @@ struct GemvMemberArgs {
     unsigned csilu = 0;
 };
 
+// Row-sharded multi-GPU passes without a collective: every rank stores its output rows into its own act and, over
+// NVLink, into the same offsets of every peer's act (IPC-mapped). Each sharded launch of a list has a sync slot. Per
+// slot and rank, a rank counts its own launches of the slot (`mine`, raised by the launch's last CTA); a launch k of
+// the slot announces in every peer that it has reached the slot (ready = k: its earlier work, which read those rows,
+// is complete) and raises its data word to k once all its rows are in every peer. Words only grow, so nothing is
+// cleared between lists; all ranks run the same launches in the same order.
+constexpr unsigned kMaxPeers = 8;
+constexpr unsigned kSyncSlots = 512;
+__host__ __device__ inline unsigned ready_word(unsigned slot, unsigned rank) { return slot * kMaxPeers + rank; }
+__host__ __device__ inline unsigned data_word(unsigned slot, unsigned rank) {
+    return kSyncSlots * kMaxPeers + slot * kMaxPeers + rank;
+}
+constexpr unsigned kSyncCountWord = 2 * kSyncSlots * kMaxPeers;    // [slot] CTAs of the running launch
+constexpr unsigned kSyncMineWord = kSyncCountWord + kSyncSlots;    // [slot] launches of the slot completed here
+constexpr unsigned kSyncWords = kSyncMineWord + kSyncSlots;
+
+struct PeerSync {
+    float *act = nullptr;              // this rank's act (offsets of peer stores are taken against it)
+    float *peer_act[kMaxPeers] = {};   // peers' act; null for this rank
+    unsigned *peer_sync[kMaxPeers] = {};  // peers' sync words (IPC-mapped)
+    unsigned *sync = nullptr;          // this rank's sync words
+    unsigned world = 1, rank = 0, slot = 0;
+};
+
+// A kernel that reads rows of sharded launches first waits for the peers' data words of slots [slot0, slot0 + n)
+// (n = 0: nothing to wait for).
+struct PeerWait {
+    const unsigned *sync = nullptr;
+    unsigned slot0 = 0, n = 0, world = 1, rank = 0;
+    unsigned *err = nullptr;
+};
+
 constexpr unsigned kMaxUnits = 4;
 // bytes of a quantized x image of up to 16384 values (quants + meta words)
 constexpr unsigned kQImageBytes = 16384 + 16384 / 32 * 16;
@@ -66,6 +98,8 @@ struct GemvArgs {
     uint8_t *qout = nullptr;
     unsigned qout_member = 0;
     unsigned qout_act = 0;        // 0 Q8_0, 1 Q8_1 (the next pass's activation type)
+    PeerSync ps;                  // world > 1: sharded members' rows also go to the peers
+    PeerWait pw;                  // rows of earlier sharded launches this pass reads
 };
 
 // Quantize x (optionally through the RMSNORM arithmetic) to scratch: the same device code as the GEMV prologue.
@@ -81,6 +115,7 @@ struct QuantArgs {
     float *s = nullptr;
     int32_t *b = nullptr;
     uint16_t *d16 = nullptr;      // optional FP16 bits of the scales (Q8_0: d, Q8_1: d and s interleaved)
+    PeerWait pw;
 };
 
 }  // namespace b200q

@@ -17,6 +17,7 @@ struct EwArgs {
     unsigned row = 0, stride = 0;  // strided a (UNARY x / SILU_MUL g): rows of `row` floats every `stride` floats
     unsigned kind = 0;    // UNARY kind
     unsigned sigmoid = 0; // SILU_MUL sigmoid flag
+    PeerWait pw;
 };
 
 struct GdnArgs {
@@ -29,6 +30,7 @@ struct GdnArgs {
     float *y = nullptr;
     float scale = 0.0f, l2_eps = 0.0f, rms_eps = 0.0f;
     unsigned l2 = 0;
+    PeerWait pw;
 };
 
 struct AttnArgs {
@@ -43,6 +45,7 @@ struct AttnArgs {
     float *part = nullptr;      // [n_head][max_chunks][head_dim + 2] chunk outputs, maximum, sum
     unsigned *counters = nullptr;  // [n_kv_head] finished chunks (zero between launches)
     unsigned *err = nullptr;       // set when a bounded wait for the chunk copies ran out
+    PeerWait pw;
 };
 
 // fill in the shared-memory plan of a pass (stages, result buffers) and return its dynamic shared memory
@@ -57,17 +60,18 @@ cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned fa, unsigned fb, unsigned
 cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
 cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,
-                           float eps, unsigned flags, cudaStream_t st, bool pdl);
+                           float eps, unsigned flags, const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_conv(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
-                        unsigned use_silu, cudaStream_t st, bool pdl);
+                        unsigned use_silu, const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_rope(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows,
-                        cudaStream_t st, bool pdl);
+                        const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_argmax(const float *x, unsigned n, float *y, unsigned long long *slot, unsigned *counter,
-                          cudaStream_t st, bool pdl);
+                          const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx, float *y, unsigned *status,
-                           cudaStream_t st, bool pdl);
+                           const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_peer_wait(const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
 unsigned attn_chunk(unsigned kv_ctx, unsigned n_kv_head, unsigned sms);
 size_t attn_smem_bytes(unsigned n_head, unsigned n_kv_head, unsigned head_dim, unsigned chunk, unsigned max_chunks);

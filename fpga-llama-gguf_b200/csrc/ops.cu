@@ -4,17 +4,19 @@
 // All FP32 arithmetic uses the _rn intrinsics in the CPU reference's operation order, so results match the CPU
 // bit for bit except where exp/log are involved (see common.cuh). Bandwidth-bound and tiny (<= 65536 floats).
 #include "launch.h"
+#include "peer.cuh"
 #include "quant.cuh"
 
 namespace b200q {
 
 // ---- RMSNORM rows: one CTA per row --------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *w, float *y, unsigned n,
-                                                       unsigned stride, float eps, unsigned flags) {
+                                                       unsigned stride, float eps, unsigned flags, const PeerWait pw) {
     __shared__ double red[32];
     __shared__ float scale_s;
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(pw);
     const float *xr = x + size_t(blockIdx.x) * stride;
     float *yr = y + size_t(blockIdx.x) * n;
     const float s = cta_norm_scale(xr, n, eps, flags & 1u, red, &scale_s);
@@ -28,6 +30,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
 __global__ void ew_kernel(const EwArgs a) {
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(a.pw);
     for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < a.n; e += gridDim.x * blockDim.x) {
         const size_t ai = a.row ? size_t(e / a.row) * a.stride + e % a.row : e;
         const float av = a.a[ai];
@@ -46,9 +49,10 @@ __global__ void ew_kernel(const EwArgs a) {
 
 // ---- CONV (ggml_ssm_conv, one token, d_conv 4) --------------------------------------------------------------------
 __global__ void conv_kernel(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
-                            unsigned use_silu) {
+                            unsigned use_silu, const PeerWait pw) {
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(pw);
     const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= ch) return;
     const float s0 = s_src[3 * c], s1 = s_src[3 * c + 1], s2 = s_src[3 * c + 2], xv = x[c];
@@ -64,9 +68,11 @@ __global__ void conv_kernel(const float *x, const float *w, float *y, const floa
 }
 
 // ---- ROPE, NEOX pairing --------------------------------------------------------------------------------------------
-__global__ void rope_kernel(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows) {
+__global__ void rope_kernel(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows,
+                            const PeerWait pw) {
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(pw);
     const unsigned half = n_dims / 2;
     const unsigned per_row = half + (ne0 - n_dims);
     for (unsigned t = blockIdx.x * blockDim.x + threadIdx.x; t < rows * per_row; t += gridDim.x * blockDim.x) {
@@ -99,11 +105,12 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, unsigned i) {
 // atomicMax; the last CTA to finish (counter) writes the result and clears slot and counter for the next launch.
 // Like a scalar scan with `>` from index 0: a NaN at index 0 keeps index 0, other NaNs are skipped.
 __global__ void __launch_bounds__(256) argmax_kernel(const float *x, unsigned n, float *y, unsigned long long *slot,
-                                                     unsigned *counter) {
+                                                     unsigned *counter, const PeerWait pw) {
     __shared__ unsigned long long red[8];
     __shared__ bool last_s;
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(pw);
     unsigned long long best = 0;
     const unsigned n4 = n / 4, stride = gridDim.x * blockDim.x;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
@@ -139,9 +146,11 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *x, unsigned n,
 }
 
 // ---- GET_ROW (extension): one dequantized row, index read from act (ggml dequantize_row_q4_0 / q8_0) -------------
-__global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *idx_f, float *y, unsigned *status) {
+__global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *idx_f, float *y, unsigned *status,
+                               const PeerWait pw) {
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(pw);
     const unsigned row = __float_as_uint(*idx_f);
     if (row < w.row0 || row >= w.row0 + w.rows) {
         if (blockIdx.x == 0 && threadIdx.x == 0 && status) atomicExch(status, 1u);
@@ -166,6 +175,14 @@ __global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *i
     }
 }
 
+// ---- row-sharded passes: the wait for the peers' rows as a kernel of its own ----------------------------------------
+// (before a copy or a host read of act that no kernel in between covers)
+__global__ void peer_wait_kernel(const PeerWait pw) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) peer_wait_rows(pw);
+}
+
 // ---- launchers ------------------------------------------------------------------------------------------------------
 static cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
                                    cudaLaunchAttribute *attr) {
@@ -182,10 +199,10 @@ static cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStrea
 }
 
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,
-                           float eps, unsigned flags, cudaStream_t st, bool pdl) {
+                           float eps, unsigned flags, const PeerWait &pw, cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(rows), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, rmsnorm_kernel, x, w, y, n, stride, eps, flags);
+    return cudaLaunchKernelEx(&cfg, rmsnorm_kernel, x, w, y, n, stride, eps, flags, pw);
 }
 
 cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl) {
@@ -196,36 +213,42 @@ cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_conv(const float *x, const float *w, float *y, const float *s_src, float *s_dst, unsigned ch,
-                        unsigned use_silu, cudaStream_t st, bool pdl) {
+                        unsigned use_silu, const PeerWait &pw, cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3((ch + 127) / 128), dim3(128), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, conv_kernel, x, w, y, s_src, s_dst, ch, use_silu);
+    return cudaLaunchKernelEx(&cfg, conv_kernel, x, w, y, s_src, s_dst, ch, use_silu, pw);
 }
 
 cudaError_t launch_rope(const float *x, const float *cs, float *y, unsigned n_dims, unsigned ne0, unsigned rows,
-                        cudaStream_t st, bool pdl) {
+                        const PeerWait &pw, cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     const unsigned work = rows * (n_dims / 2 + ne0 - n_dims);
     const unsigned grid = (work + 255) / 256 < 148 ? (work + 255) / 256 : 148;
     cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, rope_kernel, x, cs, y, n_dims, ne0, rows);
+    return cudaLaunchKernelEx(&cfg, rope_kernel, x, cs, y, n_dims, ne0, rows, pw);
 }
 
 cudaError_t launch_argmax(const float *x, unsigned n, float *y, unsigned long long *slot, unsigned *counter,
-                          cudaStream_t st, bool pdl) {
+                          const PeerWait &pw, cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     const unsigned per_cta = 256 * 4 * 4;  // about four float4 per thread
     unsigned grid = (n + per_cta - 1) / per_cta;
     grid = grid < 1 ? 1 : (grid > 148 ? 148 : grid);
     cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, argmax_kernel, x, n, y, slot, counter);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, x, n, y, slot, counter, pw);
 }
 
 cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx, float *y, unsigned *status,
-                           cudaStream_t st, bool pdl) {
+                           const PeerWait &pw, cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3((cols + 255) / 256), dim3(256), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, get_row_kernel, w, cols, idx, y, status);
+    return cudaLaunchKernelEx(&cfg, get_row_kernel, w, cols, idx, y, status, pw);
+}
+
+cudaError_t launch_peer_wait(const PeerWait &pw, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(32), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, peer_wait_kernel, pw);
 }
 
 }  // namespace b200q

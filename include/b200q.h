@@ -267,7 +267,10 @@ B200Q_API int b200q_quantize_noalloc(int device, const float *x, unsigned n, uns
 #define B200Q_UNIQUE_ID_BYTES 128
 B200Q_API int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]);
 /* Join a communicator of world ranks; from then on uploads keep only this rank's row slice of each shardable
- * matrix and every pass all-gathers its GEMV outputs so all ranks hold the full act, as with one GPU. */
+ * matrix (rows divisible by 16 x world) and every pass gathers its GEMV outputs so all ranks hold the full act, as
+ * with one GPU (results bit-identical to one GPU). The gather is an NCCL all-gather per sharded output, or with the
+ * environment variable B200Q_PEER=1 the GEMV kernels store their rows straight into every peer's act over NVLink
+ * (CUDA IPC mappings made here) and the next kernel waits for the peers' flags (bounded waits). */
 B200Q_API int b200q_comm_init(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]);
 B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
 
