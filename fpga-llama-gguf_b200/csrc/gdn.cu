@@ -5,12 +5,13 @@
 // optionally with q/k L2-normalized per head (RMSNORM with flags 3), the gates beta = sigmoid(beta),
 // g = softplus(g + dt) * a, and the gated output (RMSNORM(y) * w) * silu(z) per head.
 //
-// One cluster of 4 CTAs per value head, 32 state rows per CTA, one thread per state row: the thread holds its
-// 128-float row in registers for the whole step (read once, written once) and sums both dot products in index
-// order with IEEE-rounded FP32 adds, the CPU reference's order, so the new state and y match it bit for bit
-// whenever exp() does. The per-head sums of squares (L2 of q and k, RMS of y) are taken as four 32-value
-// shuffle-tree sums added in row order; each CTA forms the q / k sums itself and the y sum from the four CTAs'
-// parts, exchanged through distributed shared memory.
+// One cluster of 4 CTAs per value head, 32 state rows per CTA, four threads per state row: each thread holds a
+// 32-float segment of its row in registers for the whole step (read once, written once) and sums its part of both
+// dot products in index order; the four parts are added as (p0 + p1) + (p2 + p3). (One thread per row, the CPU's
+// fully sequential order, left a single warp per SM running ~1800 dependent instructions: ~8 us per step.) The
+// result is within the reference's tolerance, not bit-exact. The per-head sums of squares (L2 of q and k, RMS of y)
+// are four 32-value shuffle-tree sums added in row order, as the CPU oracle is checked against; each CTA forms the
+// q / k sums itself and the y sum from the four CTAs' parts, exchanged through distributed shared memory.
 #include "launch.h"
 #include "peer.cuh"
 #include "pipeline.cuh"
@@ -18,7 +19,8 @@
 
 namespace b200q {
 
-constexpr unsigned kGdnSplit = 4;  // CTAs per head (one cluster), 32 state rows each
+constexpr unsigned kGdnSplit = 4;    // CTAs per head (one cluster), 32 state rows each
+constexpr unsigned kGdnThreads = 128;  // four threads per state row
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -26,54 +28,52 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
-__global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(32) gdn_kernel(const GdnArgs a) {
-    __shared__ float qs[128], ks[128];
+// sum of the four segment parts of a row, (p0 + p1) + (p2 + p3), in all four threads of the quad
+__device__ __forceinline__ float quad_sum(float p) {
+    p = fadd(p, __shfl_xor_sync(0xffffffffu, p, 1));
+    return fadd(p, __shfl_xor_sync(0xffffffffu, p, 2));
+}
+
+__global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads) gdn_kernel(const GdnArgs a) {
+    __shared__ __align__(16) float qs[128], ks[128];
+    __shared__ float ycta[32];
+    __shared__ double red[4];
     __shared__ double ysum[kGdnSplit];  // part p of the head's sum of y^2, written by CTA p into every CTA
     __shared__ float gate[2];
     cluster_arrive_relaxed();
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
     peer_wait_rows_cta(a.pw);
-    const unsigned part = cluster_rank(), h = blockIdx.x / kGdnSplit, kh = h % a.hk, lane = threadIdx.x;
-    const unsigned j = part * 32 + lane;
-    // state row of this thread: issue the loads first
-    const float4 *src = reinterpret_cast<const float4 *>(a.state_in + (size_t(h) * 128 + j) * 128);
-    float row[128];
+    const unsigned part = cluster_rank(), h = blockIdx.x / kGdnSplit, kh = h % a.hk;
+    const unsigned tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const unsigned rloc = tid / 4, seg = tid % 4, j = part * 32 + rloc;
+    // this thread's 32-float segment of state row j: issue the loads first
+    const float4 *src = reinterpret_cast<const float4 *>(a.state_in + (size_t(h) * 128 + j) * 128 + seg * 32);
+    float row[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 8; ++i) {
         const float4 v = src[i];
         row[4 * i] = v.x;
         row[4 * i + 1] = v.y;
         row[4 * i + 2] = v.z;
         row[4 * i + 3] = v.w;
     }
-    float qv[kGdnSplit], kv[kGdnSplit];
-#pragma unroll
-    for (unsigned w = 0; w < kGdnSplit; ++w) {
-        qv[w] = a.q[kh * 128 + 32 * w + lane];
-        kv[w] = a.k[kh * 128 + 32 * w + lane];
-    }
+    float qv = a.q[kh * 128 + tid], kv = a.k[kh * 128 + tid];
     if (a.l2) {  // 1 / fmaxf(sqrtf(float(sum x^2)), eps), x * scale (gemvq_ref.h:309-324 with flags 3)
-        double sq = 0.0, sk = 0.0;
-#pragma unroll
-        for (unsigned w = 0; w < kGdnSplit; ++w) {
-            sq = w == 0 ? warp_sum_d(double(fmul(qv[w], qv[w]))) : sq + warp_sum_d(double(fmul(qv[w], qv[w])));
-            sk = w == 0 ? warp_sum_d(double(fmul(kv[w], kv[w]))) : sk + warp_sum_d(double(fmul(kv[w], kv[w])));
-        }
-        const float iq = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sq)), a.l2_eps));
-        const float ik = fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sk)), a.l2_eps));
-#pragma unroll
-        for (unsigned w = 0; w < kGdnSplit; ++w) {
-            qv[w] = fmul(qv[w], iq);
-            kv[w] = fmul(kv[w], ik);
-        }
+        const double sq = warp_sum_d(double(fmul(qv, qv))), sk = warp_sum_d(double(fmul(kv, kv)));
+        if (lane == 0) red[warp] = sq;
+        __syncthreads();
+        const double tq = ((red[0] + red[1]) + red[2]) + red[3];
+        __syncthreads();
+        if (lane == 0) red[warp] = sk;
+        __syncthreads();
+        const double tk = ((red[0] + red[1]) + red[2]) + red[3];
+        qv = fmul(qv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(tq)), a.l2_eps)));
+        kv = fmul(kv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(tk)), a.l2_eps)));
     }
-#pragma unroll
-    for (unsigned w = 0; w < kGdnSplit; ++w) {
-        qs[32 * w + lane] = qv[w];
-        ks[32 * w + lane] = kv[w];
-    }
-    if (lane == 0) {
+    qs[tid] = qv;
+    ks[tid] = kv;
+    if (tid == 0) {
         float g = a.g[h], b = a.beta[h];
         if (a.dt) {  // gemvqc_gdn.h:265-280: g = softplus(g + dt) * a, beta = sigmoid(beta)
             g = fmul(softplus_f32(fadd(g, a.dt[h])), a.a[h]);
@@ -82,42 +82,57 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(32) gdn_kern
         gate[0] = exp_f32(g);
         gate[1] = b;
     }
-    __syncwarp();
+    __syncthreads();
     const float decay = gate[0], beta = gate[1];
+    float kseg[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 k4 = reinterpret_cast<const float4 *>(ks + seg * 32)[i];
+        kseg[4 * i] = k4.x;
+        kseg[4 * i + 1] = k4.y;
+        kseg[4 * i + 2] = k4.z;
+        kseg[4 * i + 3] = k4.w;
+    }
     float dot = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 128; ++i) {
+    for (int i = 0; i < 32; ++i) {
         row[i] = fmul(row[i], decay);
-        dot = fadd(dot, fmul(row[i], ks[i]));
+        dot = fadd(dot, fmul(row[i], kseg[i]));
     }
+    dot = quad_sum(dot);
     const float delta = fmul(fsub(a.v[h * 128 + j], dot), beta);
     float out = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 128; ++i) {
-        row[i] = fadd(row[i], fmul(ks[i], delta));
-        out = fadd(out, fmul(row[i], qs[i]));
+    for (int i = 0; i < 32; ++i) {
+        row[i] = fadd(row[i], fmul(kseg[i], delta));
+        out = fadd(out, fmul(row[i], qs[seg * 32 + i]));
     }
-    float4 *dst = reinterpret_cast<float4 *>(a.state_out + (size_t(h) * 128 + j) * 128);
+    out = quad_sum(out);
+    float4 *dst = reinterpret_cast<float4 *>(a.state_out + (size_t(h) * 128 + j) * 128 + seg * 32);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) dst[i] = make_float4(row[4 * i], row[4 * i + 1], row[4 * i + 2], row[4 * i + 3]);
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(row[4 * i], row[4 * i + 1], row[4 * i + 2], row[4 * i + 3]);
     float yv = fmul(out, a.scale);
     cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
     if (a.z) {  // (y * rms scale) * w, then silu(z) * that (RMSNORM + SILU_MUL, gemvqc_gdn.h:284-346)
-        const double mine = warp_sum_d(double(fmul(yv, yv)));
-        if (lane < kGdnSplit) st_cluster_f64(peer_smem(smem_addr(&ysum[part]), lane), mine);
+        if (seg == 0) ycta[rloc] = yv;
+        __syncthreads();
+        if (warp == 0) {
+            const double mine = warp_sum_d(double(fmul(ycta[lane], ycta[lane])));
+            if (lane < kGdnSplit) st_cluster_f64(peer_smem(smem_addr(&ysum[part]), lane), mine);
+        }
         cluster_sync();
         const double s = ((ysum[0] + ysum[1]) + ysum[2]) + ysum[3];
         const float sc = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(s, 128.0)), a.rms_eps)));
         const float nv = fmul(fmul(yv, sc), a.wn[j]);
         yv = fmul(silu_f32(a.z[h * 128 + j]), nv);
     }
-    a.y[h * 128 + j] = yv;
+    if (seg == 0) a.y[h * 128 + j] = yv;
 }
 
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.hv * kGdnSplit);
-    cfg.blockDim = dim3(32);
+    cfg.blockDim = dim3(kGdnThreads);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -79,7 +79,9 @@ def _gdn_inputs(r, hv, hk):
     return q, k, v, g, beta
 
 
-def test_gdn_step_plain_bit_exact(ctx, b2, orc):
+def test_gdn_step_plain_within_tolerance(ctx, b2, orc):
+    """One plain GDN step (no options) on 16 heads: state and y within the reference's verify tolerance, with the
+    term magnitudes (4e-6 x magnitude, gemvq_ref.h), and 1e-4 relative."""
     hv, hk = 16, 16
     r = rng(62)
     state = r.normal(0, 0.1, hv * 128 * 128).astype(np.float32)
@@ -93,10 +95,12 @@ def test_gdn_step_plain_bit_exact(ctx, b2, orc):
     act[6144:6160], act[6160:6176] = gg, bb
     cl = b2.gdn(hv, hk, 0, 2048, 4096, 6144, 6160, 8192, 0, 0, 128 ** -0.5)
     got, ref, gs, rs = _run_both(ctx, orc, cl, act, state=state)
-    # exp() of the decay may differ in the last bit from glibc: check bits and the relative error
-    same = np.mean(_bits(gs) == _bits(rs))
+    _, y_ref, y_mag, s_mag = orc.gdn(state, qn, kn, v, gg, bb, hv, hk, 128 ** -0.5)
+    assert np.array_equal(_bits(got[8192:8192 + hv * 128]), _bits(y_ref)) or \
+        (np.abs(got[8192:8192 + hv * 128] - y_ref) <= 1e-6 + 1e-5 * np.abs(y_ref) + 4e-6 * y_mag).all()
+    assert (np.abs(gs - rs) <= 1e-6 + 1e-5 * np.abs(rs) + 4e-6 * s_mag).all()
     rel = np.abs(gs - rs) / np.maximum(np.abs(rs), 1e-3)
-    assert same > 0.99 and rel.max() <= 1e-4
+    assert rel.max() <= 1e-4
 
 
 def test_gdn_full_options_128_steps_config3(ctx, b2, synth, orc):
