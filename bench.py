@@ -274,6 +274,8 @@ def main():
     ap.add_argument("--decode", default="4b,9b", help="synthetic decode models to run after the GEMV stack "
                     "(comma list of 4b, 9b; empty for none)")
     ap.add_argument("--decode-tokens", type=int, default=128)
+    ap.add_argument("--decode-only", action="store_true", help="run only the decode measurement (for profiling "
+                    "runs); the line then carries the decode object and no GEMV metric")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -312,6 +314,40 @@ def main():
     dev = local if world > 1 else 0
     torch.cuda.set_device(dev)
 
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if not dist:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    import fpga_llama_gguf_b200.decode as D
+    shapes = {"4b": (D.SHAPE_4B, "4B-like: 24 GDN + 8 gated GQA layers, hidden 2560, FFN 9216, vocab 151936, Q4_0 + "
+                                 "Q6_K head, 512-token F16 KV"),
+              "9b": (D.SHAPE_9B, "9B-like: as 4B-like with hidden 4096, FFN 12288")}
+
+    def run_decodes():
+        out = {}
+        for key in [k for k in args.decode.split(",") if k]:
+            shape, label = shapes[key]
+            out[key] = decode_bench(b2, torch, dist, dev, world, rank, shape, label, args.decode_tokens,
+                                    max(3, min(args.warmup, 16)), max_over_ranks, barrier)
+        return out
+
+    if args.decode_only:
+        decode = run_decodes()
+        if dist:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"metric": "decode tokens/s", "n_gpus": world, "impl": "b200q", "mode": "decode-only",
+                              "data": "synthetic", "decode": decode}), flush=True)
+        return 0
+
     # n_layers: enough layers that one step reads more than 3x the L2
     ctx = b2.Context(device=dev, weight_bytes=n_layers * (per_layer + (8 << 20)) + (64 << 20), act_floats=ACT_FLOATS)
     if world > 1:
@@ -329,18 +365,6 @@ def main():
     ctx.write(XIN, x)
     ctx.write(GAIN, gain)
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
-
-    def barrier():
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if not dist:
-            return v
-        t = torch.tensor([v], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     # warm-up
     ctx.launch_many([stack], args.warmup)
@@ -408,15 +432,7 @@ def main():
         g.close()
     ctx.close()
 
-    decode = {}
-    import fpga_llama_gguf_b200.decode as D
-    shapes = {"4b": (D.SHAPE_4B, "4B-like: 24 GDN + 8 gated GQA layers, hidden 2560, FFN 9216, vocab 151936, Q4_0 + "
-                                 "Q6_K head, 512-token F16 KV"),
-              "9b": (D.SHAPE_9B, "9B-like: as 4B-like with hidden 4096, FFN 12288")}
-    for key in [k for k in args.decode.split(",") if k]:
-        shape, label = shapes[key]
-        decode[key] = decode_bench(b2, torch, dist, dev, world, rank, shape, label, args.decode_tokens,
-                                   max(3, min(args.warmup, 16)), max_over_ranks, barrier)
+    decode = run_decodes()
     if dist:
         dist.destroy_process_group()
     if rank == 0:

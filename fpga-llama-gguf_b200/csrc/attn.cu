@@ -57,28 +57,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     __shared__ unsigned last_s, ok_s;
     const unsigned G = a.n_head / a.n_kv_head, hd = a.head_dim, C = a.chunk, nvec = hd / 8;
     const AttnSmem S = attn_smem(attn_sm, G, hd, C, a.max_chunks);
-    pdl_wait();
-    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
-    peer_wait_rows_cta(a.pw);
-    const unsigned pos = __float_as_uint(*a.pos);
-    if (pos >= a.kv_ctx) {
-        if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, 2u);
-        return;
-    }
-    const unsigned T = pos + 1, chunk = blockIdx.x, kvh = blockIdx.y, c0 = chunk * C;
-    if (c0 >= T) return;
-    const unsigned n_chunks = (T + C - 1) / C, cn = T - c0 < C ? T - c0 : C;
-    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const unsigned chunk = blockIdx.x, kvh = blockIdx.y, c0 = chunk * C;
     const size_t row0 = size_t(kvh) * a.kv_ctx + c0;  // first cache row of the chunk
+    // The chunk's rows come in before the wait on the previous kernel: only ATTN itself writes the cache
+    // (the row at pos, which this CTA replaces after the copy), so the copy overlaps the previous kernel's end.
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         mbar_fence_init();
-        const unsigned bytes = cn * hd * 2;
+        const unsigned rows = a.kv_ctx - c0 < C ? a.kv_ctx - c0 : C;  // the slot's last chunk may be shorter
+        const unsigned bytes = rows * hd * 2;
         mbar_expect_tx(&bar, 2 * bytes);
         const uint64_t pol = evict_first_policy();
         bulk_copy(S.k, a.kcache + row0 * hd, bytes, &bar, pol);
         bulk_copy(S.v, a.vcache + row0 * hd, bytes, &bar, pol);
     }
+    pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(a.pw);
+    const unsigned pos = __float_as_uint(*a.pos);
+    const unsigned T = pos + 1;
+    const bool active = pos < a.kv_ctx && c0 < T;
+    if (!active) {  // outside the slot, or a chunk past pos: let the copies land, then leave
+        if (pos >= a.kv_ctx && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status)
+            atomicOr(a.status, 2u);
+        if (threadIdx.x == 0 && !mbar_wait(&bar, 0) && a.err) atomicExch(a.err, 1u);
+        return;
+    }
+    const unsigned n_chunks = (T + C - 1) / C, cn = T - c0 < C ? T - c0 : C;
+    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     for (unsigned e = threadIdx.x; e < G * hd; e += kAttnThreads) S.q[e] = a.q[size_t(kvh) * G * hd + e];
     if (threadIdx.x == 0) {
         ok_s = mbar_wait(&bar, 0);

@@ -59,6 +59,18 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
         row[4 * i + 3] = v.w;
     }
     float qv = a.q[kh * 128 + tid], kv = a.k[kh * 128 + tid];
+    // every other input of the step now, so no load waits in the middle of the dependent chain
+    const float vj = a.v[h * 128 + j];
+    const float zj = a.z ? a.z[h * 128 + j] : 0.0f, wj = a.z ? a.wn[j] : 0.0f;
+    float g_in = 0.0f, b_in = 0.0f, dt_in = 0.0f, a_in = 0.0f;
+    if (tid == 0) {
+        g_in = a.g[h];
+        b_in = a.beta[h];
+        if (a.dt) {
+            dt_in = a.dt[h];
+            a_in = a.a[h];
+        }
+    }
     if (a.l2) {  // 1 / fmaxf(sqrtf(float(sum x^2)), eps), x * scale (gemvq_ref.h:309-324 with flags 3)
         const double sq = warp_sum_d(double(fmul(qv, qv))), sk = warp_sum_d(double(fmul(kv, kv)));
         if (lane == 0) red[warp] = sq;
@@ -74,9 +86,9 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
     qs[tid] = qv;
     ks[tid] = kv;
     if (tid == 0) {
-        float g = a.g[h], b = a.beta[h];
+        float g = g_in, b = b_in;
         if (a.dt) {  // gemvqc_gdn.h:265-280: g = softplus(g + dt) * a, beta = sigmoid(beta)
-            g = fmul(softplus_f32(fadd(g, a.dt[h])), a.a[h]);
+            g = fmul(softplus_f32(fadd(g, dt_in)), a_in);
             b = sigmoid_f32(b);
         }
         gate[0] = exp_f32(g);
@@ -100,7 +112,7 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
         dot = fadd(dot, fmul(row[i], kseg[i]));
     }
     dot = quad_sum(dot);
-    const float delta = fmul(fsub(a.v[h * 128 + j], dot), beta);
+    const float delta = fmul(fsub(vj, dot), beta);
     float out = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -123,8 +135,8 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
         cluster_sync();
         const double s = ((ysum[0] + ysum[1]) + ysum[2]) + ysum[3];
         const float sc = fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(s, 128.0)), a.rms_eps)));
-        const float nv = fmul(fmul(yv, sc), a.wn[j]);
-        yv = fmul(silu_f32(a.z[h * 128 + j]), nv);
+        const float nv = fmul(fmul(yv, sc), wj);
+        yv = fmul(silu_f32(zj), nv);
     }
     if (seg == 0) a.y[h * 128 + j] = yv;
 }
