@@ -19,7 +19,14 @@ namespace b200q {
 constexpr unsigned kRecWords = 12;  // per (row, super-block): aux[8], mins, d | dmin << 16, pad
 
 // y5: per (sb, j, l) int8x4 (y[32j+l], y[32j+l+8], y[32j+l+16], y[32j+l+24]); y6: per (sb, j, l) int16x2
-// (y[16j+l], y[16j+l+8]).
+// (y[16j+l], y[16j+l+8]). Word order inside a super-block: the 4-word groups that the eight parts of one
+// (row, super-block) read together are adjacent, so a quarter-warp's 128-bit loads hit 32 distinct banks:
+// y5 [sb][half h][part j][t] holds word (j, l = 4h + t); y6 [sb][jj][half h][part p][t] holds (j = 2p + jj, 4h + t).
+__device__ __forceinline__ unsigned y5_word(unsigned j, unsigned l) { return ((l / 4) * 8 + j) * 4 + l % 4; }
+__device__ __forceinline__ unsigned y6_word(unsigned j, unsigned l) {
+    return (((j % 2) * 2 + l / 4) * 8 + j / 2) * 4 + l % 4;
+}
+
 __device__ __forceinline__ void build_transposed(const XImage &X, unsigned cols, bool need5, bool need6, uint32_t *y5,
                                                  uint32_t *y6) {
     const unsigned nsb = cols / 256, t = threadIdx.x - 32;
@@ -27,15 +34,15 @@ __device__ __forceinline__ void build_transposed(const XImage &X, unsigned cols,
         for (unsigned i = t; i < nsb * 64; i += kXThreads) {
             const unsigned sb = i / 64, j = (i / 8) % 8, l = i % 8;
             const int8_t *y = X.q + sb * 256 + 32 * j + l;
-            y5[i] = uint32_t(uint8_t(y[0])) | uint32_t(uint8_t(y[8])) << 8 | uint32_t(uint8_t(y[16])) << 16 |
-                    uint32_t(uint8_t(y[24])) << 24;
+            y5[sb * 64 + y5_word(j, l)] = uint32_t(uint8_t(y[0])) | uint32_t(uint8_t(y[8])) << 8 |
+                                          uint32_t(uint8_t(y[16])) << 16 | uint32_t(uint8_t(y[24])) << 24;
         }
     }
     if (need6) {
         for (unsigned i = t; i < nsb * 128; i += kXThreads) {
             const unsigned sb = i / 128, j = (i / 8) % 16, l = i % 8;
             const int8_t *y = X.q + sb * 256 + 16 * j + l;
-            y6[i] = uint32_t(uint16_t(int16_t(y[0]))) | uint32_t(uint16_t(int16_t(y[8]))) << 16;
+            y6[sb * 128 + y6_word(j, l)] = uint32_t(uint16_t(int16_t(y[0]))) | uint32_t(uint16_t(int16_t(y[8]))) << 16;
         }
     }
     named_sync_x();
@@ -82,8 +89,8 @@ __device__ __forceinline__ void part_q5k(const uint8_t *qs, const uint8_t *dm, u
     const uint4 h1 = *reinterpret_cast<const uint4 *>(qs + 144);
     const uint32_t QL[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
     const uint32_t QH[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    const uint4 ya = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + 8 * j);
-    const uint4 yb = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + 8 * j + 4);
+    const uint4 ya = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + y5_word(j, 0));
+    const uint4 yb = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + y5_word(j, 4));
     const uint32_t Y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
     int sc, m;
     scale_min_k4(j, dm, sc, m);
@@ -110,8 +117,8 @@ __device__ __forceinline__ void part_q6k(const uint8_t *qs, const uint8_t *dm, u
         const unsigned j = 2 * p + jj;
         const int sc = int(int8_t(scw >> (8 * jj)));
         const uint32_t l0 = jj ? lw.z : lw.x, l1 = jj ? lw.w : lw.y, h = jj ? hw.y : hw.x;
-        const uint4 ya = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + 8 * j);
-        const uint4 yb = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + 8 * j + 4);
+        const uint4 ya = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + y6_word(j, 0));
+        const uint4 yb = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + y6_word(j, 4));
         const uint32_t Y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
         uint32_t g[4];
         g[0] = (l0 & m4) | ((h << 4) & m2);
