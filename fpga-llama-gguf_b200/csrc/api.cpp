@@ -487,6 +487,43 @@ int exec_elementwise(b200q_ctx *c, const Pass &p) {
     return 0;
 }
 
+int exec_rowops(b200q_ctx *c, const Pass &p) {
+    RowOpsArgs a;
+    float *A = c->act;
+    unsigned row0 = 0;
+    for (const auto &jb : p.rowjobs) {
+        RowJobArgs &J = a.job[a.n_jobs++];
+        const uint32_t *nc = jb.data(), *rc = jb.data() + 8;
+        J.row0 = row0;
+        if (nc[0] == 2) {
+            J.norm = true;
+            J.n = nc[1];
+            J.x = A + nc[2];
+            J.w = (nc[7] & 2u) ? nullptr : A + nc[3];
+            J.y = A + nc[4];
+            J.eps = *reinterpret_cast<const float *>(&nc[5]);
+            J.rows = nc[6] ? nc[6] : 1u;
+            const unsigned stride = (nc[7] >> 8) & 0xffffu;
+            J.xstride = stride ? stride * 16 : nc[1];
+            J.flags = nc[7] & 3u;
+        }
+        if (rc[0] == 10) {
+            J.nd = rc[1];
+            J.rx = A + rc[2];
+            J.cs = A + rc[3];
+            J.ry = A + rc[4];
+            J.ne0 = rc[5];
+            J.rows = rc[6];
+        }
+        row0 += J.rows;
+    }
+    a.total_rows = row0;
+    a.pw = take_wait(c);
+    CUDA_TRY(c, launch_rowops(a, c->stream, c->pdl));
+    ++c->launches;
+    return 0;
+}
+
 int exec_gdn(b200q_ctx *c, const Pass &p) {
     const uint32_t *cmd = p.cmd[0], *ext = p.cmd[1], *ext2 = p.cmd[2];
     float *A = c->act;
@@ -557,13 +594,20 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         t.scale = 1.0f / std::sqrt(float(t.head_dim));
         t.chunk = attn_chunk(c->kv_ctx, t.n_kv_head, unsigned(c->sms));
         t.max_chunks = (c->kv_ctx + t.chunk - 1) / t.chunk;
-        if (size_t(t.n_head) * t.max_chunks * (t.head_dim + 2) > kAttnPartFloats)
+        if (size_t(t.n_head) * t.max_chunks * (t.head_dim + 4) > kAttnPartFloats)
             return set_err(c, B200Q_ERR_ARG, "ATTN: n_head x kv_ctx x head_dim too large for the chunk buffer");
         if (attn_smem_bytes(t.n_head, t.n_kv_head, t.head_dim, t.chunk, t.max_chunks) > 200 * 1024)
             return set_err(c, B200Q_ERR_ARG, "ATTN: the chunk does not fit in shared memory");
         t.part = c->attn_part;
         t.counters = c->dstatus + kSyncAttnWord;
         t.err = c->dstatus + 1;
+        if (p.attn_gate) {  // SILU_MUL (sigmoid) of the output, applied in the merge (row 0: contiguous g)
+            const uint32_t *g = p.gate;
+            t.gate_g = A + g[2];
+            t.gate_y = A + g[4];
+            t.gate_row = g[6] ? g[6] : g[1];
+            t.gate_stride = g[6] ? g[7] : g[1];
+        }
         t.pw = take_wait(c);
         CUDA_TRY(c, launch_attn(t, c->stream, c->pdl));
     } else if (p.op == 13) {
@@ -658,6 +702,7 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
         case PassKind::Elementwise: rc = exec_elementwise(c, p); break;
         case PassKind::Gdn: rc = exec_gdn(c, p); break;
         case PassKind::Ext: rc = exec_ext(c, p); break;
+        case PassKind::RowOps: rc = exec_rowops(c, p); break;
         case PassKind::Nop:
             if (p.nd_store) {  // a deferred RMSNORM whose x or weight changes before its GEMVs: store its row now
                 const DeferredNorm &nd = p.nd;
@@ -1069,7 +1114,7 @@ int b200q_plan(const uint32_t *cmds, unsigned n_cmds, b200q_pass_info *passes, u
             b200q_pass_info &o = passes[k];
             o.first_cmd = p.first;
             o.n_cmds = p.count;
-            o.kind = uint32_t(p.kind);
+            o.kind = p.kind == PassKind::RowOps ? uint32_t(PassKind::Elementwise) : uint32_t(p.kind);
             o.n_members = p.kind == PassKind::Gemv ? p.n_members
                                                    : (p.kind == PassKind::Gdn ? unsigned(p.gdn_with_gemv) + unsigned(p.gdn_with_out) : 0u);
             o.fused_norm = p.from_nd ? (p.nd.materialize ? 2u : 1u) : 0u;
@@ -1182,7 +1227,7 @@ int setup_peers(b200q_ctx *c) {
     CUDA_TRY(c, cudaIpcGetMemHandle(&mine[0], c->act));
     CUDA_TRY(c, cudaIpcGetMemHandle(&mine[1], c->sync));
     static_assert(sizeof(mine) % sizeof(float) == 0, "handles travel as floats");
-    const size_t n = sizeof(mine) / sizeof(float);
+    const size_t n = sizeof(mine) / (sizeof(float));
     float *dev = nullptr;
     CUDA_TRY(c, cudaMalloc(&dev, sizeof(mine) * (size_t(c->world) + 1)));
     CUDA_TRY(c, cudaMemcpy(dev, mine, sizeof(mine), cudaMemcpyHostToDevice));

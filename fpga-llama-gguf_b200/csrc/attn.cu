@@ -162,10 +162,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     }
     __syncthreads();
     // unnormalised chunk output: item (g, vec) per thread
-    const size_t part_stride = size_t(hd) + 2;
+    const size_t part_stride = size_t(hd) + 4;  // hd outputs, maximum, sum, 2 pad (16-byte aligned records)
     for (unsigned it = threadIdx.x; it < G * nvec; it += kAttnThreads) {
         const unsigned g = it / nvec, vec = it % nvec;
         float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 4
         for (unsigned i = 0; i < cn; ++i) {
             float v8[8];
             half8_to_float(reinterpret_cast<const uint4 *>(S.v + size_t(i) * hd)[vec], v8);
@@ -209,14 +210,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         for (unsigned c = lane; c < n_chunks; c += 32) S.w[g * a.max_chunks + c] *= inv;
     }
     __syncthreads();
-    for (unsigned it = threadIdx.x; it < G * hd; it += kAttnThreads) {
-        const unsigned g = it / hd, e = it % hd;
-        const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride + e;
+    // four outputs per thread: one 16-byte load per chunk, all chunks' loads in flight before the sums (in chunk order)
+    const unsigned nv4 = hd / 4;
+    for (unsigned it = threadIdx.x; it < G * nv4; it += kAttnThreads) {
+        const unsigned g = it / nv4, e4 = it % nv4;
+        const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride + 4 * e4;
         const float *w = S.w + g * a.max_chunks;
-        float y = 0.0f;
-#pragma unroll 4
-        for (unsigned c = 0; c < n_chunks; ++c) y = fmaf(w[c], __ldcg(base + c * part_stride), y);
-        a.y[size_t(kvh * G + g) * hd + e] = y;
+        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (unsigned c0m = 0; c0m < n_chunks; c0m += 8) {
+            float4 pv[8];
+#pragma unroll
+            for (unsigned u = 0; u < 8; ++u)
+                if (c0m + u < n_chunks) pv[u] = __ldcg(reinterpret_cast<const float4 *>(base + (c0m + u) * part_stride));
+#pragma unroll
+            for (unsigned u = 0; u < 8; ++u) {
+                if (c0m + u < n_chunks) {
+                    const float wc = w[c0m + u];
+                    y.x = fmaf(wc, pv[u].x, y.x);
+                    y.y = fmaf(wc, pv[u].y, y.y);
+                    y.z = fmaf(wc, pv[u].z, y.z);
+                    y.w = fmaf(wc, pv[u].w, y.w);
+                }
+            }
+        }
+        const size_t o = size_t(kvh * G + g) * hd + 4 * e4;
+        const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (unsigned q = 0; q < 4; ++q) {
+            a.y[o + q] = yv[q];
+            if (a.gate_y) {  // the fused SILU_MUL (sigmoid) on this output element
+                const size_t gi = size_t((o + q) / a.gate_row) * a.gate_stride + (o + q) % a.gate_row;
+                a.gate_y[o + q] = fmul(sigmoid_f32(a.gate_g[gi]), yv[q]);
+            }
+        }
     }
 }
 

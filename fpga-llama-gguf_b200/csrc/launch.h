@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "kernel_args.h"
+#include "plan.h"
 
 namespace b200q {
 
@@ -42,9 +43,32 @@ struct AttnArgs {
     uint16_t *kcache = nullptr, *vcache = nullptr;  // [n_kv_head][kv_ctx][head_dim] F16 each
     float scale = 0.0f;
     unsigned chunk = 16, max_chunks = 0;            // positions per CTA; CTAs per KV head (kv_ctx / chunk)
-    float *part = nullptr;      // [n_head][max_chunks][head_dim + 2] chunk outputs, maximum, sum
+    float *part = nullptr;      // [n_head][max_chunks][head_dim + 4] chunk outputs, maximum, sum, pad
     unsigned *counters = nullptr;  // [n_kv_head] finished chunks (zero between launches)
     unsigned *err = nullptr;       // set when a bounded wait for the chunk copies ran out
+    PeerWait pw;
+    // fused gate (SILU_MUL with the sigmoid flag on y): yg[e] = sigmoid(g[(e / row) * stride + e % row]) * y[e]
+    const float *gate_g = nullptr;
+    float *gate_y = nullptr;
+    unsigned gate_row = 0, gate_stride = 0;
+};
+
+// A run of RMSNORM (stored) / ROPE commands in one launch: one CTA per row of a job; a job is a norm, a ROPE, or a
+// norm followed by the ROPE of the rows it stored.
+struct RowJobArgs {
+    const float *x = nullptr, *w = nullptr;  // norm input rows (xstride floats apart), weight (null: none)
+    float *y = nullptr;                      // norm output rows (n floats apart)
+    unsigned n = 0, xstride = 0, flags = 0;  // RMSNORM flags bits 0..1
+    float eps = 0.0f;
+    const float *rx = nullptr, *cs = nullptr;  // ROPE input rows (the norm's output when both), cos/sin row
+    float *ry = nullptr;
+    unsigned nd = 0, ne0 = 0;                // ROPE dims (0: no ROPE), row length
+    unsigned rows = 0, row0 = 0;             // rows of the job, its first CTA
+    bool norm = false;
+};
+struct RowOpsArgs {
+    RowJobArgs job[kMaxRowJobs];
+    unsigned n_jobs = 0, total_rows = 0;
     PeerWait pw;
 };
 
@@ -72,6 +96,7 @@ cudaError_t launch_get_row(const MatrixView &w, unsigned cols, const float *idx,
                            const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_peer_wait(const PeerWait &pw, cudaStream_t st, bool pdl);
+cudaError_t launch_rowops(const RowOpsArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
 unsigned attn_chunk(unsigned kv_ctx, unsigned n_kv_head, unsigned sms);
 size_t attn_smem_bytes(unsigned n_head, unsigned n_kv_head, unsigned head_dim, unsigned chunk, unsigned max_chunks);

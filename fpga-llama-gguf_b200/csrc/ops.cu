@@ -175,6 +175,46 @@ __global__ void get_row_kernel(const MatrixView w, unsigned cols, const float *i
     }
 }
 
+// ---- RMSNORM / ROPE runs in one launch (same arithmetic as rmsnorm_kernel and rope_kernel) ------------------------
+__global__ void __launch_bounds__(256) rowops_kernel(const RowOpsArgs a) {
+    __shared__ double red[32];
+    __shared__ float scale_s;
+    pdl_wait();
+    pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
+    peer_wait_rows_cta(a.pw);
+    unsigned j = 0;
+    while (j + 1 < a.n_jobs && a.job[j + 1].row0 <= blockIdx.x) ++j;
+    const RowJobArgs &J = a.job[j];
+    const unsigned r = blockIdx.x - J.row0;
+    if (J.norm) {
+        const float *xr = J.x + size_t(r) * J.xstride;
+        float *yr = J.y + size_t(r) * J.n;
+        const float s = cta_norm_scale(xr, J.n, J.eps, J.flags & 1u, red, &scale_s);
+        for (unsigned i = threadIdx.x; i < J.n; i += blockDim.x) {
+            const float t = fmul(xr[i], s);
+            yr[i] = (J.flags & 2u) ? t : fmul(t, J.w[i]);
+        }
+        __syncthreads();
+    }
+    if (J.nd) {
+        const float *xr = J.rx + size_t(r) * J.ne0;
+        float *yr = J.ry + size_t(r) * J.ne0;
+        const unsigned half = J.nd / 2, per_row = half + (J.ne0 - J.nd);
+        for (unsigned i = threadIdx.x; i < per_row; i += blockDim.x) {
+            if (i < half) {
+                const float x0 = xr[i], x1 = xr[i + half], c = J.cs[2 * i], sn = J.cs[2 * i + 1];
+                const float va = fsub(fmul(x0, c), fmul(x1, sn));
+                const float vb = fadd(fmul(x0, sn), fmul(x1, c));
+                yr[i] = va;
+                yr[i + half] = vb;
+            } else {
+                const unsigned k = J.nd + (i - half);
+                yr[k] = xr[k];
+            }
+        }
+    }
+}
+
 // ---- row-sharded passes: the wait for the peers' rows as a kernel of its own ----------------------------------------
 // (before a copy or a host read of act that no kernel in between covers)
 __global__ void peer_wait_kernel(const PeerWait pw) {
@@ -249,6 +289,12 @@ cudaError_t launch_peer_wait(const PeerWait &pw, cudaStream_t st, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(32), 0, st, pdl, attr);
     return cudaLaunchKernelEx(&cfg, peer_wait_kernel, pw);
+}
+
+cudaError_t launch_rowops(const RowOpsArgs &a, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_cfg(dim3(a.total_rows), dim3(256), 0, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, rowops_kernel, a);
 }
 
 }  // namespace b200q

@@ -140,6 +140,128 @@ void pass_writes(const Pass &p, std::vector<std::pair<size_t, size_t>> &w) {
 
 }  // namespace
 
+// ---- fusions of consecutive small passes (same results as running them one by one) --------------------------------
+struct Span {
+    size_t off, n;
+};
+bool spans_meet(const Span &a, const Span &b) { return a.n && b.n && ranges_meet(a.off, a.n, b.off, b.n); }
+
+// Reads and writes (act floats) of a stored RMSNORM / a ROPE command.
+void norm_spans(const uint32_t *c, std::vector<Span> &rd, std::vector<Span> &wr) {
+    const unsigned n = c[1], rows = c[6] ? c[6] : 1u, stride = (c[7] >> 8) & 0xffffu;
+    rd.push_back({c[2], stride ? size_t(rows - 1) * stride * 16 + n : size_t(rows) * n});
+    if ((c[7] & 2u) == 0) rd.push_back({c[3], n});
+    wr.push_back({c[4], size_t(rows) * n});
+}
+void rope_spans(const uint32_t *c, std::vector<Span> &rd, std::vector<Span> &wr) {
+    rd.push_back({c[2], size_t(c[5]) * c[6]});
+    rd.push_back({c[3], c[1]});
+    wr.push_back({c[4], size_t(c[5]) * c[6]});
+}
+bool is_rowop(const Pass &p) {
+    return p.kind == PassKind::Elementwise && (p.op == 10 || (p.op == 2 && (p.cmd[0][7] & 4u) == 0));
+}
+
+// Runs of RMSNORM / ROPE passes become one RowOps pass: a ROPE whose x is exactly the rows an earlier RMSNORM of the
+// run stored joins that norm's job; all jobs must be independent (no job writes what another reads or writes).
+void fuse_rowops(std::vector<Pass> &passes) {
+    std::vector<Pass> out;
+    size_t i = 0;
+    while (i < passes.size()) {
+        if (!is_rowop(passes[i])) {
+            out.push_back(passes[i++]);
+            continue;
+        }
+        std::vector<std::array<uint32_t, 16>> jobs;
+        std::vector<std::vector<Span>> jrd, jwr;
+        size_t j = i;
+        for (; j < passes.size() && is_rowop(passes[j]); ++j) {
+            const uint32_t *c = passes[j].cmd[0];
+            std::vector<Span> rd, wr;
+            int link = -1;
+            if (passes[j].op == 10) {
+                rope_spans(c, rd, wr);
+                for (size_t k = 0; k < jobs.size(); ++k) {
+                    const uint32_t *nc = jobs[k].data();
+                    if (nc[0] == 2 && jobs[k][8] == 0 && nc[4] == c[2] && (nc[6] ? nc[6] : 1u) == c[6] &&
+                        nc[1] == c[5])
+                        link = int(k);
+                }
+            } else {
+                norm_spans(c, rd, wr);
+            }
+            // independence from the other jobs (the linked norm's stored rows are this ROPE's own input)
+            bool ok = true;
+            for (size_t k = 0; k < jobs.size() && ok; ++k) {
+                for (const Span &w : wr) {
+                    for (const Span &r : jrd[k]) ok = ok && !spans_meet(w, r);
+                    for (const Span &x : jwr[k]) ok = ok && !spans_meet(w, x);
+                }
+                for (const Span &r : rd)
+                    for (const Span &x : jwr[k])
+                        if (!(int(k) == link && r.off == x.off && r.n == x.n)) ok = ok && !spans_meet(r, x);
+            }
+            if (link >= 0) {  // within the job: the ROPE writes nothing the norm reads
+                for (const Span &w : wr)
+                    for (const Span &r : jrd[size_t(link)]) ok = ok && !spans_meet(w, r);
+            }
+            if (link < 0 && jobs.size() == kMaxRowJobs) ok = false;  // one launch holds at most kMaxRowJobs jobs
+            if (!ok) break;
+            if (link >= 0) {
+                std::memcpy(jobs[size_t(link)].data() + 8, c, 32);
+                for (const Span &r : rd) jrd[size_t(link)].push_back(r);
+                for (const Span &w : wr) jwr[size_t(link)].push_back(w);
+            } else {
+                std::array<uint32_t, 16> jb{};
+                std::memcpy(jb.data() + (passes[j].op == 10 ? 8 : 0), c, 32);
+                jobs.push_back(jb);
+                jrd.push_back(rd);
+                jwr.push_back(wr);
+            }
+        }
+        if (j - i < 2) {
+            out.push_back(passes[i++]);
+            continue;
+        }
+        Pass f = passes[i];
+        f.kind = PassKind::RowOps;
+        f.count = passes[j - 1].first + passes[j - 1].count - passes[i].first;
+        f.rowjobs = jobs;
+        out.push_back(f);
+        i = j;
+    }
+    passes.swap(out);
+}
+
+// ATTN followed by a sigmoid SILU_MUL of its output (the gated attention output): the gate is applied in the
+// attention merge. Its g rows must not meet the attention output or the gated output; the gated output is the
+// attention output itself or apart from it.
+void fuse_attn_gate(std::vector<Pass> &passes) {
+    std::vector<Pass> out;
+    for (size_t i = 0; i < passes.size(); ++i) {
+        Pass p = passes[i];
+        if (p.kind == PassKind::Ext && p.op == 12 && i + 1 < passes.size() &&
+            passes[i + 1].kind == PassKind::Elementwise && passes[i + 1].op == 4) {
+            const uint32_t *a = p.cmd[0], *g = passes[i + 1].cmd[0];
+            const unsigned nh = a[1] & 0xffu, hd = (a[1] >> 16) * 16u, n = g[1], row = g[6], stride = g[7];
+            const Span ya{a[5], size_t(nh) * hd}, yg{g[4], n};
+            const Span gs{g[2], row ? size_t(n / row - 1) * stride + row : n};
+            const bool ok = (g[5] & 1u) && g[3] == a[5] && n == nh * hd && !spans_meet(gs, ya) && !spans_meet(gs, yg) &&
+                            (yg.off == ya.off || !spans_meet(yg, ya));
+            if (ok) {
+                p.attn_gate = true;
+                std::memcpy(p.gate, g, 32);
+                p.count += passes[i + 1].count;
+                out.push_back(p);
+                ++i;
+                continue;
+            }
+        }
+        out.push_back(p);
+    }
+    passes.swap(out);
+}
+
 Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
     Plan plan;
     if (n_cmds > 128) {
@@ -464,6 +586,8 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
                 if (q.kind == PassKind::Nop && q.op == 2 && q.nd.cmd == p.nd.cmd && q.nd_store) p.nd.materialize = true;
         }
     }
+    fuse_rowops(plan.passes);
+    fuse_attn_gate(plan.passes);
     return plan;
 }
 

@@ -11,6 +11,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <array>
 #include <vector>
 
 namespace b200q {
@@ -41,12 +42,15 @@ struct Limits {
     const std::vector<WeightInfo> *weights = nullptr;
 };
 
+constexpr unsigned kMaxRowJobs = 8;  // jobs of one RowOps launch
+
 enum class PassKind : uint32_t {
     Gemv = 1,       // GEMV group (1..4 members) with epilogues
     Elementwise,    // RMSNORM (stored), ADD, MUL, SILU_MUL, UNARY, CONV, ROPE
     Gdn,            // GDN step (+ WITH_GEMV GEMV, + WITH_OUT GEMV with ADD)
     Nop,            // STATE_LOAD, TRACE, deferred RMSNORM (no launch of its own)
     Ext,            // ATTN, ARGMAX, GET_ROW
+    RowOps,         // consecutive RMSNORM (stored) / ROPE commands run as one launch (reported as Elementwise)
 };
 
 enum Epi : uint32_t { EpiNone = 0, EpiSwigluG = 1, EpiSwigluU = 2, EpiConv = 3, EpiAdd = 4 };
@@ -90,6 +94,11 @@ struct Pass {
     bool nd_store = false;
     // an input range that a kernel of this pass also writes: copied to scratch first
     bool snapshot = false;
+    // RowOps: jobs of one launch, each an RMSNORM (stored) and/or the ROPE of its output (op word 0: absent)
+    std::vector<std::array<uint32_t, 16>> rowjobs;
+    // ATTN followed by SILU_MUL (sigmoid) of its output: the gate command, applied in the attention merge
+    bool attn_gate = false;
+    uint32_t gate[8] = {};
 };
 
 struct Plan {

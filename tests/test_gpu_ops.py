@@ -226,3 +226,52 @@ def test_argmax_first_index_of_the_maximum(ctx, b2, orc, case):
     cl = b2.cmd_list(b2.argmax(n, 0, out))
     got, ref, _, _ = _run_both(ctx, orc, cl, act)
     assert np.array_equal(_bits(got[out:out + 2]), _bits(ref[out:out + 2]))
+
+
+def test_attention_layer_fused_norm_rope_gate(ctx, b2, orc):
+    """q/k per-head RMSNORM + NEOX ROPE (one fused launch) and ATTN with the sigmoid gate in its merge, against the
+    oracle running the six commands one by one: the normed and roped q/k rows bit-exact, the attention output and the
+    gated output within 1e-4 of the weighted mean of |v| (times the gate)."""
+    r = rng(66)
+    nh, nkv, hd, kv_ctx, pos = 16, 4, 256, 640, 200
+    QG, K, V, QN, KN, QR, KR = 0, 8192, 9216, 10240, 14336, 15360, 19456
+    YA, YG, CS, W, WK, POSW = 20480, 24576, 28672, 28800, 29056, 29312
+    act = np.zeros(29440, np.float32)
+    act[QG:QG + 2 * nh * hd] = r.normal(0, 1, 2 * nh * hd)
+    act[K:K + nkv * hd] = r.normal(0, 1, nkv * hd)
+    act[V:V + nkv * hd] = r.normal(0, 1, nkv * hd)
+    act[W:W + hd] = r.normal(1, 0.1, hd)
+    act[WK:WK + hd] = r.normal(1, 0.1, hd)
+    ang = pos * 1e7 ** (-2.0 * np.arange(32) / 64)
+    act[CS:CS + 64:2], act[CS + 1:CS + 64:2] = np.cos(ang), np.sin(ang)
+    act[POSW] = np.array([pos], np.uint32).view(np.float32)[0]
+    kv = np.zeros(2 * nkv * kv_ctx * hd, np.uint16)
+    pre = r.normal(0, 1, (2, nkv, kv_ctx, hd)).astype(np.float16)
+    pre[:, :, pos:, :] = 0
+    kv[:] = pre.view(np.uint16).reshape(-1)
+    ctx.write_kv(0, kv)
+    cl = b2.cmd_list(
+        b2.rmsnorm(hd, QG, W, QN, 1e-6, rows=nh, stride_words=2 * hd // 16),
+        b2.rmsnorm(hd, K, WK, KN, 1e-6, rows=nkv),
+        b2.rope(64, QN, CS, QR, hd, nh), b2.rope(64, KN, CS, KR, hd, nkv),
+        b2.attn(nh, nkv, hd, QR, KR, V, YA, POSW, 0),
+        b2.silu_mul(nh * hd, QG + hd, YA, YG, sigmoid=True, row=hd, stride=2 * hd))
+    st, passes = b2.plan(cl)
+    assert st == 0 and len(passes) == 2
+    got, ref, _, _ = _run_both(ctx, orc, cl, act, kv_ctx=kv_ctx, kv=kv.copy())
+    for off, n in ((QN, nh * hd), (KN, nkv * hd), (QR, nh * hd), (KR, nkv * hd)):
+        assert np.array_equal(_bits(got[off:off + n]), _bits(ref[off:off + n]))
+    cache = kv.view(np.float16).reshape(2, nkv, kv_ctx, hd).astype(np.float64)
+    cache[0, :, pos] = ref[KR:KR + nkv * hd].reshape(nkv, hd).astype(np.float16)
+    cache[1, :, pos] = act[V:V + nkv * hd].reshape(nkv, hd).astype(np.float16)
+    mag = np.zeros(nh * hd)
+    for h in range(nh):
+        kk, vv = cache[0, h // (nh // nkv), :pos + 1], cache[1, h // (nh // nkv), :pos + 1]
+        sc = kk @ ref[QR + h * hd:QR + (h + 1) * hd].astype(np.float64) / np.sqrt(hd)
+        p = np.exp(sc - sc.max())
+        mag[h * hd:(h + 1) * hd] = (p / p.sum()) @ np.abs(vv)
+    ya_err = np.abs(got[YA:YA + nh * hd].astype(np.float64) - ref[YA:YA + nh * hd])
+    assert (ya_err <= 1e-4 * mag).all()
+    gate = 1 / (1 + np.exp(-act[QG:QG + 2 * nh * hd].reshape(nh, 2 * hd)[:, hd:].reshape(-1).astype(np.float64)))
+    yg_err = np.abs(got[YG:YG + nh * hd].astype(np.float64) - ref[YG:YG + nh * hd])
+    assert (yg_err <= 1e-4 * mag * gate + 1e-7 * np.abs(ref[YG:YG + nh * hd])).all()

@@ -138,3 +138,31 @@ def test_deferred_norm_stored_only_when_x_changes_before_a_consumer(b2):
         assert st == 0, name
         gp = [p for p in passes if p["kind"] == "gemv"][0]
         assert gp["fused_norm"] and gp["stored_norm"] == stored, name
+
+
+def test_small_passes_fuse_into_one_launch(b2):
+    """Consecutive stored RMSNORM / ROPE commands run as one launch when independent (a ROPE of a norm's stored rows
+    joins that norm), and ATTN takes a following sigmoid SILU_MUL of its output into its merge; a ROPE that reads rows
+    another job of the run writes ends the run."""
+    nh, nkv, hd = 4, 2, 128
+    QG, K, QN, KN, QR, KR, CS, YA, YG, POS = 0, 1024, 1280, 1792, 2048, 2560, 2816, 3072, 3584, 4096
+    W = 4352
+    layer = b2.cmd_list(
+        b2.rmsnorm(hd, QG, W, QN, 1e-6, rows=nh, stride_words=2 * hd // 16),
+        b2.rmsnorm(hd, K, W, KN, 1e-6, rows=nkv),
+        b2.rope(32, QN, CS, QR, hd, nh), b2.rope(32, KN, CS, KR, hd, nkv),
+        b2.attn(nh, nkv, hd, QR, KR, K, YA, POS, 0),
+        b2.silu_mul(nh * hd, QG + hd, YA, YG, sigmoid=True, row=hd, stride=2 * hd))
+    st, passes = b2.plan(layer)
+    assert st == 0
+    assert [(p["kind"], p["first"], p["count"]) for p in passes] == [("elementwise", 0, 4), ("ext", 4, 2)]
+    # the second ROPE reads the rows the first norm writes: the run stops before it
+    clash = b2.cmd_list(
+        b2.rmsnorm(hd, QG, W, QN, 1e-6, rows=nh, stride_words=2 * hd // 16),
+        b2.rope(32, K, CS, KR, hd, nkv), b2.rope(32, QN, CS, QN, hd, nkv))
+    st, passes = b2.plan(clash)
+    assert st == 0 and [(p["first"], p["count"]) for p in passes] == [(0, 2), (2, 1)]
+    # a gate whose g rows meet the attention output stays a separate pass
+    st, passes = b2.plan(b2.cmd_list(b2.attn(nh, nkv, hd, QR, KR, K, YA, POS, 0),
+                                     b2.silu_mul(nh * hd, YA, YA, YG, sigmoid=True)))
+    assert st == 0 and [p["count"] for p in passes] == [1, 1]
