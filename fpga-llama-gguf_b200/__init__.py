@@ -189,6 +189,7 @@ def lib() -> ctypes.CDLL:
         "b200q_comm_unique_id": (I, [P]),
         "b200q_comm_init": (I, [P, I, I, P]),
         "b200q_comm_world": (I, [P]),
+        "b200q_row_slice": (I, [U, U, I, I, ctypes.POINTER(U), ctypes.POINTER(U)]),
         "b200q_layout": (I, [U, U, U, U, P]),
         "b200q_repack_host": (I, [P, U, U, U, U, P]),
         "b200q_unpack_row_host": (I, [P, U, U, U, U, U, P]),
@@ -210,7 +211,7 @@ EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream",
             "b200q_graph_launch", "b200q_graph_launch_many", "b200q_graph_destroy", "b200q_graph_kernel_count", "b200q_plan",
             "b200q_debug_quantize", "b200q_debug_block_sums", "b200q_quantize_noalloc", "b200q_comm_unique_id",
             "b200q_comm_init",
-            "b200q_comm_world", "b200q_layout", "b200q_repack_host", "b200q_unpack_row_host"]
+            "b200q_comm_world", "b200q_row_slice", "b200q_layout", "b200q_repack_host", "b200q_unpack_row_host"]
 
 
 class _LayoutInfo(ctypes.Structure):
@@ -286,6 +287,15 @@ def quantize_noalloc(device: int, x_ptr: int, n: int, fmt: int, norm_w_ptr: int 
     if rc != 0:
         raise B200QError(rc, err.value.decode() or ERR.get(rc, str(rc)))
     return q, scales, bs
+
+
+def row_slice(rows: int, world: int, rank: int, flags: int = 0) -> tuple:
+    """The rows (r0, r1) of a matrix that `rank` keeps in a row-sharded context of `world` ranks (host only)."""
+    r0, r1 = ctypes.c_uint(), ctypes.c_uint()
+    rc = lib().b200q_row_slice(rows, flags, world, rank, ctypes.byref(r0), ctypes.byref(r1))
+    if rc != 0:
+        raise B200QError(rc, "bad world / rank")
+    return int(r0.value), int(r1.value)
 
 
 def gguf_row_bytes(cols: int, fmt: int) -> int:

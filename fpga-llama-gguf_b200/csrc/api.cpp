@@ -762,10 +762,6 @@ int check_ctx(b200q_ctx *c) {
     return 0;
 }
 
-bool shardable(const b200q_ctx *c, unsigned rows, unsigned flags) {
-    return c->world > 1 && !(flags & B200Q_UPLOAD_REPLICATE) && rows % (16u * unsigned(c->world)) == 0;
-}
-
 }  // namespace
 
 // =================================================================================================================
@@ -885,6 +881,18 @@ size_t b200q_weight_device_bytes(unsigned rows, unsigned cols, unsigned format) 
     return device_layout(rows, cols, format, 148).total;
 }
 
+int b200q_row_slice(unsigned rows, unsigned flags, int world, int rank, unsigned *r0, unsigned *r1) {
+    if (!r0 || !r1 || world < 1 || rank < 0 || rank >= world) return B200Q_ERR_ARG;
+    *r0 = 0;
+    *r1 = rows;
+    if (world > 1 && !(flags & B200Q_UPLOAD_REPLICATE) && rows % (16u * unsigned(world)) == 0) {
+        const unsigned per = rows / unsigned(world);
+        *r0 = per * unsigned(rank);
+        *r1 = *r0 + per;
+    }
+    return 0;
+}
+
 int b200q_upload_weight_ex(b200q_ctx *c, const void *gguf, unsigned rows, unsigned cols, unsigned format,
                            unsigned block_cols, unsigned flags, uint64_t *w_off) {
     int rc = check_ctx(c);
@@ -895,11 +903,7 @@ int b200q_upload_weight_ex(b200q_ctx *c, const void *gguf, unsigned rows, unsign
         (block_cols != 0 && block_cols != 256))
         return set_err(c, B200Q_ERR_ARG, "upload: bad shape or format");
     unsigned r0 = 0, r1 = rows;
-    if (shardable(c, rows, flags)) {
-        const unsigned per = rows / unsigned(c->world);
-        r0 = per * unsigned(c->rank);
-        r1 = r0 + per;
-    }
+    b200q_row_slice(rows, flags, c->world, c->rank, &r0, &r1);
     const DeviceLayout L = device_layout(r1 - r0, cols, format, unsigned(c->sms));
     if (c->wused + L.total > c->wbytes) return set_err(c, B200Q_ERR_NOMEM, "weight arena full");
     std::vector<uint8_t> host(L.total);

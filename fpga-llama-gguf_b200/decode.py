@@ -314,11 +314,11 @@ class HybridDecoder:
     def context_config(self, world: int = 1) -> dict:
         """Context arguments that fit this model on one rank of a world-way row-sharded run."""
         s = self.s
-        from . import weight_device_bytes
+        from . import row_slice, weight_device_bytes
         wb = 0
         for name, fmt, rows, cols, bc, fl, _ in self.matrices():
-            r = rows if (fl & UPLOAD_REPLICATE) or rows % (16 * world) else rows // world
-            wb += (weight_device_bytes(r, cols, fmt) + 255) // 256 * 256
+            r0, r1 = row_slice(rows, world, 0, fl)
+            wb += (weight_device_bytes(r1 - r0, cols, fmt) + 255) // 256 * 256
         return dict(weight_bytes=wb + (64 << 20), act_floats=self.L.size, state_rows=s.n_gdn * s.gdn_rows,
                     kv_bytes=s.n_attn * s.kv_slot_bytes, kv_ctx=s.kv_ctx)
 

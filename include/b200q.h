@@ -272,6 +272,9 @@ B200Q_API int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]);
  * environment variable B200Q_PEER=1 the GEMV kernels store their rows straight into every peer's act over NVLink
  * (CUDA IPC mappings made here) and the next kernel waits for the peers' flags (bounded waits). */
 B200Q_API int b200q_comm_init(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]);
+/* The rows [*r0, *r1) of a rows-row matrix that rank `rank` of `world` keeps at upload (host only): a slice of
+ * rows / world when rows divide by 16 x world and flags has no B200Q_UPLOAD_REPLICATE, else all rows. */
+B200Q_API int b200q_row_slice(unsigned rows, unsigned flags, int world, int rank, unsigned *r0, unsigned *r1);
 B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
 
 #ifdef __cplusplus

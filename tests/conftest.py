@@ -63,5 +63,17 @@ def ctx(b2):
     c.close()
 
 
+@pytest.fixture
+def scratch(request):
+    """A fresh directory under tests/_scratch (git-ignored) for files the test's child processes exchange; also the
+    TMPDIR of those processes. Removed after the test."""
+    import shutil
+    d = os.path.join(ROOT, "tests", "_scratch", f"{request.node.name}-{os.getpid()}".replace("/", "_"))
+    shutil.rmtree(d, ignore_errors=True)
+    os.makedirs(d)
+    yield d
+    shutil.rmtree(d, ignore_errors=True)
+
+
 def rng(*salt):
     return np.random.default_rng([0x5EED, *salt])

@@ -32,7 +32,7 @@ def _run(world: int, out: str, n_tokens: int, extra_env=None):
     procs = []
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
-                   NCCL_NVLS_ENABLE="0", **(extra_env or {}))
+                   NCCL_NVLS_ENABLE="0", TMPDIR=out, **(extra_env or {}))
         procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "_mgpu_worker.py"), out, str(n_tokens)],
                                       env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
     logs = []
@@ -50,10 +50,10 @@ def _run(world: int, out: str, n_tokens: int, extra_env=None):
 @pytest.mark.gpu
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("mode", ["peer", "nccl"])
-def test_two_gpu_sharded_decode_is_bit_identical_to_one_gpu(tmp_path, mode):
-    one, two = tmp_path / "one", tmp_path / "two"
-    one.mkdir()
-    two.mkdir()
+def test_two_gpu_sharded_decode_is_bit_identical_to_one_gpu(scratch, mode):
+    one, two = os.path.join(scratch, "one"), os.path.join(scratch, "two")
+    os.makedirs(one)
+    os.makedirs(two)
     a = _run(1, str(one), 6)
     b = _run(2, str(two), 6, {"B200Q_PEER": "1" if mode == "peer" else "0"})
     assert list(a["toks"]) == list(b["toks"])
