@@ -4,11 +4,11 @@
 //   plus (Q5_K) the mins sum sum_j bsum16_j * m_(j/2); per row, in super-block order,
 //   sums[l] += (d_w * d_x) * float(aux[l]), Q5_K: sumf -= (dmin_w * d_x) * float(mins); then sumf += sums[0..7].
 //
-// Same tile pipeline as gemv_q8.cu (bulk copies into a stage ring, issued before the wait on the previous kernel).
-// Eight threads share one (row, super-block): each takes 1/8 of it (Q5_K: one 32-element sub-block, Q6_K: two
-// 16-element sub-blocks), computes partial lane sums with dp4a / dp2a on the permuted quant words of the device
-// layout, and the eight partials are added exactly with shuffles (lane p ends with aux[p]). One thread per row then
-// applies the FP32 fold in super-block order.
+// A producer warp streams tiles (32 rows x C super-blocks, layout.h) with bulk copies into a stage ring; compute
+// warp w takes super-block w of the tile and each of its lanes one row: the lane forms the whole super-block's
+// integer sums from the packed quant words (dp2a / dp4a; every lane of the warp reads the same activation words, a
+// shared-memory broadcast) and writes them as one record; the fold warp adds each row's records in super-block
+// order. (An earlier mapping of 8 threads per super-block with shuffle reductions was instruction-bound at ~2 TB/s.)
 //
 // Roofline: HBM bandwidth, 176 (Q5_K) / 210 (Q6_K) bytes per 256 weights.
 #include "gemv_common.cuh"
@@ -59,120 +59,120 @@ __device__ __forceinline__ void scale_min_k4(unsigned j, const uint8_t *q, int &
     }
 }
 
-// Exact sum of the 8 partial lane-sum vectors of an aligned group of 8 lanes; lane p of the group gets aux[p].
-__device__ __forceinline__ int reduce8(int v[8]) {
-    const unsigned lane = threadIdx.x & 7u;
-    int a1[4], a2[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const bool up = (lane & 4u) != 0;
-        const int mine = up ? v[i + 4] : v[i], other = up ? v[i] : v[i + 4];
-        a1[i] = mine + __shfl_xor_sync(0xffffffffu, other, 4);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const bool up = (lane & 2u) != 0;
-        const int mine = up ? a1[i + 2] : a1[i], other = up ? a1[i] : a1[i + 2];
-        a2[i] = mine + __shfl_xor_sync(0xffffffffu, other, 2);
-    }
-    const bool up = (lane & 1u) != 0;
-    const int mine = up ? a2[1] : a2[0], other = up ? a2[0] : a2[1];
-    return mine + __shfl_xor_sync(0xffffffffu, other, 1);
-}
-
-// Q5_K part p = sub-block j of (row, super-block) item i of the tile.
-__device__ __forceinline__ void part_q5k(const uint8_t *qs, const uint8_t *dm, unsigned j, unsigned sb,
-                                         const XImage &X, const uint32_t *y5, int aux[8], int &mins) {
-    const uint4 l0 = *reinterpret_cast<const uint4 *>(qs + 32 * (j / 2));
-    const uint4 l1 = *reinterpret_cast<const uint4 *>(qs + 32 * (j / 2) + 16);
-    const uint4 h0 = *reinterpret_cast<const uint4 *>(qs + 128);
-    const uint4 h1 = *reinterpret_cast<const uint4 *>(qs + 144);
-    const uint32_t QL[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-    const uint32_t QH[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    const uint4 ya = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + y5_word(j, 0));
-    const uint4 yb = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + y5_word(j, 4));
-    const uint32_t Y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
-    int sc, m;
-    scale_min_k4(j, dm, sc, m);
-#pragma unroll
-    for (int l = 0; l < 8; ++l) {
-        const uint32_t lo = (j & 1) ? ((QL[l] >> 4) & 0x0F0F0F0Fu) : (QL[l] & 0x0F0F0F0Fu);
-        const uint32_t hi = ((QH[l] >> j) & 0x01010101u) << 4;
-        aux[l] = sc * __dp4a(int(lo | hi), int(Y[l]), 0);
-    }
-    mins = (X.b[sb * 16 + 2 * j] + X.b[sb * 16 + 2 * j + 1]) * m;
-}
-
-// Q6_K part p = sub-blocks 2p, 2p + 1 of (row, super-block).
-__device__ __forceinline__ void part_q6k(const uint8_t *qs, const uint8_t *dm, unsigned p, unsigned sb,
-                                         const uint32_t *y6, int aux[8]) {
-    const uint4 lw = *reinterpret_cast<const uint4 *>(qs + 16 * p);       // QL words 4p .. 4p + 3
-    const uint2 hw = *reinterpret_cast<const uint2 *>(qs + 128 + 8 * p);  // QH words 2p, 2p + 1
-    const uint16_t scw = *reinterpret_cast<const uint16_t *>(dm + 2 * p);
+// Q6_K super-block of one row: packed quant words at q + 512 k (k = 0..11; QL words 0..31, QH words 32..47, layout.cpp
+// q6k_pack), 16 int8 scales at sc. Group j (16 elements): QL words 2j, 2j + 1 and QH word j give the four dp2a words
+// G(j, p) holding elements (2p, 2p + 8, 2p + 1, 2p + 9) of the group, as 6-bit values minus 32.
+__device__ __forceinline__ void sb_q6k(const uint8_t *q, const uint8_t *sc, unsigned sb, const uint32_t *y6,
+                                       int aux[8]) {
     const uint32_t m4 = 0x0F0F0F0Fu, m2 = 0x30303030u;
+    uint32_t QH[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint4 h = *reinterpret_cast<const uint4 *>(q + (8 + k) * 512);
+        QH[4 * k] = h.x, QH[4 * k + 1] = h.y, QH[4 * k + 2] = h.z, QH[4 * k + 3] = h.w;
+    }
+    const uint4 s4 = *reinterpret_cast<const uint4 *>(sc);
+    const uint32_t SW[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
     for (int l = 0; l < 8; ++l) aux[l] = 0;
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-        const unsigned j = 2 * p + jj;
-        const int sc = int(int8_t(scw >> (8 * jj)));
-        const uint32_t l0 = jj ? lw.z : lw.x, l1 = jj ? lw.w : lw.y, h = jj ? hw.y : hw.x;
-        const uint4 ya = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + y6_word(j, 0));
-        const uint4 yb = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + y6_word(j, 4));
-        const uint32_t Y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
-        uint32_t g[4];
-        g[0] = (l0 & m4) | ((h << 4) & m2);
-        g[1] = ((l0 >> 4) & m4) | ((h << 2) & m2);
-        g[2] = (l1 & m4) | (h & m2);
-        g[3] = ((l1 >> 4) & m4) | ((h >> 2) & m2);
+    for (int jp = 0; jp < 8; ++jp) {
+        const uint4 ql = *reinterpret_cast<const uint4 *>(q + jp * 512);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int a = int(__vsub4(g[q], 0x20202020u));  // bytes w - 32 in -32..31
-            aux[2 * q] += sc * __dp2a_lo(int(Y[2 * q]), a, 0);
-            aux[2 * q + 1] += sc * __dp2a_hi(int(Y[2 * q + 1]), a, 0);
+        for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * jp + jj;
+            const uint32_t l0 = jj ? ql.z : ql.x, l1 = jj ? ql.w : ql.y, h = QH[j];
+            const int scj = int(int8_t(SW[j / 4] >> (8 * (j % 4))));
+            const uint4 ya = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + y6_word(j, 0));
+            const uint4 yb = *reinterpret_cast<const uint4 *>(y6 + sb * 128 + y6_word(j, 4));
+            const uint32_t Y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
+            uint32_t g[4];
+            g[0] = (l0 & m4) | ((h << 4) & m2);
+            g[1] = ((l0 >> 4) & m4) | ((h << 2) & m2);
+            g[2] = (l1 & m4) | (h & m2);
+            g[3] = ((l1 >> 4) & m4) | ((h >> 2) & m2);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const int a = int(__vsub4(g[p], 0x20202020u));  // bytes w - 32 in -32..31
+                aux[2 * p] += scj * __dp2a_lo(int(Y[2 * p]), a, 0);
+                aux[2 * p + 1] += scj * __dp2a_hi(int(Y[2 * p + 1]), a, 0);
+            }
         }
     }
 }
 
-// One tile: items (row, super-block) x 8 parts.
+// Q5_K super-block of one row: packed quant words at q + 512 k (k = 0..9; QL words 0..31, QH words 32..39, layout.cpp
+// q5k_pack), 12 packed 6-bit scales / mins at dm. Sub-block j, class l: the 4 elements 32j + l + 8b, 5-bit values.
+__device__ __forceinline__ void sb_q5k(const uint8_t *q, const uint8_t *dm, unsigned sb, const XImage &X,
+                                       const uint32_t *y5, int aux[8], int &mins) {
+    const uint32_t m4 = 0x0F0F0F0Fu;
+    uint32_t QH[8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint4 h = *reinterpret_cast<const uint4 *>(q + (8 + k) * 512);
+        QH[4 * k] = h.x, QH[4 * k + 1] = h.y, QH[4 * k + 2] = h.z, QH[4 * k + 3] = h.w;
+    }
+    uint8_t sc12[12];
+    {
+        const uint4 d4 = *reinterpret_cast<const uint4 *>(dm);
+        const uint32_t w[3] = {d4.x, d4.y, d4.z};
+#pragma unroll
+        for (int i = 0; i < 12; ++i) sc12[i] = uint8_t(w[i / 4] >> (8 * (i % 4)));
+    }
+#pragma unroll
+    for (int l = 0; l < 8; ++l) aux[l] = 0;
+    mins = 0;
+#pragma unroll
+    for (int jp = 0; jp < 4; ++jp) {  // sub-blocks 2jp (low nibbles) and 2jp + 1 (high nibbles) share QL words
+        const uint4 qa = *reinterpret_cast<const uint4 *>(q + (2 * jp) * 512);
+        const uint4 qb = *reinterpret_cast<const uint4 *>(q + (2 * jp + 1) * 512);
+        const uint32_t QL[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * jp + jj;
+            int scj, mj;
+            scale_min_k4(j, sc12, scj, mj);
+            const uint4 ya = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + y5_word(j, 0));
+            const uint4 yb = *reinterpret_cast<const uint4 *>(y5 + sb * 64 + y5_word(j, 4));
+            const uint32_t Y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
+#pragma unroll
+            for (int l = 0; l < 8; ++l) {
+                const uint32_t lo = jj ? ((QL[l] >> 4) & m4) : (QL[l] & m4);
+                const uint32_t hi = ((QH[l] >> j) & 0x01010101u) << 4;
+                aux[l] += scj * __dp4a(int(lo | hi), int(Y[l]), 0);
+            }
+            mins += (X.b[sb * 16 + 2 * j] + X.b[sb * 16 + 2 * j + 1]) * mj;
+        }
+    }
+}
+
+// One tile (32 rows x C super-blocks): compute warp w takes super-block w, lane i row i; one record per (row, sb).
 __device__ __forceinline__ void compute_tile_kq(const uint8_t *tile, const MatrixView &w, unsigned nr, unsigned k,
                                                 const XImage &X, const uint32_t *y5, const uint32_t *y6,
                                                 uint32_t *rec, int32_t *dbg, unsigned r0) {
-    const unsigned C = w.ct, items = nr * C * 8;
-    const unsigned QB = w.format == 13 ? 160u : 192u;
-    const unsigned DD = w.format == 13 ? 4u : 2u;
-    const uint8_t *dmp = tile + w.qs_part, *ddp = tile + w.qs_part + w.dm_part;
-    // items beyond the tile run the shuffles with zero work (the whole warp takes part in every round)
-    const unsigned rounds = (items + kComputeThreads - 1) / kComputeThreads, ct = threadIdx.x - 64;
-    for (unsigned rd = 0; rd < rounds; ++rd) {
-        const unsigned idx = rd * kComputeThreads + ct;
-        const bool live = idx < items;
-        const unsigned i = live ? idx / 8 : 0, p = idx & 7u;  // i = r * C + c
-        const unsigned c = i % C, sb = k * C + c;
-        int aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const unsigned C = w.ct, QW = w.format == 13 ? 10u : 12u, DD = w.format == 13 ? 4u : 2u;
+    const unsigned cw = threadIdx.x / 32 - 2, lane = threadIdx.x % 32;
+    const uint8_t *scp = tile + w.qs_part, *ddp = tile + w.qs_part + w.dm_part;
+    if (lane >= nr) return;
+    for (unsigned c = cw; c < C; c += kComputeWarps) {
+        const unsigned sb = k * C + c;
+        const uint8_t *q = tile + size_t(c) * QW * 512 + lane * 16;
+        const uint8_t *sc = scp + (c * 32 + lane) * 16;
+        int aux[8];
         int mins = 0;
-        if (live) {
-            const uint8_t *qs = tile + size_t(i) * QB, *dm = dmp + size_t(i) * 16;
-            if (w.format == 13) part_q5k(qs, dm, p, sb, X, y5, aux, mins);
-            else part_q6k(qs, dm, p, sb, y6, aux);
-        }
-        const int mine = reduce8(aux);
-        mins += __shfl_xor_sync(0xffffffffu, mins, 4);
-        mins += __shfl_xor_sync(0xffffffffu, mins, 2);
-        mins += __shfl_xor_sync(0xffffffffu, mins, 1);
-        if (live) {
-            uint32_t *o = rec + size_t(i) * kRecWords;
-            o[p] = uint32_t(mine);
-            if (p == 0) {
-                o[8] = uint32_t(mins);
-                o[9] = DD == 4 ? *reinterpret_cast<const uint32_t *>(ddp + size_t(i) * 4)
-                               : uint32_t(*reinterpret_cast<const uint16_t *>(ddp + size_t(i) * 2));
-            }
-            if (dbg) {
-                int32_t *d = dbg + (size_t(w.row0 + r0 + i / C) * (w.kc * C) + sb) * 9;
-                d[p] = mine;
-                if (p == 0) d[8] = w.format == 13 ? mins : 0;
-            }
+        if (w.format == 13) sb_q5k(q, sc, sb, X, y5, aux, mins);
+        else sb_q6k(q, sc, sb, y6, aux);
+        uint32_t *o = rec + size_t(lane * C + c) * kRecWords;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) o[l] = uint32_t(aux[l]);
+        o[8] = uint32_t(mins);
+        o[9] = DD == 4 ? *reinterpret_cast<const uint32_t *>(ddp + (c * 32 + lane) * 4)
+                       : uint32_t(*reinterpret_cast<const uint16_t *>(ddp + (c * 32 + lane) * 2));
+        if (dbg) {
+            int32_t *d = dbg + (size_t(w.row0 + r0 + lane) * (w.kc * C) + sb) * 9;
+#pragma unroll
+            for (int l = 0; l < 8; ++l) d[l] = aux[l];
+            d[8] = w.format == 13 ? mins : 0;
         }
     }
 }

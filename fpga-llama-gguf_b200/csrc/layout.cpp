@@ -176,25 +176,21 @@ DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sm
         L.total = (size_t(L.n_rt) * L.kc * L.tile_bytes + 255) & ~size_t(255);
         return L;
     }
-    const unsigned ub = L.qb + L.db + L.dd;
-    const size_t target = kTileTargetK;
-    // K-quants: R rows per tile such that the matrix splits into about one tile per CTA of a pass (two CTAs per
-    // SM), at most 32 (one fold lane per row); C the largest divisor of the row's super-blocks within the target.
-    const unsigned ctas = 2u * (sms ? sms : 148u);
-    unsigned R = (rows + ctas - 1) / ctas;
-    R = R < 1 ? 1 : (R > 32 ? 32 : R);
+    // K-quants: row tiles of 32 rows (one per lane of a compute warp), tiles of C super-blocks (C the largest
+    // divisor of the row's super-blocks up to 8, one per compute warp). Inside a tile, step c (super-block c) holds
+    // the 32 rows' packed quants word-interleaved (16-byte word q of row i at (c * qb / 16 + q) * 512 + 16 i, so a
+    // warp reading word q of its 32 rows reads 512 contiguous bytes), then all steps' scales (16 bytes per row and
+    // step), then their d (Q6_K) / d and dmin (Q5_K).
+    L.rt = 32;
     unsigned C = 1;
-    for (unsigned c = L.blocks; c >= 1; --c) {
-        if (L.blocks % c == 0 && size_t(R) * c * ub <= target) { C = c; break; }
-    }
-    while (R > 1 && size_t(R) * C * ub > target) --R;
-    L.rt = R;
+    for (unsigned c = 8; c >= 1; --c)
+        if (L.blocks % c == 0) { C = c; break; }
     L.ct = C;
     L.kc = L.blocks / C;
-    L.n_rt = (rows + R - 1) / R;
-    L.qs_part = R * C * L.qb;
-    L.dm_part = align16(R * C * L.db);
-    L.dd_part = align16(R * C * L.dd);
+    L.n_rt = (rows + 31) / 32;
+    L.qs_part = 32 * C * L.qb;
+    L.dm_part = 32 * C * L.db;
+    L.dd_part = align16(32 * C * L.dd);
     L.tile_bytes = L.qs_part + L.dm_part + L.dd_part;
     L.total = (size_t(L.n_rt) * L.kc * L.tile_bytes + 255) & ~size_t(255);
     return L;
@@ -208,9 +204,20 @@ struct BlockAt {
 BlockAt block_at(const DeviceLayout &L, unsigned r, unsigned b) {
     const unsigned t = r / L.rt, rr = r % L.rt, k = b / L.ct, cc = b % L.ct;
     const size_t tile = (size_t(t) * L.kc + k) * L.tile_bytes;
+    if (L.format == 13 || L.format == 14) {  // quant word q of this (row, super-block) at qs + q * 512
+        const size_t i = size_t(cc) * 32 + rr;
+        return {tile + size_t(cc) * (L.qb / 16) * 512 + size_t(rr) * 16, tile + L.qs_part + i * L.db,
+                tile + L.qs_part + L.dm_part + i * L.dd};
+    }
     const size_t i = size_t(rr) * L.ct + cc;
-    const bool q8 = L.format == 2 || L.format == 3 || L.format == 8;
-    return {tile + i * (q8 ? 16u : L.qb), tile + L.qs_part + i * L.db, tile + L.qs_part + L.dm_part + i * L.dd};
+    return {tile + i * 16u, tile + L.qs_part + i * L.db, tile + L.qs_part + L.dm_part + i * L.dd};
+}
+// the packed quant words of a K-quant (row, super-block) to / from their interleaved places
+void scatter_words(const uint8_t *packed, unsigned qb, uint8_t *qs) {
+    for (unsigned q = 0; q < qb / 16; ++q) std::memcpy(qs + size_t(q) * 512, packed + 16 * q, 16);
+}
+void gather_words(const uint8_t *qs, unsigned qb, uint8_t *packed) {
+    for (unsigned q = 0; q < qb / 16; ++q) std::memcpy(packed + 16 * q, qs + size_t(q) * 512, 16);
 }
 }  // namespace
 
@@ -218,7 +225,7 @@ void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, cons
     const unsigned rows = row_end - row_begin, f = L.format;
     const size_t rb = gguf_row_bytes(L.cols, f);
     std::memset(dst, 0, L.total);
-    uint8_t lo[256], hi[256];
+    uint8_t lo[256], hi[256], packed[192];
     for (unsigned r = 0; r < rows; ++r) {
         const uint8_t *row = gguf + size_t(row_begin + r) * rb;
         for (unsigned b = 0; b < L.blocks; ++b) {
@@ -236,13 +243,15 @@ void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, cons
             } else if (f == 14) {
                 const uint8_t *blk = row + size_t(b) * 210;
                 q6k_fields(blk, lo, hi);
-                q6k_pack(lo, hi, dst + a.qs);
+                q6k_pack(lo, hi, packed);
+                scatter_words(packed, 192, dst + a.qs);
                 std::memcpy(dst + a.dm, blk + 192, 16);
                 std::memcpy(dst + a.dd, blk + 208, 2);
             } else {  // 13
                 const uint8_t *blk = row + size_t(b) * 176;
                 q5k_fields(blk, lo, hi);
-                q5k_pack(lo, hi, dst + a.qs);
+                q5k_pack(lo, hi, packed);
+                scatter_words(packed, 160, dst + a.qs);
                 std::memcpy(dst + a.dm, blk + 4, 12);
                 std::memcpy(dst + a.dd, blk, 4);
             }
@@ -252,7 +261,7 @@ void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, cons
 
 void unpack_row(const uint8_t *dev, const DeviceLayout &L, unsigned r, uint8_t *out) {
     const unsigned f = L.format;
-    uint8_t lo[256], hi[256];
+    uint8_t lo[256], hi[256], packed[192];
     for (unsigned b = 0; b < L.blocks; ++b) {
         const BlockAt a = block_at(L, r, b);
         if (f == 2) {
@@ -267,7 +276,8 @@ void unpack_row(const uint8_t *dev, const DeviceLayout &L, unsigned r, uint8_t *
             std::memcpy(out + size_t(b) * 20 + 4, dev + a.qs, 16);
         } else if (f == 14) {
             uint8_t *blk = out + size_t(b) * 210;
-            q6k_unpack(dev + a.qs, lo, hi);
+            gather_words(dev + a.qs, 192, packed);
+            q6k_unpack(packed, lo, hi);
             q6k_fields_inverse(lo, hi, blk);
             std::memcpy(blk + 192, dev + a.dm, 16);
             std::memcpy(blk + 208, dev + a.dd, 2);
@@ -275,7 +285,8 @@ void unpack_row(const uint8_t *dev, const DeviceLayout &L, unsigned r, uint8_t *
             uint8_t *blk = out + size_t(b) * 176;
             std::memcpy(blk, dev + a.dd, 4);
             std::memcpy(blk + 4, dev + a.dm, 12);
-            q5k_unpack(dev + a.qs, lo, hi);
+            gather_words(dev + a.qs, 160, packed);
+            q5k_unpack(packed, lo, hi);
             q5k_fields_inverse(lo, hi, blk);
         }
     }

@@ -43,8 +43,8 @@ struct DeviceLayout {
 bool format_supported(unsigned format);
 size_t gguf_row_bytes(unsigned cols, unsigned format);
 // Tiling for `rows` rows on a GPU with `sms` multiprocessors: Q8_0-family panels for one wave of
-// kPanelCtasPerSm CTAs per SM; K-quant row tiles for two CTAs per SM, tiles of at most kTileTargetK bytes.
-constexpr unsigned kTileTargetK = 16384, kPanelCtasPerSm = 3;
+// kPanelCtasPerSm CTAs per SM; K-quant tiles of 32 rows x up to 8 super-blocks.
+constexpr unsigned kPanelCtasPerSm = 3;
 DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms = 148);
 // Repacks GGUF rows [row_begin, row_end) into dst (a layout L made for row_end - row_begin rows).
 void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, const DeviceLayout &L, uint8_t *dst);

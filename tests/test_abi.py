@@ -50,11 +50,15 @@ def test_layout_panels_fill_the_warps(b2):
         assert lay["tile_bytes"] == 32 * (qb + db)
         assert lay["tiles_per_row_tile"] == -(-cols // 32 // lay["blocks_per_tile"])
         assert lay["row_tiles"] == -(-rows // P)
-    # K-quants: about one row tile per CTA of a pass (two per SM), tiles within 16 KB
-    lay = b2.layout(65520, 2560, 14)
-    assert lay["rows_per_tile"] == 32 and lay["tile_bytes"] <= 16384
-    lay = b2.layout(9216, 2560, 13)
-    assert 2 * 148 * 0.9 <= lay["row_tiles"] <= 2 * 148 and lay["tile_bytes"] <= 16384
+    # K-quants: tiles of 32 rows (a lane each) x C super-blocks (a compute warp each), C the largest divisor of the
+    # row's super-blocks up to 8; per row and super-block the packed quants, 16 scale bytes and d (Q5_K: d, dmin)
+    for rows, cols, fmt, C in [(65520, 2560, 14, 5), (9216, 2560, 13, 5), (50688, 4096, 14, 8), (300, 9216, 13, 6),
+                               (7, 256, 14, 1)]:
+        lay = b2.layout(rows, cols, fmt)
+        qb, dd = {14: (192, 2), 13: (160, 4)}[fmt]
+        assert lay["rows_per_tile"] == 32 and lay["blocks_per_tile"] == C, (rows, cols, lay)
+        assert lay["tile_bytes"] == 32 * C * (qb + 16) + -(-32 * C * dd // 16) * 16
+        assert lay["row_tiles"] == -(-rows // 32) and lay["tiles_per_row_tile"] == cols // 256 // C
 
 
 def test_device_bytes_and_row_bytes(b2):
