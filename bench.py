@@ -198,6 +198,60 @@ def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
                       f"each, gemvq_ref.h generic path, {cores} threads"}
 
 
+def kquant_bench(b2, torch, synth, dev: int, world: int, max_over_ranks, barrier) -> dict:
+    """the Q5_K GEMV [9216 x 2560] and the Q6_K output head [151936 x 2560] (three GEMV pieces on one x),
+    against a Q8_K-quantized N(0, 1) x. The Q5_K matrix fits in L2, so a list holds 24 distinct copies whose
+    consecutive GEMVs read alternating x rows (one pass each); the head reads 320 MB per pass. CUDA events on the
+    library's stream; GB/s of the weights in their GGUF bits + x + y."""
+    peak, _ = measured_peak()
+    out = {}
+    ctx = b2.Context(device=dev, weight_bytes=1200 << 20, act_floats=1 << 20)
+    if world > 1:
+        ctx.close()
+        return {"note": "measured on one GPU only"}
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+    r = synth.rng(2, 0)
+    H = 2560
+    ctx.write(0, synth.activation(r, H))
+    ctx.write(H, synth.activation(r, H))
+
+    def timed(cl, bytes_per_rep, passes):
+        g = ctx.graph(cl)
+        ctx.launch_many([g], 5)
+        ctx.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.launch_many([g], 50)
+        e1.record(stream)
+        e1.synchronize()
+        us = max_over_ranks(e0.elapsed_time(e1) / 50 * 1e3) / passes
+        g.close()
+        gbs = bytes_per_rep / passes / (us * 1e-6) / 1e9
+        return {"us_per_pass": round(us, 2), "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
+
+    w5 = synth.q5_k(r, 9216, H)
+    n5 = 24
+    cmds = []
+    for i in range(n5):
+        h = ctx.upload(w5, 9216, H, 13)
+        cmds.append(b2.gemv(13, 9216, H, h, (i % 2) * H, 4 * H + (i % 2) * 9216))
+    q5 = timed(b2.cmd_list(*cmds), n5 * (w5.nbytes + 4 * H + 4 * 9216), n5)
+    out["q5k_9216x2560"] = dict(q5, bytes_per_pass=w5.nbytes + 4 * H + 4 * 9216, copies=n5)
+    ctx.reset_weights()
+    w6 = synth.q6_k(r, 151936, H)
+    rb = b2.gguf_row_bytes(H, 14)
+    cmds, r0 = [], 0
+    while r0 < 151936:
+        n = min(50688, 151936 - r0)
+        h = ctx.upload(w6.reshape(-1)[r0 * rb:(r0 + n) * rb], n, H, 14)
+        cmds.append(b2.gemv(14, n, H, h, 0, 4 * H + r0))
+        r0 += n
+    head_bytes = w6.nbytes + 4 * H + 4 * 151936
+    out["q6k_head_151936x2560"] = dict(timed(b2.cmd_list(*cmds), head_bytes, 1), bytes_per_pass=head_bytes)
+    ctx.close()
+    return out
+
+
 def decode_bench(b2, torch, dist, dev: int, world: int, rank: int, shape, label: str, tokens: int, warm: int,
                  max_over_ranks, barrier):
     """Batch-1 greedy decode of the synthetic hybrid model: `tokens` tokens at positions prefill ..
@@ -274,6 +328,7 @@ def main():
     ap.add_argument("--decode", default="4b,9b", help="synthetic decode models to run after the GEMV stack "
                     "(comma list of 4b, 9b; empty for none)")
     ap.add_argument("--decode-tokens", type=int, default=128)
+    ap.add_argument("--no-kquant", action="store_true", help="skip the configs[2] K-quant GEMV measurement")
     ap.add_argument("--decode-only", action="store_true", help="run only the decode measurement (for profiling "
                     "runs); the line then carries the decode object and no GEMV metric")
     args = ap.parse_args()
@@ -433,6 +488,7 @@ def main():
     ctx.close()
 
     decode = run_decodes()
+    kquant = kquant_bench(b2, torch, synth, dev, world, max_over_ranks, barrier) if not args.no_kquant else {}
     if dist:
         dist.destroy_process_group()
     if rank == 0:
@@ -444,7 +500,7 @@ def main():
                                                              f"({n_layers * per_layer >> 20} MiB per GPU > 3x L2)",
                                frac_of_peak=round(value / peak, 4)),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
-                "decode": decode}
+                "decode": decode, "kquant": kquant}
         print(json.dumps(line), flush=True)
     return 0
 
