@@ -13,10 +13,12 @@
 //   Q8_0: 2 x 16 quant bytes = GGUF bytes 2..17 and 18..33, DB 2 = FP16 d
 //   Q4_1: 16 quant bytes = GGUF bytes 4..19, DB 4 = FP16 d, FP16 m (GGUF bytes 0..3)
 //   KC = ceil(blocks / C): units past the last block, and rows past the matrix, are zero.
-// K-quants (Q5_K, Q6_K): tiles of about one per CTA of a pass, moved by one bulk copy (TMA) into shared memory:
-//     [ quants : R x C x QB bytes, row-major (row, block) ]
-//     [ scales : R x C x DB bytes, row-major, padded to 16 ]
-//     [ d/dmin : R x C x DD bytes, row-major, padded to 16 ]
+// K-quants (Q5_K, Q6_K): tiles of R = 32 rows x C super-blocks (C the largest divisor of the row's super-blocks
+// up to 8), each moved by one bulk copy (TMA) into shared memory; lane i of a compute warp owns row i and the
+// warp owns one super-block c:
+//     [ quants : C steps x QB / 16 words x 32 rows x 16 bytes (word q of row i, step c at (c QB/16 + q) 512 + 16 i) ]
+//     [ scales : C x R x DB bytes, (step, row) order ]
+//     [ d/dmin : C x R x DD bytes, (step, row) order, padded to 16 ]
 //   Q6_K: QB 192 = ql/qh fields permuted per super-block, DB 16 = int8 scales (GGUF 192..207), DD 2 = FP16 d
 //   Q5_K: QB 160 = qs/qh fields permuted per super-block, DB 16 = packed scales (GGUF 4..15) + 4 zero bytes,
 //         DD 4 = FP16 d, FP16 dmin (GGUF 0..3)
