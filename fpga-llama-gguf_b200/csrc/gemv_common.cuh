@@ -26,6 +26,7 @@ constexpr unsigned kComputeThreads = 32 * kComputeWarps;
 constexpr unsigned kXThreads = kPassThreads - 32;              // fold + compute warps prepare x
 constexpr unsigned kNR = 2;                                     // result buffers
 constexpr unsigned kMaxStages = 6;
+constexpr unsigned kL2Ahead = 2;                                // tiles asked of L2 beyond the stage ring
 
 // Position in the tile sequence of one CTA: items (row tiles of units) blockIdx.x, blockIdx.x + gridDim.x, ...;
 // each item is streamed as its unit's kc tiles.
@@ -224,10 +225,29 @@ __device__ __forceinline__ void init_pass_barriers(const GemvArgs &a, const Pass
     mbar_fence_init();
 }
 
-// Producer (one thread): streams the CTA's tiles through the stage ring.
+// L2 prefetch of the bytes issue_stage copies for one tile (no data returns to the SM).
+__device__ __forceinline__ void prefetch_stage(const GemvArgs &a, const TileIt &it) {
+    const GemvMemberArgs &M = unit_member(a, it.unit);
+    const unsigned t = it.item - a.item_start[it.unit];
+    const int pair = a.unit_pair[it.unit];
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(tile_src(M.w, t, it.k)), "r"(M.w.tile_bytes)
+                 : "memory");
+    if (pair >= 0)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(tile_src(a.m[pair].w, t, it.k)),
+                     "r"(M.w.tile_bytes)
+                     : "memory");
+}
+
+// Producer (one thread): streams the CTA's tiles through the stage ring. The kL2Ahead tiles after the ring's are
+// asked of L2 ahead of their copies, so HBM keeps streaming while every stage waits for its compute.
 __device__ __forceinline__ void producer_loop(const GemvArgs &a, const PassSmem &P) {
     const uint64_t policy = evict_first_policy();
-    TileIt it = tile_first(a);
+    TileIt it = tile_first(a), pf = it;
+    for (unsigned i = 0; i < a.n_stages && tile_valid(a, pf); ++i) tile_next(a, pf);
+    for (unsigned i = 0; i < kL2Ahead && tile_valid(a, pf); ++i) {
+        prefetch_stage(a, pf);
+        tile_next(a, pf);
+    }
     unsigned seq = 0;
     bool failed = false;
     while (tile_valid(a, it)) {
@@ -237,6 +257,10 @@ __device__ __forceinline__ void producer_loop(const GemvArgs &a, const PassSmem 
             break;
         }
         issue_stage(a, it, P.stages + size_t(s) * a.stage_bytes, &P.full[s], policy);
+        if (seq >= a.n_stages && tile_valid(a, pf)) {
+            prefetch_stage(a, pf);
+            tile_next(a, pf);
+        }
         tile_next(a, it);
         ++seq;
     }

@@ -177,14 +177,16 @@ DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sm
         return L;
     }
     // K-quants: row tiles of 32 rows (one per lane of a compute warp), tiles of C super-blocks (C the largest
-    // divisor of the row's super-blocks up to 8, one per compute warp). Inside a tile, step c (super-block c) holds
+    // divisor of the row's super-blocks up to 8 whose tile stays within kKqTileCap, so two stages and two CTAs fit
+    // an SM; the compute warps share a tile's super-blocks out in parts). Inside a tile, step c (super-block c) holds
     // the 32 rows' packed quants word-interleaved (16-byte word q of row i at (c * qb / 16 + q) * 512 + 16 i, so a
     // warp reading word q of its 32 rows reads 512 contiguous bytes), then all steps' scales (16 bytes per row and
     // step), then their d (Q6_K) / d and dmin (Q5_K).
     L.rt = 32;
     unsigned C = 1;
-    for (unsigned c = 8; c >= 1; --c)
-        if (L.blocks % c == 0) { C = c; break; }
+    const unsigned per_sb = 32u * (L.qb + L.db + L.dd);
+    for (unsigned c = 8; c > 1; --c)
+        if (L.blocks % c == 0 && c * per_sb <= kKqTileCap) { C = c; break; }
     L.ct = C;
     L.kc = L.blocks / C;
     L.n_rt = (rows + 31) / 32;

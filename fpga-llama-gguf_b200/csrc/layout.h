@@ -14,8 +14,8 @@
 //   Q4_1: 16 quant bytes = GGUF bytes 4..19, DB 4 = FP16 d, FP16 m (GGUF bytes 0..3)
 //   KC = ceil(blocks / C): units past the last block, and rows past the matrix, are zero.
 // K-quants (Q5_K, Q6_K): tiles of R = 32 rows x C super-blocks (C the largest divisor of the row's super-blocks
-// up to 8), each moved by one bulk copy (TMA) into shared memory; lane i of a compute warp owns row i and the
-// warp owns one super-block c:
+// up to 8 with C x 32 x (QB + DB + DD) <= kKqTileCap), each moved by one bulk copy (TMA) into shared memory; lane i
+// of a compute warp owns row i:
 //     [ quants : C steps x QB / 16 words x 32 rows x 16 bytes (word q of row i, step c at (c QB/16 + q) 512 + 16 i) ]
 //     [ scales : C x R x DB bytes, (step, row) order ]
 //     [ d/dmin : C x R x DD bytes, (step, row) order, padded to 16 ]
@@ -45,8 +45,9 @@ struct DeviceLayout {
 bool format_supported(unsigned format);
 size_t gguf_row_bytes(unsigned cols, unsigned format);
 // Tiling for `rows` rows on a GPU with `sms` multiprocessors: Q8_0-family panels for one wave of
-// kPanelCtasPerSm CTAs per SM; K-quant tiles of 32 rows x up to 8 super-blocks.
+// kPanelCtasPerSm CTAs per SM; K-quant tiles of 32 rows x up to 8 super-blocks, at most kKqTileCap bytes.
 constexpr unsigned kPanelCtasPerSm = 3;
+constexpr unsigned kKqTileCap = 34 * 1024;
 DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms = 148);
 // Repacks GGUF rows [row_begin, row_end) into dst (a layout L made for row_end - row_begin rows).
 void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, const DeviceLayout &L, uint8_t *dst);

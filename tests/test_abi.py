@@ -50,10 +50,10 @@ def test_layout_panels_fill_the_warps(b2):
         assert lay["tile_bytes"] == 32 * (qb + db)
         assert lay["tiles_per_row_tile"] == -(-cols // 32 // lay["blocks_per_tile"])
         assert lay["row_tiles"] == -(-rows // P)
-    # K-quants: tiles of 32 rows (a lane each) x C super-blocks (a compute warp each), C the largest divisor of the
-    # row's super-blocks up to 8; per row and super-block the packed quants, 16 scale bytes and d (Q5_K: d, dmin)
-    for rows, cols, fmt, C in [(65520, 2560, 14, 5), (9216, 2560, 13, 5), (50688, 4096, 14, 8), (300, 9216, 13, 6),
-                               (7, 256, 14, 1)]:
+    # K-quants: tiles of 32 rows (a lane each) x C super-blocks, C the largest divisor of the row's super-blocks up
+    # to 8 whose tile is at most 34 KB; per row and super-block the packed quants, 16 scale bytes and d (Q5_K: d, dmin)
+    for rows, cols, fmt, C in [(65520, 2560, 14, 5), (9216, 2560, 13, 5), (50688, 4096, 14, 4), (300, 9216, 13, 6),
+                               (7, 256, 14, 1), (64, 2048, 13, 4), (64, 8192, 14, 4)]:
         lay = b2.layout(rows, cols, fmt)
         qb, dd = {14: (192, 2), 13: (160, 4)}[fmt]
         assert lay["rows_per_tile"] == 32 and lay["blocks_per_tile"] == C, (rows, cols, lay)
