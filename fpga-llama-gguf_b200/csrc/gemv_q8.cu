@@ -4,16 +4,16 @@
 //
 // A CTA takes one panel at a time (P rows x all blocks of one matrix, or of a SwiGLU g/u pair; one wave of CTAs
 // covers the pass when it fits) and splits the panel's steps over its 8 warps (warp w: steps w, w + 8, ...):
-//   1. before the wait on the previous kernel (programmatic dependent launch) the warps ask L2 for the CTA's
-//      first panels (bulk prefetch; weights never change within a list), so HBM streams while x is prepared;
+//   1. before the wait on the previous kernel (programmatic dependent launch) the CTA bulk-copies the leading steps
+//      of its first panel into shared memory and asks L2 for the rest of it (weights never change within a list),
+//      so HBM streams while the previous kernel ends and while x is prepared;
 //   2. the CTA quantizes x into shared memory once (optionally through the deferred RMSNORM);
 //   3. per step (one 32-unit tile: P rows x 32 / P blocks, lane = unit) each lane loads its unit's 16-byte quant
 //      words and scale with coalesced 128-bit loads, several steps ahead in registers, forms the exact integer
 //      block dot (dp4a) and the block term float(sumi) * (d_w * d_x) (two IEEE roundings, as the CPU path), and
 //      stores the term to the panel's term buffer in shared memory (one 128-byte row per step);
 //   4. after the panel, one lane per row adds the row's terms in block order, reproducing the CPU's FP32 sum bit
-//      for bit (gemvq_ref.h:248-262), applies the epilogue and writes y;
-//   5. a CTA out of panels asks L2 for its share of the next GEMV pass's weights.
+//      for bit (gemvq_ref.h:248-262), applies the epilogue and writes y.
 //
 // Roofline: HBM bandwidth. Bytes per row: cols/32 * (16 + 2) for Q4_0, * (32 + 2) for Q8_0, * (16 + 4) for Q4_1.
 #include <algorithm>
@@ -522,8 +522,11 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
     };
     pdl_launch_dependents();  // the next kernel may start as SMs free up
     // weights never change within a list: a CTA that is resident before the previous kernel completes starts its
-    // staging copy now, so HBM streams while that kernel finishes
+    // staging copy now, and asks L2 for the rest of its first panel, so HBM streams while that kernel finishes and
+    // while x is prepared. (Issued after the wait, the L2 requests held up thread 0's warp behind the staging copies
+    // in the copy engine's queue for ~1.5 us; later panels are not prefetched: that cost more than it saved.)
     issue_staging();
+    if (threadIdx.x == 0 && blockIdx.x < total) prefetch_panel(a, blockIdx.x, stg.k);
     pdl_wait();
     constexpr bool peers = PEERS;
     if (peers && blockIdx.x == 0 && threadIdx.x == 0) peer_announce(a.ps);
@@ -535,9 +538,6 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
     } else {
         prepare_x_cluster(a, X, FA == 3 ? 1u : 0u, [] {});
     }
-    // the rest of the first panel (and the next one) into L2, in step order
-    if (threadIdx.x == 0 && blockIdx.x < total) prefetch_panel(a, blockIdx.x, stg.k);
-    if (threadIdx.x == 32) prefetch_panel(a, blockIdx.x + gridDim.x, 0);
     const unsigned n = a.cols, nb = n / 32;
     const XSmem xs{reinterpret_cast<const uint4 *>(X.q), reinterpret_cast<const uint4 *>(X.q + n / 2), X.meta};
     const uint64_t pol = evict_first_policy();
@@ -545,7 +545,6 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
     const PeerSync *ps = nullptr;  // set once every peer has reached this launch (before the first store)
     unsigned np = 0;
     for (unsigned it = blockIdx.x; it < total; it += gridDim.x, ++np) {
-        if (threadIdx.x == 0 && np) prefetch_panel(a, it + gridDim.x, 0);
         const unsigned u = unit_of(a, it), pnl = it - a.item_start[u];
         const GemvMemberArgs &MA = unit_member(a, u);
         const GemvMemberArgs &MB = FB ? a.m[a.unit_pair[u]] : MA;
