@@ -11,7 +11,7 @@
 //   3. per step (one 32-unit tile: P rows x 32 / P blocks, lane = unit) each lane loads its unit's 16-byte quant
 //      words and scale with coalesced 128-bit loads, several steps ahead in registers, forms the exact integer
 //      block dot (dp4a) and the block term float(sumi) * (d_w * d_x) (two IEEE roundings, as the CPU path), and
-//      stores the term to the panel's term buffer in shared memory (one 128-byte row per step);
+//      stores the term to the panel's term buffer in shared memory (row-major: a row's terms contiguous);
 //   4. after the panel, one lane per row adds the row's terms in block order, reproducing the CPU's FP32 sum bit
 //      for bit (gemvq_ref.h:248-262), applies the epilogue and writes y.
 //
@@ -24,6 +24,14 @@
 namespace b200q {
 
 constexpr unsigned kPanelWarps = 8, kPanelThreads = 32 * kPanelWarps;
+
+// Term buffer of a panel: row i's block terms contiguous at word i * term_stride(blocks), blocks = the row's units over
+// all steps (zero padding included). The stride is a multiple of 4 with stride / 4 odd, so the 16-byte loads of 8
+// consecutive rows hit 8 distinct bank groups (and a P = 8 step's 32 stores hit 32 banks).
+__host__ __device__ inline unsigned term_stride(unsigned blocks) {
+    const unsigned s = (blocks + 3u) & ~3u;
+    return (s / 4u) % 2u ? s : s + 4u;
+}
 
 // ---- one lane's share of one step ---------------------------------------------------------------------------------
 template <unsigned FMT>
@@ -395,8 +403,9 @@ __device__ __forceinline__ bool compute_steps(const GemvArgs &a, const GemvMembe
                                               uint64_t pol, float *term_a, float *term_b, const Staging &stg,
                                               uint64_t *stage_bar) {
     const MatrixView &w = MA.w;
-    const unsigned J = w.ct, S = w.kc, nb = a.cols / 32;
+    const unsigned J = w.ct, S = w.kc, nb = a.cols / 32, TS = term_stride(S * J);
     const unsigned j = lane & (J - 1u), lrow = pnl * w.rt + lane / J;
+    const unsigned tslot = (lane / J) * TS + j;  // + s J: the term of (row lane / J, block s J + j)
     const unsigned TA = w.tile_bytes, TB = FB ? MB.w.tile_bytes : 0u;
     const uint8_t *ta = w.base + size_t(pnl) * S * TA;
     const uint8_t *tb = FB ? MB.w.base + size_t(pnl) * S * TB : nullptr;
@@ -411,11 +420,11 @@ __device__ __forceinline__ bool compute_steps(const GemvArgs &a, const GemvMembe
         const unsigned b = s * J + j, bc = b < nb ? b : 0u;
         const XBlock x = load_xblock(xs, bc);
         int sumi;
-        term_a[s * 32 + lane] = block_term<FA>(ca, x, sumi);
+        term_a[tslot + s * J] = block_term<FA>(ca, x, sumi);
         if (dbg && b < nb) dbg[b] = sumi;
         if (FB) {
             int su;
-            term_b[s * 32 + lane] = block_term<FB_>(cb, x, su);
+            term_b[tslot + s * J] = block_term<FB_>(cb, x, su);
         }
     };
     Step<FA> ba[U];
@@ -454,25 +463,28 @@ __device__ __forceinline__ bool compute_steps(const GemvArgs &a, const GemvMembe
     return ok;
 }
 
-// Row r's terms in block order, sum += term from 0: the CPU's sequential FP32 sum (gemvq_ref.h:248-262). The term
-// of block k of row r sits at terms[32 (k / J) + r J + k % J]; 16 terms are loaded ahead of their 16 additions.
-__device__ __forceinline__ float fold_row(const float *terms, unsigned r, unsigned J, unsigned nb) {
-    const float *t = terms + r * J;
-    const unsigned jl = __ffs(J) - 1, jm = J - 1;
+// Row r's terms in block order, sum += term from 0: the CPU's sequential FP32 sum (gemvq_ref.h:248-262). The terms
+// of row r are contiguous at terms[r TS ..] (term_stride), read 16 at a time with 16-byte loads ahead of their
+// additions, so the dependent chain of additions is the only wait.
+__device__ __forceinline__ float fold_row(const float *terms, unsigned r, unsigned TS, unsigned nb) {
+    const float *t = terms + r * TS;
+    const float4 *t4 = reinterpret_cast<const float4 *>(t);
     float acc = 0.0f;
     unsigned k = 0;
 #pragma unroll 2
     for (; k + 16 <= nb; k += 16) {
-        float v[16];
+        float4 v[4];
 #pragma unroll
-        for (unsigned e = 0; e < 16; ++e) {
-            const unsigned kk = k + e;
-            v[e] = t[((kk >> jl) << 5) + (kk & jm)];
+        for (unsigned e = 0; e < 4; ++e) v[e] = t4[k / 4 + e];
+#pragma unroll
+        for (unsigned e = 0; e < 4; ++e) {
+            acc = fadd(acc, v[e].x);
+            acc = fadd(acc, v[e].y);
+            acc = fadd(acc, v[e].z);
+            acc = fadd(acc, v[e].w);
         }
-#pragma unroll
-        for (unsigned e = 0; e < 16; ++e) acc = fadd(acc, v[e]);
     }
-    for (; k < nb; ++k) acc = fadd(acc, t[((k >> jl) << 5) + (k & jm)]);
+    for (; k < nb; ++k) acc = fadd(acc, t[k]);
     return acc;
 }
 
@@ -562,7 +574,13 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
         }
         if (__syncthreads_or(failed)) break;
         if (!a.dbg) {
-            if (FB && warp == 1 && lane < P) usum[lane] = fold_row(term_b, lane, w.ct, nb);
+            // the row sums: warp 0 folds the g (or only) terms while warp 1 folds a pair's u terms
+            const unsigned out_member = FB ? unsigned(a.unit_pair[u]) : a.unit_member[u];
+            const bool handoff = a.qout && out_member == a.qout_member && P == 32;
+            const unsigned TS = term_stride(w.kc * w.ct);
+            float acc = 0.0f;
+            if (warp == 0 && (handoff || mine)) acc = fold_row(term_a, lane, TS, nb);
+            if (FB && warp == 1 && lane < P) usum[lane] = fold_row(term_b, lane, TS, nb);
             if (FB) __syncthreads();
             if (warp == 0) {
                 if (peers && np == 0) {
@@ -570,16 +588,13 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
                     if (ok) ps = &a.ps;
                     else if (lane == 0 && a.err) atomicExch(a.err, 1u);
                 }
-                const unsigned out_member = FB ? unsigned(a.unit_pair[u]) : a.unit_member[u];
-                if (a.qout && out_member == a.qout_member && P == 32) {
+                if (handoff) {
                     // this panel is block pnl of the next pass's x: every lane holds a row (rows % 32 == 0)
-                    const float acc = fold_row(term_a, lane, w.ct, nb);
                     const float val = FB ? row_value(MB, w.row0 + lrow, usum[lane], acc)
                                          : row_value(MA, w.row0 + lrow, acc, 0.0f, &res);
                     OUT.y[w.row0 + lrow] = val;
                     write_image_block(a.qout, OUT.total_rows, pnl, val, lane, a.qout_act);
                 } else if (mine) {
-                    const float acc = fold_row(term_a, lane, w.ct, nb);
                     if (FB) write_row(MB, w.row0 + lrow, usum[lane], acc, nullptr, ps);
                     else write_row(MA, w.row0 + lrow, acc, 0.0f, &res, ps);
                 }
@@ -661,7 +676,13 @@ void plan_gemv_q8(GemvArgs &a, size_t &smem) {
         }
         stage_step_bytes = stage_step_bytes > sb ? stage_step_bytes : sb;
     }
-    a.term_bytes = unsigned(align128(size_t(steps) * 128));
+    unsigned tb = 0;
+    for (unsigned u = 0; u < a.n_units; ++u) {
+        const MatrixView &g = a.m[a.unit_member[u]].w;
+        const unsigned b = g.rt * term_stride(g.kc * g.ct) * 4u;
+        tb = tb > b ? tb : b;
+    }
+    a.term_bytes = unsigned(align128(tb));
     const size_t fixed = align128(qimage_bytes(a.cols)) + (pair ? 2u : 1u) * size_t(a.term_bytes) + 256;
     // staged leading steps: what is left of a third of the SM's shared memory (three CTAs per SM)
     const size_t per_cta = 227 * 1024 / 3 - 1024;
