@@ -35,6 +35,11 @@ Q4_0, Q4_1, Q8_0, Q5_K, Q6_K = 2, 3, 8, 13, 14
 FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53000F)
 UPLOAD_REPLICATE = 1
 
+
+def UPLOAD_PASS_ROWS(n: int) -> int:
+    """Upload flag: the matrix joins a multi-output pass of n rows in all (panel height chosen for the pass)."""
+    return int(n) << 8
+
 ERR = {-1: "bad argument", -2: "CUDA failure", -3: "out of memory", -4: "context disabled", -5: "NCCL failure",
        -6: "call out of order", -7: "bounded wait ran out"}
 
@@ -165,6 +170,7 @@ def lib() -> ctypes.CDLL:
         "b200q_upload_weight": (I, [P, P, U, U, U, U, ctypes.POINTER(ctypes.c_uint64)]),
         "b200q_upload_weight_ex": (I, [P, P, U, U, U, U, U, ctypes.POINTER(ctypes.c_uint64)]),
         "b200q_weight_device_bytes": (SZ, [U, U, U]),
+        "b200q_weight_device_bytes_ex": (SZ, [U, U, U, U]),
         "b200q_gguf_row_bytes": (SZ, [U, U]),
         "b200q_weights_reset": (I, [P]),
         "b200q_act_write": (I, [P, SZ, P, SZ]),
@@ -191,6 +197,7 @@ def lib() -> ctypes.CDLL:
         "b200q_comm_world": (I, [P]),
         "b200q_row_slice": (I, [U, U, I, I, ctypes.POINTER(U), ctypes.POINTER(U)]),
         "b200q_layout": (I, [U, U, U, U, P]),
+        "b200q_layout_ex": (I, [U, U, U, U, U, P]),
         "b200q_repack_host": (I, [P, U, U, U, U, P]),
         "b200q_unpack_row_host": (I, [P, U, U, U, U, U, P]),
     }
@@ -204,14 +211,15 @@ def lib() -> ctypes.CDLL:
 
 EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream", "b200q_synchronize",
             "b200q_act_device_ptr", "b200q_state_device_ptr", "b200q_kv_device_ptr", "b200q_features",
-            "b200q_upload_weight", "b200q_upload_weight_ex", "b200q_weight_device_bytes", "b200q_gguf_row_bytes",
+            "b200q_upload_weight", "b200q_upload_weight_ex", "b200q_weight_device_bytes", "b200q_weight_device_bytes_ex",
+            "b200q_gguf_row_bytes",
             "b200q_weights_reset", "b200q_act_write", "b200q_act_read", "b200q_act_fill", "b200q_act_write_async",
             "b200q_act_read_async", "b200q_state_write",
             "b200q_state_read", "b200q_kv_write", "b200q_run", "b200q_run_async", "b200q_graph_create",
             "b200q_graph_launch", "b200q_graph_launch_many", "b200q_graph_destroy", "b200q_graph_kernel_count", "b200q_plan",
             "b200q_debug_quantize", "b200q_debug_block_sums", "b200q_quantize_noalloc", "b200q_comm_unique_id",
             "b200q_comm_init",
-            "b200q_comm_world", "b200q_row_slice", "b200q_layout", "b200q_repack_host", "b200q_unpack_row_host"]
+            "b200q_comm_world", "b200q_row_slice", "b200q_layout", "b200q_layout_ex", "b200q_repack_host", "b200q_unpack_row_host"]
 
 
 class _LayoutInfo(ctypes.Structure):
@@ -220,9 +228,9 @@ class _LayoutInfo(ctypes.Structure):
                 ("tile_bytes", ctypes.c_uint32), ("total_bytes", ctypes.c_uint64)]
 
 
-def layout(rows: int, cols: int, fmt: int, sms: int = 148) -> dict:
+def layout(rows: int, cols: int, fmt: int, sms: int = 148, flags: int = 0) -> dict:
     info = _LayoutInfo()
-    if lib().b200q_layout(rows, cols, fmt, sms, ctypes.byref(info)) != 0:
+    if lib().b200q_layout_ex(rows, cols, fmt, sms, flags, ctypes.byref(info)) != 0:
         raise ValueError("unsupported shape or format")
     return {f: int(getattr(info, f)) for f, _ in _LayoutInfo._fields_}
 
@@ -302,9 +310,9 @@ def gguf_row_bytes(cols: int, fmt: int) -> int:
     return int(lib().b200q_gguf_row_bytes(cols, fmt))
 
 
-def weight_device_bytes(rows: int, cols: int, fmt: int) -> int:
+def weight_device_bytes(rows: int, cols: int, fmt: int, flags: int = 0) -> int:
     """Device bytes of one uploaded matrix (its repacked layout), before the arena's 256-byte rounding."""
-    return int(lib().b200q_weight_device_bytes(rows, cols, fmt))
+    return int(lib().b200q_weight_device_bytes_ex(rows, cols, fmt, flags))
 
 
 class Graph:

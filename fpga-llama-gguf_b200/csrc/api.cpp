@@ -877,8 +877,12 @@ int b200q_synchronize(b200q_ctx *c) {
 size_t b200q_gguf_row_bytes(unsigned cols, unsigned format) { return gguf_row_bytes(cols, format); }
 
 size_t b200q_weight_device_bytes(unsigned rows, unsigned cols, unsigned format) {
+    return b200q_weight_device_bytes_ex(rows, cols, format, 0);
+}
+
+size_t b200q_weight_device_bytes_ex(unsigned rows, unsigned cols, unsigned format, unsigned flags) {
     if (!format_supported(format)) return 0;
-    return device_layout(rows, cols, format, 148).total;
+    return device_layout(rows, cols, format, 148, flags >> 8).total;
 }
 
 int b200q_row_slice(unsigned rows, unsigned flags, int world, int rank, unsigned *r0, unsigned *r1) {
@@ -904,7 +908,9 @@ int b200q_upload_weight_ex(b200q_ctx *c, const void *gguf, unsigned rows, unsign
         return set_err(c, B200Q_ERR_ARG, "upload: bad shape or format");
     unsigned r0 = 0, r1 = rows;
     b200q_row_slice(rows, flags, c->world, c->rank, &r0, &r1);
-    const DeviceLayout L = device_layout(r1 - r0, cols, format, unsigned(c->sms));
+    // the pass hint, scaled to this rank's share when the matrix is sharded
+    const unsigned pass_rows = unsigned(uint64_t(flags >> 8) * (r1 - r0) / rows);
+    const DeviceLayout L = device_layout(r1 - r0, cols, format, unsigned(c->sms), pass_rows);
     if (c->wused + L.total > c->wbytes) return set_err(c, B200Q_ERR_NOMEM, "weight arena full");
     std::vector<uint8_t> host(L.total);
     repack_rows(static_cast<const uint8_t *>(gguf), r0, r1, L, host.data());
@@ -1192,8 +1198,13 @@ int b200q_debug_block_sums(b200q_ctx *c, const uint32_t cmd[8], int32_t *out) {
 }
 
 int b200q_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms, b200q_layout_info *out) {
+    return b200q_layout_ex(rows, cols, format, sms, 0, out);
+}
+
+int b200q_layout_ex(unsigned rows, unsigned cols, unsigned format, unsigned sms, unsigned flags,
+                    b200q_layout_info *out) {
     if (!out || !format_supported(format) || rows == 0 || cols == 0) return B200Q_ERR_ARG;
-    const DeviceLayout L = device_layout(rows, cols, format, sms);
+    const DeviceLayout L = device_layout(rows, cols, format, sms, flags >> 8);
     if (L.blocks == 0) return B200Q_ERR_ARG;
     out->rows_per_tile = L.rt;
     out->blocks_per_tile = L.ct;

@@ -132,7 +132,7 @@ namespace {
 unsigned align16(unsigned v) { return (v + 15u) & ~15u; }
 }
 
-DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sms) {
+DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sms, unsigned pass_rows) {
     DeviceLayout L;
     L.format = f;
     L.rows = rows;
@@ -149,10 +149,12 @@ DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned f, unsigned sm
     if (f == 2 || f == 3 || f == 8) {
         // Panels of P rows (one per CTA of a pass), streamed as steps of 32 units (P rows x J = 32 / P blocks; the
         // last step of a panel is zero-padded when J does not divide the blocks). P: the largest for which the
-        // panels fill between half and all of the CTA slots of the GPU (one wave), with at most 15% padding;
-        // matrices too large for one wave take P = 32, too small ones the smallest P (most panels).
+        // panels of the pass (of this matrix, or of all members of the multi-output pass it joins) fill between half
+        // and all of the CTA slots of the GPU (one wave), with at most 15% padding; passes too large for one wave
+        // take P = 32, too small ones the smallest P (most panels).
         const unsigned slots = (sms ? sms : 148u) * kPanelCtasPerSm;
-        auto panels = [&](unsigned P) { return (rows + P - 1) / P; };
+        const unsigned fill_rows = pass_rows > rows ? pass_rows : rows;
+        auto panels = [&](unsigned P) { return (fill_rows + P - 1) / P; };
         auto padded_ok = [&](unsigned P) {
             const unsigned J = 32u / P;
             return double((L.blocks + J - 1) / J * J) <= 1.15 * double(L.blocks);

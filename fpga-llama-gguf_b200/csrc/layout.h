@@ -48,7 +48,9 @@ size_t gguf_row_bytes(unsigned cols, unsigned format);
 // kPanelCtasPerSm CTAs per SM; K-quant tiles of 32 rows x up to 8 super-blocks, at most kKqTileCap bytes.
 constexpr unsigned kPanelCtasPerSm = 3;
 constexpr unsigned kKqTileCap = 34 * 1024;
-DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms = 148);
+// pass_rows: rows of the whole multi-output pass the matrix joins (its members' panels share one wave of CTAs), or 0
+// for a matrix that is a pass of its own.
+DeviceLayout device_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms = 148, unsigned pass_rows = 0);
 // Repacks GGUF rows [row_begin, row_end) into dst (a layout L made for row_end - row_begin rows).
 void repack_rows(const uint8_t *gguf, unsigned row_begin, unsigned row_end, const DeviceLayout &L, uint8_t *dst);
 // Inverse for one row (tests: the repack keeps every bit).

@@ -29,7 +29,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import (CMD_WORDS, GDN_GATED, GDN_GATES, GDN_L2_QK, GDN_WITH_OUT, GEMV_ADD, GEMV_CONV, GEMV_SWIGLU, MAX_CMDS, NORM_DEFER,
-               Q4_0, Q6_K, UPLOAD_REPLICATE, add, argmax, attn, cmd_list, conv, gdn, gemv, get_row, gguf_row_bytes,
+               Q4_0, Q6_K, UPLOAD_PASS_ROWS, UPLOAD_REPLICATE, add, argmax, attn, cmd_list, conv, gdn, gemv, get_row, gguf_row_bytes,
                rmsnorm, rope, silu_mul)
 from . import synth
 
@@ -157,15 +157,18 @@ class HybridDecoder:
         s = self.s
         H, F, d = s.hidden, s.ffn, s.gdn_rows
         att, kvd = s.n_head * s.head_dim, s.n_kv_head * s.head_dim
+        # members of one multi-output pass are told the pass's rows, so their panels make one wave of CTAs
+        qkv_pass = UPLOAD_PASS_ROWS(2 * att + 2 * kvd)
+        gdn_pass = UPLOAD_PASS_ROWS(4 * d + 2 * s.gdn_heads)
         out = [("tok_embd", Q4_0, s.vocab, H, 0, UPLOAD_REPLICATE)]
         for i in range(s.n_layers):
             if s.is_attn(i):
-                out += [(f"{i}.wq_gate", Q4_0, 2 * att, H, 0, 0), (f"{i}.wk", Q4_0, kvd, H, 0, 0),
-                        (f"{i}.wv", Q4_0, kvd, H, 0, 0), (f"{i}.wo", Q4_0, H, att, 0, 0)]
+                out += [(f"{i}.wq_gate", Q4_0, 2 * att, H, 0, qkv_pass), (f"{i}.wk", Q4_0, kvd, H, 0, qkv_pass),
+                        (f"{i}.wv", Q4_0, kvd, H, 0, qkv_pass), (f"{i}.wo", Q4_0, H, att, 0, 0)]
             else:
-                out += [(f"{i}.wqkv", Q4_0, 3 * d, H, 0, 0), (f"{i}.wz", Q4_0, d, H, 0, 0),
-                        (f"{i}.wbeta", Q4_0, s.gdn_heads, H, 0, 0), (f"{i}.walpha", Q4_0, s.gdn_heads, H, 0, 0),
-                        (f"{i}.ssm_out", Q4_0, H, d, 256, 0)]
+                out += [(f"{i}.wqkv", Q4_0, 3 * d, H, 0, gdn_pass), (f"{i}.wz", Q4_0, d, H, 0, gdn_pass),
+                        (f"{i}.wbeta", Q4_0, s.gdn_heads, H, 0, gdn_pass),
+                        (f"{i}.walpha", Q4_0, s.gdn_heads, H, 0, gdn_pass), (f"{i}.ssm_out", Q4_0, H, d, 256, 0)]
             out += [(f"{i}.gate", Q4_0, F, H, 0, 0), (f"{i}.up", Q4_0, F, H, 0, 0), (f"{i}.down", Q4_0, H, F, 0, 0)]
         for j, (r0, n) in enumerate(s.head_pieces()):
             out.append((f"output.{j}", Q6_K, n, H, 0, 0))
@@ -318,7 +321,8 @@ class HybridDecoder:
         wb = 0
         for name, fmt, rows, cols, bc, fl, _ in self.matrices():
             r0, r1 = row_slice(rows, world, 0, fl)
-            wb += (weight_device_bytes(r1 - r0, cols, fmt) + 255) // 256 * 256
+            fl_rank = (fl & 0xFF) | UPLOAD_PASS_ROWS((fl >> 8) * (r1 - r0) // rows)  # the hint as the upload scales it
+            wb += (weight_device_bytes(r1 - r0, cols, fmt, fl_rank) + 255) // 256 * 256
         return dict(weight_bytes=wb + (64 << 20), act_floats=self.L.size, state_rows=s.n_gdn * s.gdn_rows,
                     kv_bytes=s.n_attn * s.kv_slot_bytes, kv_ctx=s.kv_ctx)
 

@@ -158,12 +158,17 @@ B200Q_API void b200q_features(uint32_t out[3]);
 B200Q_API int b200q_upload_weight(b200q_ctx *ctx, const void *gguf, unsigned rows, unsigned cols, unsigned format,
                         unsigned block_cols, uint64_t *w_off);
 /* As b200q_upload_weight; flags B200Q_UPLOAD_REPLICATE keeps all rows on every rank of a row-sharded context
- * (for matrices read by GET_ROW, such as the token embedding). */
+ * (for matrices read by GET_ROW, such as the token embedding). B200Q_UPLOAD_PASS_ROWS(n) tells a Q4_0 / Q8_0 / Q4_1
+ * matrix that its GEMVs share a multi-output pass of n rows in all (say q, k and v on one x): the panel height is
+ * then chosen for the whole pass, so that the members' panels make one wave of CTAs rather than two (a layout
+ * choice only; results are the same either way). */
 #define B200Q_UPLOAD_REPLICATE 1u
+#define B200Q_UPLOAD_PASS_ROWS(n) ((unsigned)(n) << 8)
 B200Q_API int b200q_upload_weight_ex(b200q_ctx *ctx, const void *gguf, unsigned rows, unsigned cols, unsigned format,
                            unsigned block_cols, unsigned flags, uint64_t *w_off);
-/* Device bytes one matrix takes in the arena (all rows, one rank). */
+/* Device bytes one matrix takes in the arena (all rows, one rank); _ex: uploaded with these flags. */
 B200Q_API size_t b200q_weight_device_bytes(unsigned rows, unsigned cols, unsigned format);
+B200Q_API size_t b200q_weight_device_bytes_ex(unsigned rows, unsigned cols, unsigned format, unsigned flags);
 /* Bytes of one GGUF row of the format (0 for an unknown format). */
 B200Q_API size_t b200q_gguf_row_bytes(unsigned cols, unsigned format);
 /* Reset the bump allocator of the weight arena (all handles become invalid). */
@@ -225,6 +230,9 @@ typedef struct b200q_layout_info {
     uint64_t total_bytes;
 } b200q_layout_info;
 B200Q_API int b200q_layout(unsigned rows, unsigned cols, unsigned format, unsigned sms, b200q_layout_info *out);
+/* As b200q_layout for a matrix uploaded with `flags` (B200Q_UPLOAD_PASS_ROWS). */
+B200Q_API int b200q_layout_ex(unsigned rows, unsigned cols, unsigned format, unsigned sms, unsigned flags,
+                              b200q_layout_info *out);
 /* Repack all rows (dst: total_bytes of the layout for `sms`), and the inverse of one row back to GGUF bytes. */
 B200Q_API int b200q_repack_host(const void *gguf, unsigned rows, unsigned cols, unsigned format, unsigned sms,
                                 void *dst);

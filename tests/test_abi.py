@@ -61,6 +61,19 @@ def test_layout_panels_fill_the_warps(b2):
         assert lay["row_tiles"] == -(-rows // 32) and lay["tiles_per_row_tile"] == cols // 256 // C
 
 
+def test_layout_pass_hint(b2):
+    # members of a multi-output pass (here the DeltaNet q/k/v, z, beta, alpha rows on one x: 8224 rows) take the
+    # panel height of the whole pass, so that their panels make one wave of CTAs
+    hint = b2.UPLOAD_PASS_ROWS(8224)
+    for rows, alone in [(6144, 16), (2048, 8), (16, 2)]:
+        assert b2.layout(rows, 2560, b2.Q4_0)["rows_per_tile"] == alone
+        lay = b2.layout(rows, 2560, b2.Q4_0, flags=hint)
+        assert lay["rows_per_tile"] == 32 and lay["row_tiles"] == -(-rows // 32)
+        assert b2.weight_device_bytes(rows, 2560, b2.Q4_0, hint) == lay["total_bytes"]
+    # K-quant tiles do not depend on the hint
+    assert b2.layout(65520, 2560, 14, flags=hint) == b2.layout(65520, 2560, 14)
+
+
 def test_device_bytes_and_row_bytes(b2):
     assert b2.gguf_row_bytes(2560, 2) == 80 * 18
     assert b2.gguf_row_bytes(2560, 14) == 10 * 210
