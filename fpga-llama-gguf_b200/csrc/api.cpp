@@ -554,6 +554,14 @@ int exec_gdn(b200q_ctx *c, const Pass &p) {
         g.a = snap_if(c, A + ext2[1], g.hv, w, nullptr, rc);
     }
     if (rc) return rc;
+    // the ssm_out GEMV of a WITH_OUT step reads y: the GDN kernel hands it over quantized (Q8_0 / Q8_1 formats)
+    ImageLink out_link;
+    if (p.gdn_with_out && act_type(p.gdn_out.format) != 2 && p.gdn_out.cols == g.hv * S &&
+        size_t(g.hv) * S * 3 / 2 <= kQImageBytes) {
+        g.img = c->qimg[0];
+        g.img_act = act_type(p.gdn_out.format);
+        out_link.in = c->qimg[0];
+    }
     g.pw = take_wait(c);
     CUDA_TRY(c, launch_gdn(g, c->stream, c->pdl));
     ++c->launches;
@@ -564,7 +572,8 @@ int exec_gdn(b200q_ctx *c, const Pass &p) {
             return rc;
     }
     if (p.gdn_with_out) {
-        if ((rc = exec_gemv(c, &p.gdn_out, 1, cmd[7], p.gdn_out.cols, false, none, false, nullptr, nullptr)))
+        if ((rc = exec_gemv(c, &p.gdn_out, 1, cmd[7], p.gdn_out.cols, false, none, false, nullptr, nullptr,
+                            out_link)))
             return rc;
     }
     return 0;

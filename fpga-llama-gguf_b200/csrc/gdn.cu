@@ -11,7 +11,8 @@
 // fully sequential order, left a single warp per SM running ~1800 dependent instructions: ~8 us per step.) The
 // result is within the reference's tolerance, not bit-exact. The per-head sums of squares (L2 of q and k, RMS of y)
 // are four 32-value shuffle-tree sums added in row order, as the CPU oracle is checked against; each CTA forms the
-// q / k sums itself and the y sum from the four CTAs' parts, exchanged through distributed shared memory.
+// q / k sums itself and the y sum from the four CTAs' parts, exchanged through distributed shared memory. When the
+// step's WITH_OUT GEMV follows, each CTA also quantizes its 32 outputs (one Q8_0 block) into that GEMV's x image.
 #include "launch.h"
 #include "peer.cuh"
 #include "pipeline.cuh"
@@ -36,7 +37,7 @@ __device__ __forceinline__ float quad_sum(float p) {
 
 __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads) gdn_kernel(const GdnArgs a) {
     __shared__ __align__(16) float qs[128], ks[128];
-    __shared__ float ycta[32];
+    __shared__ float ycta[32], yout[32];
     __shared__ double red[4];
     __shared__ double ysum[kGdnSplit];  // part p of the head's sum of y^2, written by CTA p into every CTA
     __shared__ float gate[2];
@@ -139,6 +140,11 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
         yv = fmul(silu_f32(zj), nv);
     }
     if (seg == 0) a.y[h * 128 + j] = yv;
+    if (a.img) {  // this CTA's 32 rows are block 4 h + part of the next GEMV's x: its image block, as that pass would
+        if (seg == 0) yout[rloc] = yv;
+        __syncthreads();
+        if (warp == 0) write_image_block(a.img, a.hv * 128, h * kGdnSplit + part, yout[lane], lane, a.img_act);
+    }
 }
 
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st, bool pdl) {

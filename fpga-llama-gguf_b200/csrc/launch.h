@@ -31,6 +31,8 @@ struct GdnArgs {
     float *y = nullptr;
     float scale = 0.0f, l2_eps = 0.0f, rms_eps = 0.0f;
     unsigned l2 = 0;
+    uint8_t *img = nullptr;  // when set: y also as the quantized x image of the next GEMV (one Q8_0 / Q8_1 block per CTA)
+    unsigned img_act = 0;
     PeerWait pw;
 };
 

@@ -183,4 +183,28 @@ __device__ __forceinline__ void load_quant_cta(const int8_t *q, const float *d, 
     __syncthreads();
 }
 
+// Image block b (32 values, lane r holding value r) of a next pass's x, written by a warp: the reference's Q8_0 /
+// Q8_1 arithmetic (gemvq_ref.h:196-245), the same as the x preparation. n: the values of the whole x.
+__device__ __forceinline__ void write_image_block(uint8_t *img, unsigned n, unsigned b, float y, unsigned lane,
+                                                  unsigned act) {
+    const float amax = warp_max(fabsf(y));
+    const float s = fdiv(amax, 127.0f);
+    const float id = s != 0.0f ? fdiv(1.0f, s) : 0.0f;
+    const int q = int(roundf(fmul(y, id)));
+    const int sum = warp_sum_i(q);
+    const uint32_t qb = uint32_t(q & 0xff);
+    const uint32_t w = qb | (__shfl_down_sync(0xffffffffu, qb, 1) << 8) | (__shfl_down_sync(0xffffffffu, qb, 2) << 16) |
+                       (__shfl_down_sync(0xffffffffu, qb, 3) << 24);
+    if ((lane & 3u) == 0) {  // bytes 4k .. 4k + 3: half k / 4, word k % 4
+        const unsigned k = lane / 4;
+        *reinterpret_cast<uint32_t *>(img + (k / 4) * (n / 2) + b * 16 + (k % 4) * 4) = w;
+    }
+    if (lane == 0) {
+        const float dh = half_bits_to_float(float_to_half_bits(s));
+        const float sh = act == 1 ? half_bits_to_float(float_to_half_bits(fmul(float(sum), s))) : 0.0f;
+        *reinterpret_cast<uint4 *>(img + n + b * 16) =
+            make_uint4(__float_as_uint(dh), __float_as_uint(sh), uint32_t(sum), 0u);
+    }
+}
+
 }  // namespace b200q

@@ -158,6 +158,40 @@ def test_gdn_full_options_128_steps_config3(ctx, b2, synth, orc):
     assert out_rel.max() <= 1e-4
 
 
+@pytest.mark.parametrize("fmt", [2, 3])
+def test_gdn_out_image_handoff_bit_identical(ctx, b2, synth, fmt):
+    """A WITH_OUT step hands its ssm_out GEMV the quantized y from the GDN kernel (one Q8_0 / Q8_1 block per CTA);
+    the same step without WITH_OUT leaves the GEMV to quantize y from act. Both give the same bits."""
+    ctx.reset_weights()
+    hv = hk = 16
+    H = 2560
+    r = rng(65, fmt)
+    w_out = synth.q4_0(r, H, hv * 128) if fmt == 2 else synth.q4_1(r, H, hv * 128)
+    h_out = ctx.upload(w_out, H, hv * 128, fmt, block_cols=256)
+    state = r.normal(0, 0.1, hv * 128 * 128).astype(np.float32)
+    QKV, G, B, DT, A, Z, WN, Y, RES, OUT = 0, 6144, 6160, 6176, 6192, 6208, 8256, 8384, 10432, 12992
+    act = np.zeros(16384, np.float32)
+    act[QKV:QKV + 6144] = r.normal(0, 1, 6144)
+    act[G:G + 32] = r.normal(0, 1, 32)
+    act[DT:DT + 16] = r.normal(0, 1, 16)
+    act[A:A + 16] = -np.exp(r.normal(0, 0.5, 16))
+    act[Z:Z + 2048] = r.normal(0, 1, 2048)
+    act[WN:WN + 128] = r.normal(1, 0.1, 128)
+    act[RES:RES + H] = r.normal(0, 1, H)
+    outs = []
+    for flags in (b2.GDN_WITH_OUT, 0):
+        ctx.write(0, act)
+        ctx.write_state(0, state)
+        cl = b2.cmd_list(
+            b2.gdn(hv, hk, QKV, QKV + 2048, QKV + 4096, G, B, Y, 0, 0, 128 ** -0.5,
+                   flags=b2.GDN_L2_QK | b2.GDN_GATED | b2.GDN_GATES | flags, w_off=WN, z_off=Z, dt_off=DT, a_off=A),
+            b2.gemv(fmt, H, 2048, h_out, Y, OUT, b2.GEMV_ADD), b2.add(H, OUT, RES, OUT))
+        assert ctx.run(cl) == 0
+        outs.append(ctx.read(0, act.size))
+    assert np.array_equal(_bits(outs[0][Y:Y + 2048]), _bits(outs[1][Y:Y + 2048]))
+    assert np.array_equal(_bits(outs[0][OUT:OUT + H]), _bits(outs[1][OUT:OUT + H]))
+
+
 @pytest.mark.parametrize("pos", [0, 15, 16, 512, 639])
 def test_attention_argmax_getrow(ctx, b2, synth, orc, pos):
     """ATTN at positions that take one chunk, end or start a chunk, and fill the slot; then ARGMAX and GET_ROW."""
