@@ -228,7 +228,8 @@ __device__ __forceinline__ QImage carve_qimage(unsigned char *p, unsigned cols) 
 // each block into all kXCluster images (distributed shared memory, 16-byte stores). The RMSNORM sum of squares
 // over the whole x: every CTA computes it in the same fixed order (per thread, then a shuffle tree, then the warps
 // in order), so all CTAs get the same scale. Same arithmetic as the reference CPU quantizer (quant.cuh,
-// gemvq_ref.h:196-245). Ends with a cluster barrier: afterwards every image is complete.
+// gemvq_ref.h:196-245). The caller arrived on the cluster barrier at the kernel's start; the wait here (every peer
+// has started) precedes the first store into a peer. Ends with a cluster barrier: afterwards every image is complete.
 constexpr unsigned kXCluster = 4;
 static_assert(kMaxQuantCols / 32 / kXCluster <= kPanelThreads / 2, "one round of two lanes per block");
 template <class Hook>
@@ -280,6 +281,7 @@ __device__ __forceinline__ void prepare_x_cluster(const GemvArgs &a, const QImag
         word[e / 4] |= uint32_t(q & 0xff) << (8 * (e % 4));
     }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    cluster_wait();  // every CTA of the cluster has started (the arrive is at the kernel's start)
     if (live) {
         const uint32_t qa = smem_addr(X.q) + h * (n / 2) + b * 16, ma = smem_addr(X.meta) + b * 16;
         const uint4 qw = make_uint4(word[0], word[1], word[2], word[3]);
@@ -509,6 +511,10 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
         bulk_copy(p, g.base + size_t(pnl0) * g.kc * g.tile_bytes, stg.b_off, stage_bar, pol);
         if (v) bulk_copy(p + stg.b_off, v->base + size_t(pnl0) * v->kc * v->tile_bytes, bytes_b, stage_bar, pol);
     };
+    // x prepared across the cluster: announce that this CTA has started (its shared memory may be written by the
+    // others); the matching wait comes before the first store into a peer
+    const bool cluster_x = !a.qin && !a.xq;
+    if (cluster_x) cluster_arrive_relaxed();
     pdl_launch_dependents();  // the next kernel may start as SMs free up
     // weights never change within a list: a CTA that is resident before the previous kernel completes starts its
     // staging copy now, and asks L2 for the rest of its first panel, so HBM streams while that kernel finishes and
