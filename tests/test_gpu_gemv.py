@@ -126,6 +126,37 @@ def test_group_with_swiglu_conv_add_epilogues(ctx, b2, synth, orc):
     _compare_list(ctx, orc, cl, ws, act, N)
 
 
+def test_pass_rows_hint_changes_layout_not_results(ctx, b2, synth, orc):
+    """The DeltaNet q/k/v, z, beta, alpha rows on one normed x (4 members, 8224 rows): uploaded with
+    B200Q_UPLOAD_PASS_ROWS they take 32-row panels (one wave), without it 16 / 8 / 2-row panels (two waves); the
+    outputs are the same bits, and the oracle's."""
+    r = rng(47)
+    H = 2560
+    shapes = [(6144, H), (2048, H), (16, H), (16, H)]
+    mats = [synth.q4_0(r, rows, cols) for rows, cols in shapes]
+    act = np.zeros(1 << 15, np.float32)
+    act[:H] = r.normal(0, 1, H)
+    act[H:2 * H] = r.normal(1, 0.1, H)
+    XN, Y = 2 * H, 3 * H
+    outs = []
+    for flags in (0, b2.UPLOAD_PASS_ROWS(8224)):
+        ctx.reset_weights()
+        hs = [ctx.upload(m, rows, cols, b2.Q4_0, flags=flags) for m, (rows, cols) in zip(mats, shapes)]
+        offs = [Y, Y + 6144, Y + 8192, Y + 8208]
+        cl = b2.cmd_list(b2.rmsnorm(H, 0, H, XN, 1e-6, flags=b2.NORM_DEFER),
+                         *[b2.gemv(b2.Q4_0, rows, cols, h, XN, o) for h, (rows, cols), o in zip(hs, shapes, offs)])
+        ctx.write(0, act)
+        assert ctx.run(cl) == 0
+        outs.append(ctx.read(Y, 8224))
+        if flags:
+            ws = {h: (m.reshape(-1), rows, cols, b2.Q4_0) for h, m, (rows, cols) in zip(hs, mats, shapes)}
+            ref = act.copy()
+            assert orc.run_list(ref, cl, ws) == 0
+            assert np.array_equal(_bits(outs[-1]), _bits(ref[Y:Y + 8224]))
+    assert b2.layout(2048, H, b2.Q4_0)["rows_per_tile"] != b2.layout(2048, H, b2.Q4_0, flags=b2.UPLOAD_PASS_ROWS(8224))["rows_per_tile"]
+    assert np.array_equal(_bits(outs[0]), _bits(outs[1]))
+
+
 def test_fused_ffn_block_config1(ctx, b2, synth, orc):
     """Config 1: RMSNorm (deferred) -> Q8_0 gate+up in one pass -> SwiGLU -> down -> residual add."""
     ctx.reset_weights()
