@@ -20,6 +20,7 @@
 namespace b200q {
 
 constexpr unsigned kAttnThreads = 256, kAttnWarps = kAttnThreads / 32, kAttnMaxGroup = 16;
+constexpr unsigned kMergeBatch = 24;  // chunk partials a merging thread holds in registers at once
 
 __device__ __forceinline__ void half8_to_float(uint4 u, float *f) {
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -192,6 +193,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     __syncthreads();
     if (!last_s) return;
     __threadfence();
+    // the chunks' partial outputs of this thread's first item, requested now so that they arrive with the chunk
+    // statistics read below (one round trip for both)
+    const unsigned nv4 = hd / 4;
+    float4 pv[kMergeBatch];
+    if (threadIdx.x < G * nv4) {
+        const unsigned g = threadIdx.x / nv4, e4 = threadIdx.x % nv4;
+        const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride + 4 * e4;
+#pragma unroll
+        for (unsigned u = 0; u < kMergeBatch; ++u)
+            if (u < n_chunks) pv[u] = __ldcg(reinterpret_cast<const float4 *>(base + u * part_stride));
+    }
     // merge weights per (query head, chunk): warp g reduces over the chunks
     for (unsigned g = warp; g < G; g += kAttnWarps) {
         const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride;
@@ -210,20 +222,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         for (unsigned c = lane; c < n_chunks; c += 32) S.w[g * a.max_chunks + c] *= inv;
     }
     __syncthreads();
-    // four outputs per thread: one 16-byte load per chunk, all chunks' loads in flight before the sums (in chunk order)
-    const unsigned nv4 = hd / 4;
+    // four outputs per thread: one 16-byte load per chunk, a batch of chunks' loads in flight before their sums (in
+    // chunk order); the first batch of the first item is already here
     for (unsigned it = threadIdx.x; it < G * nv4; it += kAttnThreads) {
         const unsigned g = it / nv4, e4 = it % nv4;
         const float *base = a.part + size_t(kvh * G + g) * a.max_chunks * part_stride + 4 * e4;
         const float *w = S.w + g * a.max_chunks;
         float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (unsigned c0m = 0; c0m < n_chunks; c0m += 8) {
-            float4 pv[8];
+        for (unsigned c0m = 0; c0m < n_chunks; c0m += kMergeBatch) {
+            if (c0m > 0 || it != threadIdx.x) {
 #pragma unroll
-            for (unsigned u = 0; u < 8; ++u)
-                if (c0m + u < n_chunks) pv[u] = __ldcg(reinterpret_cast<const float4 *>(base + (c0m + u) * part_stride));
+                for (unsigned u = 0; u < kMergeBatch; ++u)
+                    if (c0m + u < n_chunks)
+                        pv[u] = __ldcg(reinterpret_cast<const float4 *>(base + (c0m + u) * part_stride));
+            }
 #pragma unroll
-            for (unsigned u = 0; u < 8; ++u) {
+            for (unsigned u = 0; u < kMergeBatch; ++u) {
                 if (c0m + u < n_chunks) {
                     const float wc = w[c0m + u];
                     y.x = fmaf(wc, pv[u].x, y.x);
