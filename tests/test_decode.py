@@ -40,7 +40,7 @@ def _oracle_tokens(orc, m, ws, n_tokens, act=None, state=None, kv=None):
     return toks, logits, act, state, kv
 
 
-def test_survey_byte_counts_and_list_structure():
+def test_byte_counts_and_list_structure():
     """Bytes per token of the 4B-like and 9B-like shapes (layers + Q6_K head + KV at 512 + DeltaNet state r/w), and
     every token list plans with status 0 in at most 128 commands, with the fusions the model relies on."""
     assert D.SHAPE_4B.bytes_per_token() == 2_180_345_344
