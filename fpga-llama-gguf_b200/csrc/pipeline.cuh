@@ -69,6 +69,13 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
                  "r"(v.w)
                  : "memory");
 }
+// Store into a peer's shared memory that also counts its 16 bytes on the peer's mbarrier (complete_tx), so the peer
+// can wait for a known number of bytes instead of a cluster barrier.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint4 v, uint32_t mbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(mbar)
+                 : "memory");
+}
 __device__ __forceinline__ void st_cluster_f64(uint32_t addr, double v) {
     asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(addr), "d"(v) : "memory");
 }
