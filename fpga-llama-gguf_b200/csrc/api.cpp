@@ -99,6 +99,7 @@ struct b200q_ctx {
     // quantized x images handed from a GEMV pass to the next (Q8_0 / Q8_1 of the output, in the GEMV shared-memory
     // layout), two alternating buffers
     uint8_t *qimg[2] = {nullptr, nullptr};
+    double *nsq[2] = {nullptr, nullptr};  // per-panel sums of squares handed to a deferred norm (alternating)
     float *snap = nullptr;
     size_t snap_used = 0;
     unsigned *dstatus = nullptr;
@@ -231,6 +232,10 @@ struct ImageLink {
     unsigned out_member = 0;
     unsigned out_act = 0;        // activation type of the next pass (0 Q8_0, 1 Q8_1)
     const uint8_t *in = nullptr;  // this pass reads its x image from here
+    double *nsq_out = nullptr;    // this pass writes member nsq_member's per-panel sums of squares here (nsq_out_n)
+    unsigned nsq_member = 0, nsq_out_n = 0;
+    const double *nsq_in = nullptr;  // this pass's deferred norm reads nsq_n such partials instead of its whole x
+    unsigned nsq_n = 0;
 };
 
 int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsigned cols, bool from_nd,
@@ -297,6 +302,14 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
         a.qout = link.out;
         a.qout_member = link.out_member;
         a.qout_act = link.out_act;
+    }
+    if (link.nsq_out && !dbg && !kq) {
+        a.nsq_out = link.nsq_out;
+        a.nsq_member = link.nsq_member;
+    }
+    if (link.nsq_in && !dbg && !kq && from_nd && !nd.materialize && !prequant && !xhit) {
+        a.nsq_in = link.nsq_in;
+        a.nsq_n = link.nsq_n;
     }
     if ((prequant || xhit) && !dbg) {
         QuantArgs q;
@@ -674,6 +687,29 @@ int link_image(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link
     return -1;
 }
 
+// Pass p's GEMV output that pass q (the next pass that launches work) normalizes as its deferred RMSNORM's x: p sums
+// the squares of that member's stored values per panel and q adds those partials instead of reading all of x.
+// Needs: q a Q4_0 / Q4_1 GEMV pass on a live deferred norm (not stored), p's member a Q8_0-family matrix whose
+// y is exactly the norm's x, unsharded, with a plain or residual-ADD writer. Returns the member index or -1.
+// (Measured on one box: the 4B-like Q4_0 decode 706 -> 718 tokens/s; for a Q8_0 consumer, whose x preparation
+// overlaps twice the weight bytes, the producer's extra tail cost more than it saved: 140.2 -> 140.7 us per stack
+// step, so Q8_0 consumers read x as before.)
+int link_nsq(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link) {
+    if (p.kind != PassKind::Gemv || q.kind != PassKind::Gemv || !q.from_nd || q.nd.materialize || q.prequant) return -1;
+    if (act_type(q.m[0].format) == 2 || q.m[0].format == B200Q_Q8_0) return -1;
+    for (unsigned i = 0; i < p.n_members; ++i) {
+        const Member &m = p.m[i];
+        if ((m.epi != EpiNone && m.epi != EpiAdd) || m.y_off != q.nd.x_off || m.rows != q.nd.n) continue;
+        const WeightInfo *w = m.w ? m.w : find_w(c, m.handle);
+        if (!w || act_type(w->format) == 2 || w->row_begin != 0 || w->row_end != w->rows || w->n_rt > kMaxNsqPanels)
+            return -1;
+        link.nsq_member = i;
+        link.nsq_out_n = w->n_rt;
+        return int(i);
+    }
+    return -1;
+}
+
 // Executes the passes of a plan on the context stream (no synchronization).
 int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
@@ -686,9 +722,14 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     int rc = 0;
     const uint8_t *img_in = nullptr;  // the image the previous GEMV pass wrote for this one
     unsigned img_turn = 0;
+    const double *nsq_in = nullptr;   // the norm partials the previous GEMV pass wrote for this one
+    unsigned nsq_in_n = 0, nsq_turn = 0;
     for (size_t pi = 0; pi < plan.passes.size(); ++pi) {
         const Pass &p = plan.passes[pi];
-        if (p.kind != PassKind::Gemv && !(p.kind == PassKind::Nop && !p.nd_store)) img_in = nullptr;
+        if (p.kind != PassKind::Gemv && !(p.kind == PassKind::Nop && !p.nd_store)) {
+            img_in = nullptr;
+            nsq_in = nullptr;
+        }
         if ((rc = stamp(c, tr, p.first, 0))) return rc;
         const bool is_pass = p.kind == PassKind::Gemv || p.kind == PassKind::Gdn;
         if (is_pass && (rc = stamp(c, tr, p.first, 1))) return rc;
@@ -698,12 +739,23 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
             ImageLink link;
             if (img_in) link.in = img_in;
             img_in = nullptr;
+            if (nsq_in) {
+                link.nsq_in = nsq_in;
+                link.nsq_n = nsq_in_n;
+            }
+            nsq_in = nullptr;
             size_t qi = pi + 1;  // the next pass that launches work (a deferred RMSNORM's own pass launches none)
             while (qi < plan.passes.size() && plan.passes[qi].kind == PassKind::Nop && !plan.passes[qi].nd_store) ++qi;
             if (qi < plan.passes.size() && link_image(c, p, plan.passes[qi], link) >= 0) {
                 link.out = c->qimg[img_turn];
                 img_in = c->qimg[img_turn];
                 img_turn ^= 1u;
+            }
+            if (qi < plan.passes.size() && link_nsq(c, p, plan.passes[qi], link) >= 0) {
+                link.nsq_out = c->nsq[nsq_turn];
+                nsq_in = c->nsq[nsq_turn];
+                nsq_in_n = link.nsq_out_n;
+                nsq_turn ^= 1u;
             }
             rc = exec_gemv(c, p.m, p.n_members, p.x_off, p.cols, p.from_nd, p.nd, p.prequant, nullptr, nullptr, link);
         }
@@ -842,6 +894,10 @@ int b200q_create(const b200q_config *cfg, b200q_ctx **out) {
     if ((e = cudaMalloc(&qi, 2 * kQImageBytes)) != cudaSuccess) return fail(e, "image scratch");
     c->qimg[0] = qi;
     c->qimg[1] = qi + kQImageBytes;
+    double *nq = nullptr;
+    if ((e = cudaMalloc(&nq, 2 * kMaxNsqPanels * sizeof(double))) != cudaSuccess) return fail(e, "norm partials");
+    c->nsq[0] = nq;
+    c->nsq[1] = nq + kMaxNsqPanels;
     const char *pdl = getenv("B200Q_NO_PDL");
     c->pdl = !(pdl && pdl[0] == '1');
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return fail(e, "init");
@@ -861,6 +917,7 @@ void b200q_destroy(b200q_ctx *c) {
     if (c->comm && g_nccl.comm_destroy) g_nccl.comm_destroy(c->comm);
     cudaFree(c->warena);
     cudaFree(c->qimg[0]);
+    cudaFree(c->nsq[0]);
     cudaFree(c->act);
     cudaFree(c->state);
     cudaFree(c->kv);

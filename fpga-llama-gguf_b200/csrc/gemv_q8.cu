@@ -255,16 +255,30 @@ __device__ __forceinline__ void prepare_x_cluster(const GemvArgs &a, const QImag
         v[4 * i] = xv.x, v[4 * i + 1] = xv.y, v[4 * i + 2] = xv.z, v[4 * i + 3] = xv.w;
         w16[4 * i] = wv.x, w16[4 * i + 1] = wv.y, w16[4 * i + 2] = wv.z, w16[4 * i + 3] = wv.w;
     }
-    // the whole x for the RMSNORM sum (canonical order); the first round is requested before the hook
+    // the RMSNORM sum: from the previous pass's per-panel partials when it wrote them (in panel order, then the
+    // fixed tree), else from the whole x (canonical order); either is requested before the hook
+    const bool partials = norm && a.nsq_in;
     float4 nv[4];
-    if (norm) load16(a.x, n, 0, false, nv);
+    double pa = 0.0;
+    if (partials) {
+        const double p0 = threadIdx.x < a.nsq_n ? __ldcg(a.nsq_in + threadIdx.x) : 0.0;
+        const double p1 = threadIdx.x + kPanelThreads < a.nsq_n ? __ldcg(a.nsq_in + threadIdx.x + kPanelThreads) : 0.0;
+        pa = p0 + p1;
+    } else if (norm) {
+        load16(a.x, n, 0, false, nv);
+    }
     after_loads();
     float scale = 1.0f;
     if (norm) {
-        double acc = sumsq16(nv);
-        for (unsigned r = 1; r * (kPanelThreads / 2) < nb; ++r) {
-            load16(a.x, n, r, false, nv);
-            acc += sumsq16(nv);
+        double acc = pa;
+        if (partials) {
+            for (unsigned i = threadIdx.x + 2 * kPanelThreads; i < a.nsq_n; i += kPanelThreads) acc += __ldcg(a.nsq_in + i);
+        } else {
+            acc = sumsq16(nv);
+            for (unsigned r = 1; r * (kPanelThreads / 2) < nb; ++r) {
+                load16(a.x, n, r, false, nv);
+                acc += sumsq16(nv);
+            }
         }
         scale = norm_scale(acc, n, a.norm_eps, a.norm_mode & 1u, X.red);
     }
@@ -599,6 +613,16 @@ __global__ void __cluster_dims__(kXCluster, 1, 1) __launch_bounds__(kPanelThread
                 } else if (mine) {
                     if (FB) write_row(MB, w.row0 + lrow, usum[lane], acc, nullptr, ps);
                     else write_row(MA, w.row0 + lrow, acc, 0.0f, &res, ps);
+                }
+                if (a.nsq_out && out_member == a.nsq_member) {
+                    // the next pass's deferred-norm sum: this panel's stored values squared, summed in a fixed tree
+                    const float v = !mine ? 0.0f
+                                          : (FB ? row_value(MB, w.row0 + lrow, usum[lane], acc)
+                                                : row_value(MA, w.row0 + lrow, acc, 0.0f, &res));
+                    double sq = double(fmul(v, v));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                    if (lane == 0) a.nsq_out[pnl] = sq;
                 }
                 const unsigned end = min((pnl + 1) * P, w.rows);
                 if (end == w.rows) write_padding(OUT, w.row0 + end, lane, ps);

@@ -63,6 +63,7 @@ struct PeerWait {
 constexpr unsigned kMaxUnits = 4;
 // bytes of a quantized x image of up to 16384 values (quants + meta words)
 constexpr unsigned kQImageBytes = 16384 + 16384 / 32 * 16;
+constexpr unsigned kMaxNsqPanels = 4096;  // per-panel partial sums of squares a pass hands to the next
 
 struct GemvArgs {
     const float *x = nullptr;     // act + x_off (or the deferred norm's x)
@@ -98,6 +99,13 @@ struct GemvArgs {
     uint8_t *qout = nullptr;
     unsigned qout_member = 0;
     unsigned qout_act = 0;        // 0 Q8_0, 1 Q8_1 (the next pass's activation type)
+    // the deferred norm's sum of squares from the pass that wrote x: nsq_in holds one FP64 partial per panel of that
+    // pass (nsq_n of them), read instead of the whole x; nsq_out: this pass writes those partials for member
+    // nsq_member's y (its squares summed per panel)
+    const double *nsq_in = nullptr;
+    unsigned nsq_n = 0;
+    double *nsq_out = nullptr;
+    unsigned nsq_member = 0;
     PeerSync ps;                  // world > 1: sharded members' rows also go to the peers
     PeerWait pw;                  // rows of earlier sharded launches this pass reads
 };

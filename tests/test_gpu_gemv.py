@@ -252,13 +252,15 @@ def test_gemv_chain_hands_over_quantized_x(ctx, b2, synth, orc, chain):
     _compare_list(ctx, orc, cl, ws, act, act.size)
 
 
-def test_two_layer_ffn_stack(ctx, b2, synth, orc):
-    """Two config-1 FFN blocks in one list, the second reading the residual the first wrote through its deferred
-    RMSNORM (each gate+up pass hands its down pass the quantized SwiGLU output)."""
+@pytest.mark.parametrize("fmt", [8, 2])
+def test_two_layer_ffn_stack(ctx, b2, synth, orc, fmt):
+    """Two FFN blocks in one list, the second reading the residual the first wrote through its deferred RMSNORM
+    (each gate+up pass hands its down pass the quantized SwiGLU output; with Q4_0 the first down pass also hands the
+    second gate+up pass its per-panel sums of squares for the norm)."""
     ctx.reset_weights()
-    r = rng(55)
+    r = rng(55, fmt)
     H, F = 2560, 9216
-    ws = _weights_and_list(b2, synth, ctx, [(8, F, H), (8, F, H), (8, H, F)] * 2, r)
+    ws = _weights_and_list(b2, synth, ctx, [(fmt, F, H), (fmt, F, H), (fmt, H, F)] * 2, r)
     hs = list(ws)
     R0, GAIN, XN, FF, R1 = 0, H, 2 * H, 4 * H, 4 * H + F
     act = np.zeros(R1 + H, np.float32)
@@ -268,8 +270,8 @@ def test_two_layer_ffn_stack(ctx, b2, synth, orc):
     for layer, (xin, out) in enumerate(((R0, R1), (R1, R0))):
         hg, hu, hd = hs[3 * layer:3 * layer + 3]
         cmds += [b2.rmsnorm(H, xin, GAIN, XN, 1e-6, flags=b2.NORM_DEFER),
-                 b2.gemv(8, F, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(8, F, H, hu, XN, FF),
-                 b2.gemv(8, H, F, hd, FF, out, b2.GEMV_ADD), b2.add(H, out, xin, out)]
+                 b2.gemv(fmt, F, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(fmt, F, H, hu, XN, FF),
+                 b2.gemv(fmt, H, F, hd, FF, out, b2.GEMV_ADD), b2.add(H, out, xin, out)]
     cl = b2.cmd_list(*cmds)
     got, ref = _compare_list(ctx, orc, cl, ws, act, act.size, exact=False)
     rel = np.abs(got[R0:R0 + H] - ref[R0:R0 + H]) / np.maximum(np.abs(ref[R0:R0 + H]), 1e-30)
