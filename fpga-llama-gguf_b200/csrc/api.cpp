@@ -537,7 +537,7 @@ int exec_rowops(b200q_ctx *c, const Pass &p) {
     return 0;
 }
 
-int exec_gdn(b200q_ctx *c, const Pass &p) {
+int exec_gdn(b200q_ctx *c, const Pass &p, const ImageLink &nsq_link) {
     const uint32_t *cmd = p.cmd[0], *ext = p.cmd[1], *ext2 = p.cmd[2];
     float *A = c->act;
     GdnArgs g;
@@ -575,6 +575,8 @@ int exec_gdn(b200q_ctx *c, const Pass &p) {
         g.img_act = act_type(p.gdn_out.format);
         out_link.in = c->qimg[0];
     }
+    out_link.nsq_out = nsq_link.nsq_out;  // the next pass's deferred-norm partials, from the ssm_out rows
+    out_link.nsq_member = 0;
     g.pw = take_wait(c);
     CUDA_TRY(c, launch_gdn(g, c->stream, c->pdl));
     ++c->launches;
@@ -694,18 +696,32 @@ int link_image(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link
 // (Measured on one box: the 4B-like Q4_0 decode 706 -> 718 tokens/s; for a Q8_0 consumer, whose x preparation
 // overlaps twice the weight bytes, the producer's extra tail cost more than it saved: 140.2 -> 140.7 us per stack
 // step, so Q8_0 consumers read x as before.)
+// 1: member m (index i of its pass) writes q's deferred-norm x and can hand q its partials; 0: it does not; -1: it
+// writes that x but cannot.
+static int nsq_member_ok(const b200q_ctx *c, const Member &m, unsigned i, const Pass &q, ImageLink &link) {
+    if ((m.epi != EpiNone && m.epi != EpiAdd) || m.y_off != q.nd.x_off || m.rows != q.nd.n) return 0;
+    const WeightInfo *w = m.w ? m.w : find_w(c, m.handle);
+    if (!w || act_type(w->format) == 2 || w->row_begin != 0 || w->row_end != w->rows || w->n_rt > kMaxNsqPanels)
+        return -1;
+    link.nsq_member = i;
+    link.nsq_out_n = w->n_rt;
+    return 1;
+}
+
+static bool nsq_consumer(const Pass &q) {
+    return q.kind == PassKind::Gemv && q.from_nd && !q.nd.materialize && !q.prequant &&
+           act_type(q.m[0].format) != 2 && q.m[0].format != B200Q_Q8_0;
+}
+
 int link_nsq(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link) {
-    if (p.kind != PassKind::Gemv || q.kind != PassKind::Gemv || !q.from_nd || q.nd.materialize || q.prequant) return -1;
-    if (act_type(q.m[0].format) == 2 || q.m[0].format == B200Q_Q8_0) return -1;
+    if (!nsq_consumer(q)) return -1;
+    if (p.kind == PassKind::Gdn) {  // the step's WITH_OUT GEMV (ssm_out + residual) as the producer
+        return p.gdn_with_out && nsq_member_ok(c, p.gdn_out, 0, q, link) == 1 ? 0 : -1;
+    }
+    if (p.kind != PassKind::Gemv) return -1;
     for (unsigned i = 0; i < p.n_members; ++i) {
-        const Member &m = p.m[i];
-        if ((m.epi != EpiNone && m.epi != EpiAdd) || m.y_off != q.nd.x_off || m.rows != q.nd.n) continue;
-        const WeightInfo *w = m.w ? m.w : find_w(c, m.handle);
-        if (!w || act_type(w->format) == 2 || w->row_begin != 0 || w->row_end != w->rows || w->n_rt > kMaxNsqPanels)
-            return -1;
-        link.nsq_member = i;
-        link.nsq_out_n = w->n_rt;
-        return int(i);
+        const int r = nsq_member_ok(c, p.m[i], i, q, link);
+        if (r) return r > 0 ? int(i) : -1;
     }
     return -1;
 }
@@ -761,7 +777,20 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
         }
             break;
         case PassKind::Elementwise: rc = exec_elementwise(c, p); break;
-        case PassKind::Gdn: rc = exec_gdn(c, p); break;
+        case PassKind::Gdn:
+        {
+            ImageLink nl;
+            size_t qi = pi + 1;
+            while (qi < plan.passes.size() && plan.passes[qi].kind == PassKind::Nop && !plan.passes[qi].nd_store) ++qi;
+            if (qi < plan.passes.size() && link_nsq(c, p, plan.passes[qi], nl) >= 0) {
+                nl.nsq_out = c->nsq[nsq_turn];
+                nsq_in = c->nsq[nsq_turn];
+                nsq_in_n = nl.nsq_out_n;
+                nsq_turn ^= 1u;
+            }
+            rc = exec_gdn(c, p, nl);
+        }
+            break;
         case PassKind::Ext: rc = exec_ext(c, p); break;
         case PassKind::RowOps: rc = exec_rowops(c, p); break;
         case PassKind::Nop:
