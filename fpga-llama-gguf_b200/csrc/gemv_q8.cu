@@ -257,7 +257,7 @@ __device__ __forceinline__ void prepare_x_cluster(const GemvArgs &a, const QImag
     }
     // the RMSNORM sum: from the previous pass's per-panel partials when it wrote them (in panel order, then the
     // fixed tree), else from the whole x (canonical order); either is requested before the hook
-    const bool partials = norm && a.nsq_in;
+    const bool partials = ASYNC && norm && a.nsq_in;  // (never handed to Q8_0 passes: compiled out of those)
     float4 nv[4];
     double pa = 0.0;
     if (partials) {
