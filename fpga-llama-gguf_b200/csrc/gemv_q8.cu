@@ -762,12 +762,11 @@ cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned fa, unsigned fb, unsigned
     return cudaLaunchKernelEx(&cfg, k, a);
 }
 
+// The quantizer's shared memory stays under the 48 KB every kernel may use without an attribute, for every n the
+// library accepts, so no per-device function attribute is needed.
+static_assert(ximage_bytes(kMaxQuantCols) + 127 <= 48 * 1024, "quantize_kernel's image fits the default shared memory");
+
 cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-        attr_set = true;
-    }
     const size_t smem = (ximage_bytes(a.n) + 127) & ~size_t(127);
     quantize_kernel<<<1, 256, smem, st>>>(a);
     return cudaGetLastError();

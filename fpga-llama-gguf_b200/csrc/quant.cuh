@@ -27,7 +27,7 @@ struct XImage {
     float *scale;   // the norm scale
 };
 
-__host__ __device__ inline size_t ximage_bytes(unsigned cols) {
+__host__ __device__ constexpr size_t ximage_bytes(unsigned cols) {
     return size_t(cols) + 4 * size_t(cols / 32) * 2 + 4 * size_t(cols / 16) + 32 * 8 + 16;
 }
 
