@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Benchmark of the b200q decode hot path (one JSON line on stdout, rank 0).
 
-Workload (the fused FFN block of a 4B-like layer): RMSNorm (eps 1e-6, gain N(1, 0.1))
-deferred into the Q8_0 quantizer, gate and up Q8_0 GEMVs [9216 x 2560] in one pass with the SwiGLU epilogue, the
-down Q8_0 GEMV [2560 x 9216] with the residual ADD epilogue. The blocks are stacked as the layers of a model: L
+Workload (configs[1] of the benchmark configurations, the fused FFN block of a 4B-like layer): RMSNorm (eps 1e-6,
+gain N(1, 0.1)) deferred into the Q8_0 quantizer, gate and up Q8_0 GEMVs [9216 x 2560] in one pass with the SwiGLU
+epilogue, the down Q8_0 GEMV [2560 x 9216] with the residual ADD epilogue. The blocks are stacked as the layers of a model: L
 blocks with distinct weights, each reading the residual stream the previous one wrote, form one command list of the
 reference ISA, replayed as one CUDA Graph per step (one token through the L-layer stack). L is chosen so that the
 weights of one step exceed 3x the 126 MB L2, so every block reads weights that are not L2-resident. Synthetic seeded
@@ -13,6 +13,11 @@ metric: GEMV HBM GB/s = algorithmic bytes of the block (weights in their GGUF bi
 / device time per step. N GPUs (torchrun): every matrix is row-sharded over the GPUs and the outputs all-gathered
 with NCCL inside the graph; the block is the same, so `value` = total algorithmic bytes / max-over-ranks time
 (strong scaling).
+
+Beside the headline the line carries one object per other configuration, each measured on one GPU: `q4_0`
+(configs[0], the standalone Q4_0 GEMV [9216 x 2560]), `kquant` (configs[2], Q5_K [9216 x 2560] and the Q6_K head),
+`gdn_step` (configs[3], 128 sequential DeltaNet steps with conv1d, gates and the ssm_out Q4_0 GEMV) and `decode`
+(configs[4], the 4B-like and 9B-like synthetic decoders, tokens/s).
 
 --impl reference: the reference's own CPU arithmetic (fpga/src/gemvq_ref.h built from the reference sources into
 oracle/_ref, OpenMP over row slices) on the same block and metric, on rank 0's host cores.
@@ -26,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -39,6 +45,8 @@ XIN, GAIN, XN, FF, OUT = 0, H, 2 * H, 4 * H, 4 * H + F
 RES = (XIN, OUT)  # the residual stream alternates between these two rows, layer by layer
 ACT_FLOATS = 1 << 16
 L2_BYTES = 126 << 20
+DTYPE = "int8 x int8 -> int32, f32"  # exact integer block dots, FP32 terms and sums (the reference's arithmetic)
+DATA = "synthetic (seeded GGUF Q8_0 weights of config 1)"
 
 
 def load_package():
@@ -86,7 +94,8 @@ def stack_list(b2, layers, upto=None):
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) while the timed region runs."""
+    """nvidia-smi samples (100 ms) over the whole GPU part of the run (the timed regions are short: a few ms for the
+    stack), into a temporary file."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -95,14 +104,14 @@ class ClockSampler:
     def __init__(self, device: int):
         self.device = device
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        fd, self.path = tempfile.mkstemp(prefix="b200q_clocks_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -116,8 +125,16 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
             self.f.close()
+        self.result = self._summary()
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
 
     def summary(self):
+        return getattr(self, "result", None) or self._summary()
+
+    def _summary(self):
         try:
             rows = [ln.split(",") for ln in open(self.path).read().strip().splitlines() if ln.strip()]
         except Exception:
@@ -127,12 +144,23 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]
                           and "Not" not in r[5 + i]})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        pw = [float(r[3]) for r in rows if len(r) >= 9 and r[3].strip().replace(".", "").isdigit()]
+        # under load: the samples whose power draw is in the upper half of the run's range (idle gaps between the
+        # measurements, set-up and uploads excluded)
+        busy = [c for c, p in zip(sm, pw) if pw and p >= (min(pw) + max(pw)) / 2] if len(pw) == len(sm) else sm
+        return {"sm_mhz": statistics.median(busy or sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(busy),
+                "power_w_max": max(pw) if pw else None,
+                "window": "whole GPU part of the run, 100 ms samples"}
+
+
+# the dominant kernel of the headline workload (the gate+up pass), as ncu names it in this build
+TOP_KERNEL = "gemv_q8_kernel<8, 8, 2, false>"
 
 
 def profiled_traffic(kernel: str):
-    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary, or None."""
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary of this build's kernels, or
+    None when the summary has no capture of that kernel."""
     path = os.path.join(ROOT, "profiles", "gemv_q8_config1_full.txt")
     try:
         lines = open(path).read().splitlines()
@@ -155,12 +183,25 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
-    """The reference CPU path on the host cores: the block's three GEMVs (gemvq_ref.h::reference via oracle/_ref, or
-    the oracle restatement) + the element-wise ops; bounded sample."""
+    """The reference CPU path on the host cores, on a bounded sample of the workload: the block's RMSNorm, three
+    GEMVs, SwiGLU and residual add, each a vector call of the reference's own gemvq_ref.h compiled into oracle/_ref
+    (the GEMVs parallel over row slices with OpenMP, all host threads), or of the restatement when that library is
+    absent."""
+    import ctypes
     import oracle
     sys.path.insert(0, ROOT)
-    b2 = load_package()
+    load_package()
     import fpga_llama_gguf_b200.synth as synth
     wg, wu, wd = gen_block(synth, 0)
     r = synth.rng(1, 99)
@@ -168,19 +209,27 @@ def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
     gain = r.normal(1, 0.1, H).astype(np.float32)
     cores = os.cpu_count() or 1
     use_ref = kind == "reference" and oracle.ref_available()
+    P = ctypes.c_void_p
+    ptr = lambda a: a.ctypes.data_as(P)  # noqa: E731
+    xn, g, u, h = (np.zeros(n, np.float32) for n in (H, F, F, F))
+    d, y = np.zeros(H, np.float32), np.zeros(H, np.float32)
 
     def block():
-        xn = oracle.rownorm(x, gain, H, 1, EPS, 0)
         if use_ref:
-            g = oracle.ref_gemv_omp(wg, xn, F, H, 8, cores)
-            u = oracle.ref_gemv_omp(wu, xn, F, H, 8, cores)
-        else:
-            g, _ = oracle.gemv(wg, xn, F, H, 8)
-            u, _ = oracle.gemv(wu, xn, F, H, 8)
+            R = oracle.ref()
+            R.ref_rmsnorm(ptr(x), ptr(gain), H, EPS, ptr(xn))
+            R.ref_gemv_rows_omp(ptr(wg), ptr(xn), F, H, 8, ptr(g), cores)
+            R.ref_gemv_rows_omp(ptr(wu), ptr(xn), F, H, 8, ptr(u), cores)
+            R.ref_silu_mul(ptr(g), ptr(u), F, ptr(h))
+            R.ref_gemv_rows_omp(ptr(wd), ptr(h), H, F, 8, ptr(d), cores)
+            R.ref_add(ptr(d), ptr(x), H, ptr(y))
+            return y
+        xr = oracle.rownorm(x, gain, H, 1, EPS, 0)
+        gg, _ = oracle.gemv(wg, xr, F, H, 8)
+        uu, _ = oracle.gemv(wu, xr, F, H, 8)
         L = oracle.orc()
-        h = np.array([L.orc_silu_mul1(float(a), float(b), 0) for a, b in zip(g, u)], np.float32)
-        d = oracle.ref_gemv_omp(wd, h, H, F, 8, cores) if use_ref else oracle.gemv(wd, h, H, F, 8)[0]
-        return d + x
+        hh = np.array([L.orc_silu_mul1(float(a), float(b), 0) for a, b in zip(gg, uu)], np.float32)
+        return oracle.gemv(wd, hh, H, F, 8)[0] + x
 
     for _ in range(max(0, warmup)):
         block()
@@ -192,10 +241,115 @@ def cpu_reference(steps: int, warmup: int, budget_s: float, kind: str):
         times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
     gbs = algorithmic_bytes() / per / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
+    what = ("gemvq_ref.h vector calls (rmsnorm, GEMV over OpenMP row slices, silu_mul, add)" if use_ref
+            else "the oracle restatement")
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "cpu_model": cpu_model(),
             "kind": "reference" if use_ref else "port",
-            "sample": f"{len(times)} FFN blocks (gate+up Q8_0 [9216x2560], down [2560x9216]) at {per * 1e3:.1f} ms "
-                      f"each, gemvq_ref.h generic path, {cores} threads"}
+            "sample": f"{len(times)} FFN blocks (gate+up Q8_0 [9216x2560], down [2560x9216]) at {per * 1e3:.2f} ms "
+                      f"each, {what}, {cores} threads"}
+
+
+def timed_graph(ctx, torch, stream, cl, reps: int, warm: int = 5):
+    """Device time (CUDA events on the library's stream) of one replay of list `cl` captured as a graph, in ms."""
+    g = ctx.graph(cl)
+    ctx.launch_many([g], warm)
+    ctx.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    ctx.launch_many([g], reps)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    kernels = g.kernels
+    g.close()
+    return ms, kernels
+
+
+def q4_0_bench(b2, torch, synth, dev: int, world: int) -> dict:
+    """the standalone Q4_0 GEMV [9216 x 2560] against an fp32 N(0, 1) x quantized to Q8_0 inside the pass.
+    One list holds 30 distinct copies of the matrix (398 MB, > 3x L2), consecutive GEMVs reading alternating x rows
+    (so each is its own pass and quantizes its own x); GB/s of the GGUF weight bytes + x + y per GEMV."""
+    if world > 1:
+        return {"note": "measured on one GPU only"}
+    peak, peak_kind = measured_peak()
+    rows, cols, n = 9216, H, 30
+    ctx = b2.Context(device=dev, weight_bytes=n * (b2.weight_device_bytes(rows, cols, b2.Q4_0) + (1 << 20)),
+                     act_floats=1 << 20)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+    r = synth.rng(0, 0)
+    w = synth.q4_0(r, rows, cols)
+    ctx.write(0, synth.activation(r, cols))
+    ctx.write(cols, synth.activation(r, cols))
+    cmds = []
+    for i in range(n):
+        hw = ctx.upload(w, rows, cols, b2.Q4_0)
+        cmds.append(b2.gemv(b2.Q4_0, rows, cols, hw, (i % 2) * cols, 2 * cols + i * rows))
+    ms, kernels = timed_graph(ctx, torch, stream, b2.cmd_list(*cmds), 50)
+    ctx.close()
+    per = w.nbytes + 4 * cols + 4 * rows
+    us = ms * 1e3 / n
+    gbs = per / (us * 1e-6) / 1e9
+    return {"workload": "configs[0] Q4_0 GEMV [9216x2560], x quantized to Q8_0 in the pass", "us_per_gemv": round(us, 3),
+            "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4), "peak_kind": peak_kind,
+            "bytes_per_gemv": per, "copies": n, "kernels_per_gemv": kernels / n,
+            "l2": f"{n} distinct copies ({n * w.nbytes >> 20} MiB) per list"}
+
+
+def gdn_bench(b2, torch, synth, dev: int, world: int, steps: int = 128) -> dict:
+    """128 sequential Gated DeltaNet decode steps (hidden 2560, 16 heads, d_k = d_v = 128): the causal
+    conv1d (k = 4) over the qkv projection with its 3-token state, the step with L2-normalized q / k, the gates from
+    raw projections (beta = sigmoid, g = softplus(g + dt) * a), the gated RMSNorm * silu(z) output, and the ssm_out
+    Q4_0 GEMV [2560 x 2048] with the residual add. 16 steps per list (one graph), replayed 8 times; the state
+    [16, 128, 128] fp32 carries from step to step. Algorithmic bytes per step count the state read and written once,
+    the ssm_out weights and the vectors; the 2 MiB state stays L2-resident across steps, so the latency per step is
+    the number to read (GB/s beside it)."""
+    if world > 1:
+        return {"note": "measured on one GPU only"}
+    peak, peak_kind = measured_peak()
+    hv = hk = 16
+    S = 128
+    r = synth.rng(3, 0)
+    ctx = b2.Context(device=dev, weight_bytes=64 << 20, act_floats=1 << 17, state_rows=hv * S)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+    w_out = synth.q4_0(r, H, hv * S)
+    h_out = ctx.upload(w_out, H, hv * S, b2.Q4_0, block_cols=256)
+    QKV, CW, CS, QKVC = 0, 6144, 30720, 49152
+    G, B, DT, A, Z, WN, Y, RES = 55296, 55312, 55328, 55344, 55360, 57408, 57536, 59584
+    act = np.zeros(1 << 17, np.float32)
+    act[QKV:QKV + 6144] = r.normal(0, 1, 6144)
+    act[CW:CW + 4 * 6144] = r.normal(0, 0.5, 4 * 6144)
+    act[CS:CS + 3 * 6144] = r.normal(0, 1, 3 * 6144)
+    act[G:G + 32] = r.normal(0, 1, 32)
+    act[DT:DT + 16] = r.normal(0, 1, 16)
+    act[A:A + 16] = -np.exp(r.normal(0, 0.5, 16))
+    act[Z:Z + 2048] = r.normal(0, 1, 2048)
+    act[WN:WN + 128] = r.normal(1, 0.1, 128)
+    act[RES:RES + H] = r.normal(0, 1, H)
+    ctx.write(0, act)
+    ctx.write_state(0, r.normal(0, 0.1, hv * S * S).astype(np.float32))
+    per_list = 16
+    cmds = []
+    for t in range(per_list):
+        # the residual stream alternates between two rows, step by step
+        res_in, res_out = (RES, RES + H) if t % 2 == 0 else (RES + H, RES)
+        cmds += [b2.conv(6144, QKV, CW, QKVC, CS, CS, True),
+                 b2.gdn(hv, hk, QKVC, QKVC + 2048, QKVC + 4096, G, B, Y, 0, 0, S ** -0.5,
+                        flags=b2.GDN_L2_QK | b2.GDN_GATED | b2.GDN_GATES | b2.GDN_WITH_OUT,
+                        w_off=WN, z_off=Z, dt_off=DT, a_off=A),
+                 b2.gemv(b2.Q4_0, H, hv * S, h_out, Y, res_out, b2.GEMV_ADD), b2.add(H, res_out, res_in, res_out)]
+    cl = b2.cmd_list(*cmds)
+    reps = steps // per_list
+    ms, kernels = timed_graph(ctx, torch, stream, cl, reps * 4)
+    ctx.close()
+    us = ms * 1e3 / per_list
+    # algorithmic bytes per step as the configuration's scope counts them: the state read and written once
+    # (2 x 1 MiB), the ssm_out weights in their GGUF bits (2,949,120) and the step's vectors (200,832)
+    per = 2 * hv * S * S * 4 + w_out.nbytes + 200_832
+    gbs = per / (us * 1e-6) / 1e9
+    return {"workload": "configs[3] GDN step + conv1d + gates + gated norm + ssm_out Q4_0 [2560x2048] + residual",
+            "steps": reps * 4 * per_list, "us_per_step": round(us, 3), "bytes_per_step": per, "gbs": round(gbs, 1),
+            "frac_of_peak": round(gbs / peak, 4), "peak_kind": peak_kind, "kernels_per_step": kernels / per_list,
+            "note": "the 2 MiB state is L2-resident across steps: latency per step is the figure of merit"}
 
 
 def kquant_bench(b2, torch, synth, dev: int, world: int, max_over_ranks, barrier) -> dict:
@@ -329,6 +483,7 @@ def main():
                     "(comma list of 4b, 9b; empty for none)")
     ap.add_argument("--decode-tokens", type=int, default=128)
     ap.add_argument("--no-kquant", action="store_true", help="skip the configs[2] K-quant GEMV measurement")
+    ap.add_argument("--no-extras", action="store_true", help="skip the configs[0] / configs[3] objects")
     ap.add_argument("--decode-only", action="store_true", help="run only the decode measurement (for profiling "
                     "runs); the line then carries the decode object and no GEMV metric")
     args = ap.parse_args()
@@ -343,6 +498,8 @@ def main():
     per_layer = weight_bytes() // world
     n_layers = min(40, max(2, int(np.ceil(3 * L2_BYTES / max(per_layer, 1)))))
     config["layers"] = n_layers
+    config["l2"] = (f"{n_layers} layers with distinct weights per step ({n_layers * per_layer >> 20} MiB per GPU > "
+                    f"3x L2)")
 
     if args.impl == "reference":
         if rank != 0:
@@ -351,8 +508,8 @@ def main():
         line = {"metric": "GEMV HBM GB/s", "value": cb["value"], "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(n_layers * algorithmic_bytes() / cb["value"] / 1e6, 4),
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8/f32",
-                "data": "synthetic", "config": config, "impl": "reference", "cpu_baseline": cb,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": DATA,
+                "config": config, "impl": "reference", "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
@@ -421,21 +578,21 @@ def main():
     ctx.write(GAIN, gain)
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
 
+    # clocks sampled from the warm-up to the end of the GPU measurements
+    clk = ClockSampler(dev).__enter__()
     # warm-up
     ctx.launch_many([stack], args.warmup)
     ctx.synchronize()
     barrier()
     # timed region: K steps (each a replay of the whole stack)
-    with ClockSampler(dev) as clk:
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        ctx.launch_many([stack], args.steps)
-        end.record(stream)
-        end.synchronize()
-        ms = start.elapsed_time(end) / args.steps
-        ms = max_over_ranks(ms)
-        barrier()
-    clocks = clk.summary()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    ctx.launch_many([stack], args.steps)
+    end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms)
+    barrier()
     step_bytes = n_layers * algorithmic_bytes()
     value = step_bytes / (ms * 1e-3) / 1e9
     launches = stack.kernels * args.steps
@@ -459,7 +616,7 @@ def main():
                 "kernel": "gemv_q8_kernel (deferred RMSNorm + Q8_0 gate/up pair + SwiGLU)",
                 "algorithmic_bytes_per_launch": ru_bytes, "us_per_launch": round(ru_ms * 1e3, 3),
                 "peak_kind": peak_kind}
-    roofline["traffic"] = profiled_traffic("gemv_q8_kernel<8, 8, 2>")
+    roofline["traffic"] = profiled_traffic(TOP_KERNEL)
 
     # end to end through the public API with host buffers: every step copies its x in from page-locked host memory
     # (stream-ordered b200q_act_write_async), replays the stack and copies y out (b200q_act_read_async); the host
@@ -490,31 +647,34 @@ def main():
            "d2h_bytes_per_step": 4 * H, "ms_per_step": round(t_e2e * 1e3, 4),
            "host_synced": {"value": round(step_bytes / t_sync / 1e9, 2), "ms_per_step": round(t_sync * 1e3, 4)}}
 
+    for g in (stack, ru):
+        g.close()
+    ctx.close()
+
+    q40 = gdn = {}
+    if not args.no_extras:
+        q40 = q4_0_bench(b2, torch, synth, dev, world)
+        gdn = gdn_bench(b2, torch, synth, dev, world)
+    decode = run_decodes()
+    kquant = kquant_bench(b2, torch, synth, dev, world, max_over_ranks, barrier) if not args.no_kquant else {}
+    clk.__exit__(None, None, None)
+    clocks = clk.summary()
+    if dist:
+        dist.destroy_process_group()
+
     cpu = None
     if rank == 0 and world == 1:
         try:
             cpu = cpu_reference(3, 1, min(args.cpu_budget, 20.0), "reference")
         except Exception as e:  # the CPU baseline is a reported number only
             cpu = {"value": None, "error": str(e)}
-
-    for g in (stack, ru):
-        g.close()
-    ctx.close()
-
-    decode = run_decodes()
-    kquant = kquant_bench(b2, torch, synth, dev, world, max_over_ranks, barrier) if not args.no_kquant else {}
-    if dist:
-        dist.destroy_process_group()
     if rank == 0:
         line = {"metric": "GEMV HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32",
-                "data": "synthetic (seeded GGUF Q8_0 weights of config 1)",
-                "config": dict(config, l2=f"{n_layers} layers with distinct weights per step "
-                                                             f"({n_layers * per_layer >> 20} MiB per GPU > 3x L2)",
-                               frac_of_peak=round(value / peak, 4)),
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
-                "decode": decode, "kquant": kquant}
+                "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": DATA, "config": config,
+                "frac_of_peak": round(value / peak, 4), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clocks, "q4_0": q40, "kquant": kquant, "gdn_step": gdn,
+                "decode": decode}
         print(json.dumps(line), flush=True)
     return 0
 
