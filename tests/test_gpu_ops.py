@@ -125,7 +125,7 @@ def test_gdn_full_options_128_steps_config3(ctx, b2, synth, orc):
     ctx.write(0, act)
     ctx.write_state(0, state)
     ref_act, ref_state = act.copy(), state.copy()
-    worst = 0.0
+    worst = worst_unfloored = 0.0
     for step in range(128):
         x = r.normal(0, 1, 6144).astype(np.float32)
         gb = r.normal(0, 1, 32).astype(np.float32)
@@ -150,9 +150,14 @@ def test_gdn_full_options_128_steps_config3(ctx, b2, synth, orc):
         assert orc.run_list(ref_act, cl, ws, state=ref_state) == 0
         if step % 32 == 31 or step == 0:
             gs = ctx.read_state(0, hv * 128)
-            rel = np.abs(gs - ref_state) / np.maximum(np.abs(ref_state), 1e-3)
-            worst = max(worst, float(rel.max()))
+            d = np.abs(gs - ref_state)
+            worst = max(worst, float((d / np.maximum(np.abs(ref_state), 1e-3)).max()))
+            worst_unfloored = max(worst_unfloored, float((d / np.abs(ref_state)).max()))
     got = ctx.read(0, act.size)
+    # relative error with a 1e-3 floor (1% of the state's initial standard deviation; entries below it are measured
+    # against the floor); the unfloored maximum is reported beside it (entries near zero dominate it)
+    print(f"config 3, 128 steps, GPU vs oracle states: max relative error {worst:.2e} (floor 1e-3), "
+          f"{worst_unfloored:.2e} (unfloored)")
     assert worst <= 1e-4
     out_rel = np.abs(got[OUT:OUT + H] - ref_act[OUT:OUT + H]) / np.maximum(np.abs(ref_act[OUT:OUT + H]), 1e-3)
     assert out_rel.max() <= 1e-4
