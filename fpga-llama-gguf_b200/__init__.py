@@ -34,6 +34,7 @@ SILU_MUL_SIGMOID = 1
 Q4_0, Q4_1, Q8_0, Q5_K, Q6_K = 2, 3, 8, 13, 14
 FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53000F)
 UPLOAD_REPLICATE = 1
+UPLOAD_SRC_Q4_0X8 = 2
 
 
 def UPLOAD_PASS_ROWS(n: int) -> int:
@@ -200,6 +201,19 @@ def lib() -> ctypes.CDLL:
         "b200q_layout_ex": (I, [U, U, U, U, U, P]),
         "b200q_repack_host": (I, [P, U, U, U, U, P]),
         "b200q_unpack_row_host": (I, [P, U, U, U, U, U, P]),
+        "b200q_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P), ctypes.c_char_p, U]),
+        "b200q_gguf_close": (None, [P]),
+        "b200q_gguf_version": (U32, [P]),
+        "b200q_gguf_n_tensors": (ctypes.c_uint64, [P]),
+        "b200q_gguf_n_kv": (ctypes.c_uint64, [P]),
+        "b200q_gguf_tensor": (I, [P, ctypes.c_uint64, P]),
+        "b200q_gguf_find_tensor": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+        "b200q_gguf_kv": (I, [P, ctypes.c_uint64, P]),
+        "b200q_gguf_find_kv": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+        "b200q_gguf_get_int": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]),
+        "b200q_gguf_get_float": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+        "b200q_upload_gguf_tensor": (I, [P, P, ctypes.c_uint64, U, U, ctypes.POINTER(ctypes.c_uint64)]),
+        "b200q_q4_0x8_to_q4_0": (I, [P, U, U, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -219,7 +233,10 @@ EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream",
             "b200q_graph_launch", "b200q_graph_launch_many", "b200q_graph_destroy", "b200q_graph_kernel_count", "b200q_plan",
             "b200q_debug_quantize", "b200q_debug_block_sums", "b200q_quantize_noalloc", "b200q_comm_unique_id",
             "b200q_comm_init",
-            "b200q_comm_world", "b200q_row_slice", "b200q_layout", "b200q_layout_ex", "b200q_repack_host", "b200q_unpack_row_host"]
+            "b200q_comm_world", "b200q_row_slice", "b200q_layout", "b200q_layout_ex", "b200q_repack_host", "b200q_unpack_row_host",
+            "b200q_gguf_open", "b200q_gguf_close", "b200q_gguf_version", "b200q_gguf_n_tensors", "b200q_gguf_n_kv",
+            "b200q_gguf_tensor", "b200q_gguf_find_tensor", "b200q_gguf_kv", "b200q_gguf_find_kv", "b200q_gguf_get_int",
+            "b200q_gguf_get_float", "b200q_upload_gguf_tensor", "b200q_q4_0x8_to_q4_0"]
 
 
 class _LayoutInfo(ctypes.Structure):
@@ -304,6 +321,111 @@ def row_slice(rows: int, world: int, rank: int, flags: int = 0) -> tuple:
     if rc != 0:
         raise B200QError(rc, "bad world / rank")
     return int(r0.value), int(r1.value)
+
+
+class _GgufTensorInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_uint32), ("n_dims", ctypes.c_uint32),
+                ("ne", ctypes.c_uint64 * 4), ("offset", ctypes.c_uint64), ("bytes", ctypes.c_uint64),
+                ("data", ctypes.c_void_p)]
+
+
+class _GgufKvInfo(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_char_p), ("type", ctypes.c_uint32), ("array_type", ctypes.c_uint32),
+                ("count", ctypes.c_uint64), ("value", ctypes.c_void_p), ("str_len", ctypes.c_uint64)]
+
+
+class GgufFile:
+    """A .gguf file opened by the library's reader (b200q_gguf_open): tensor table, metadata, and tensor data as
+    numpy views of the read-only mapping (valid until close)."""
+
+    def __init__(self, path: str):
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = lib().b200q_gguf_open(os.fsencode(path), ctypes.byref(h), err, len(err))
+        if rc != 0:
+            raise B200QError(rc, err.value.decode())
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().b200q_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def version(self) -> int:
+        return int(lib().b200q_gguf_version(self.h))
+
+    def tensor(self, index: int) -> dict:
+        t = _GgufTensorInfo()
+        if lib().b200q_gguf_tensor(self.h, index, ctypes.byref(t)) != 0:
+            raise IndexError(index)
+        data = None
+        if t.data and t.bytes:
+            data = np.ctypeslib.as_array(ctypes.cast(t.data, ctypes.POINTER(ctypes.c_uint8)), shape=(t.bytes,))
+        return {"name": t.name.decode(), "type": t.type, "n_dims": t.n_dims, "ne": list(t.ne)[:max(1, t.n_dims)],
+                "offset": t.offset, "bytes": t.bytes, "data": data}
+
+    def tensors(self) -> list:
+        return [self.tensor(i) for i in range(int(lib().b200q_gguf_n_tensors(self.h)))]
+
+    def find(self, name: str) -> int:
+        i = ctypes.c_uint64()
+        if lib().b200q_gguf_find_tensor(self.h, name.encode(), ctypes.byref(i)) != 0:
+            raise KeyError(name)
+        return int(i.value)
+
+    def keys(self) -> list:
+        out = []
+        for i in range(int(lib().b200q_gguf_n_kv(self.h))):
+            kv = _GgufKvInfo()
+            lib().b200q_gguf_kv(self.h, i, ctypes.byref(kv))
+            out.append(kv.key.decode())
+        return out
+
+    def get_int(self, key: str) -> int:
+        v = ctypes.c_int64()
+        if lib().b200q_gguf_get_int(self.h, key.encode(), ctypes.byref(v)) != 0:
+            raise KeyError(key)
+        return int(v.value)
+
+    def get_float(self, key: str) -> float:
+        v = ctypes.c_double()
+        if lib().b200q_gguf_get_float(self.h, key.encode(), ctypes.byref(v)) != 0:
+            raise KeyError(key)
+        return float(v.value)
+
+    def get_str(self, key: str) -> str:
+        i = ctypes.c_uint64()
+        if lib().b200q_gguf_find_kv(self.h, key.encode(), ctypes.byref(i)) != 0:
+            raise KeyError(key)
+        kv = _GgufKvInfo()
+        lib().b200q_gguf_kv(self.h, i.value, ctypes.byref(kv))
+        if kv.type != 8:
+            raise TypeError(f"{key} is not a string")
+        return ctypes.string_at(kv.value, kv.str_len).decode()
+
+
+def q4_0x8_to_q4_0(src: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Q4_0 rows back from ggml's CPU_REPACK block_q4_0x8 layout (b200q_q4_0x8_to_q4_0)."""
+    src = np.ascontiguousarray(src, dtype=np.uint8).reshape(-1)
+    out = np.zeros((rows, cols // 32 * 18), np.uint8)
+    rc = lib().b200q_q4_0x8_to_q4_0(src.ctypes.data_as(ctypes.c_void_p), rows, cols,
+                                    out.ctypes.data_as(ctypes.c_void_p))
+    if rc != 0:
+        raise B200QError(rc, "q4_0x8_to_q4_0: rows must be a multiple of 8, cols of 32")
+    return out
 
 
 def gguf_row_bytes(cols: int, fmt: int) -> int:
@@ -400,11 +522,17 @@ class Context:
 
     def upload(self, gguf: np.ndarray, rows: int, cols: int, fmt: int, block_cols: int = 0, flags: int = 0) -> int:
         data = np.ascontiguousarray(gguf, dtype=np.uint8)
-        if data.size != rows * gguf_row_bytes(cols, fmt):
+        if data.size != rows * gguf_row_bytes(cols, fmt):  # (a Q4_0x8 source has the same byte count)
             raise ValueError("GGUF byte count does not match rows x cols of the format")
         off = ctypes.c_uint64()
         self._check(lib().b200q_upload_weight_ex(self.h, data.ctypes.data_as(ctypes.c_void_p), rows, cols, fmt,
                                                  block_cols, flags, ctypes.byref(off)))
+        return int(off.value)
+
+    def upload_gguf(self, f: "GgufFile", name: str, block_cols: int = 0, flags: int = 0) -> int:
+        """b200q_upload_gguf_tensor: the named 2-D tensor of an open GGUF file, uploaded straight from its mapping."""
+        off = ctypes.c_uint64()
+        self._check(lib().b200q_upload_gguf_tensor(self.h, f.h, f.find(name), block_cols, flags, ctypes.byref(off)))
         return int(off.value)
 
     def reset_weights(self):

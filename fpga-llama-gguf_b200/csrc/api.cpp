@@ -1007,8 +1007,16 @@ int b200q_upload_weight_ex(b200q_ctx *c, const void *gguf, unsigned rows, unsign
     const unsigned pass_rows = unsigned(uint64_t(flags >> 8) * (r1 - r0) / rows);
     const DeviceLayout L = device_layout(r1 - r0, cols, format, unsigned(c->sms), pass_rows);
     if (c->wused + L.total > c->wbytes) return set_err(c, B200Q_ERR_NOMEM, "weight arena full");
+    const uint8_t *src = static_cast<const uint8_t *>(gguf);
+    std::vector<uint8_t> rows_q40;
+    if (flags & B200Q_UPLOAD_SRC_Q4_0X8) {  // CPU_REPACK source: back to GGUF rows first (ggml-xrt.cpp:675-710)
+        if (format != B200Q_Q4_0 || rows % 8) return set_err(c, B200Q_ERR_ARG, "upload: Q4_0x8 source needs Q4_0, rows % 8 == 0");
+        rows_q40.resize(size_t(rows) * (cols / 32) * 18);
+        b200q_q4_0x8_to_q4_0(gguf, rows, cols, rows_q40.data());
+        src = rows_q40.data();
+    }
     std::vector<uint8_t> host(L.total);
-    repack_rows(static_cast<const uint8_t *>(gguf), r0, r1, L, host.data());
+    repack_rows(src, r0, r1, L, host.data());
     CUDA_TRY(c, cudaMemcpy(c->warena + c->wused, host.data(), L.total, cudaMemcpyHostToDevice));
     WeightInfo w;
     w.handle = c->wused;

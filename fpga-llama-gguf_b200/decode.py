@@ -329,6 +329,21 @@ class HybridDecoder:
     def load(self, ctx, keep: dict | None = None) -> None:
         """Uploads the weights and writes act, the DeltaNet states and the KV cache."""
         self.upload(lambda g, rows, cols, fmt, bc, fl: ctx.upload(g, rows, cols, fmt, block_cols=bc, flags=fl), keep)
+        self.load_resident(ctx)
+
+    def load_gguf(self, ctx, gguf_file) -> None:
+        """As load, with every matrix read from an open GGUF file (GgufFile) by name instead of generated: the
+        library's reader hands the tensor's GGUF bytes from the file mapping straight to the upload."""
+        for name, fmt, rows, cols, bc, fl, _ in self.matrices():
+            t = gguf_file.tensor(gguf_file.find(name))
+            if t["type"] != fmt or t["ne"][:2] != [cols, rows]:
+                raise ValueError(f"GGUF tensor {name}: type {t['type']} shape {t['ne']}, expected {fmt} {[cols, rows]}")
+            self.handles[name] = ctx.upload_gguf(gguf_file, name, block_cols=bc, flags=fl)
+        self.load_resident(ctx)
+
+    def load_resident(self, ctx) -> None:
+        """Writes act (norm weights, conv kernels and histories, gates' parameters), the DeltaNet states and the KV
+        cache."""
         ctx.write(0, self.initial_act())
         ctx.write_state(0, self.initial_state())
         ctx.write_kv(0, self.initial_kv())

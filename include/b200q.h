@@ -164,6 +164,9 @@ B200Q_API int b200q_upload_weight(b200q_ctx *ctx, const void *gguf, unsigned row
  * choice only; results are the same either way). */
 #define B200Q_UPLOAD_REPLICATE 1u
 #define B200Q_UPLOAD_PASS_ROWS(n) ((unsigned)(n) << 8)
+/* the source is a Q4_0 matrix in ggml's CPU_REPACK block_q4_0x8 layout (rows a multiple of 8): it is read back to
+ * GGUF rows first (b200q_q4_0x8_to_q4_0), as the reference backend does for tensors of a CPU_REPACK buffer */
+#define B200Q_UPLOAD_SRC_Q4_0X8 2u
 B200Q_API int b200q_upload_weight_ex(b200q_ctx *ctx, const void *gguf, unsigned rows, unsigned cols, unsigned format,
                            unsigned block_cols, unsigned flags, uint64_t *w_off);
 /* Device bytes one matrix takes in the arena (all rows, one rank); _ex: uploaded with these flags. */
@@ -258,18 +261,68 @@ B200Q_API int b200q_debug_block_sums(b200q_ctx *ctx, const uint32_t cmd[8], int3
  * device memory: a host runtime whose device memory is all reserved up front by its own pool, or a diagnostic path
  * that runs after an allocation failed. It allocates nothing. Its scratch is a fixed array in device memory carried
  * by the library (one per device), so n is limited to B200Q_NOALLOC_MAX_N; larger n is rejected with B200Q_ERR_ARG.
- *   x, norm_w: device pointers on `device` (norm_w NULL: no deferred RMSNORM; else eps and norm_flags as in
- *   RMSNORM); stream: a cudaStream_t of that device (NULL: the legacy default stream), synchronized before the call
- *   returns; q / scales / bsums: host memory as in b200q_debug_quantize (NULL: not copied); err_msg: receives the
- *   reason of a failure (may be NULL).
+ *   x, norm_w: device (or managed) memory of `device`, 4-byte aligned, each holding n floats inside its allocation
+ *   (norm_w NULL: no deferred RMSNORM; else eps and norm_flags as in RMSNORM) — checked on the host before the
+ *   launch, so a host pointer, another device's pointer, a misaligned pointer or a range past the allocation's end
+ *   returns B200Q_ERR_ARG and never reaches the GPU; stream: a cudaStream_t of that device (NULL: the legacy default
+ *   stream; a stream of another device is rejected), synchronized before the call returns; q / scales / bsums: host
+ *   memory as in b200q_debug_quantize (NULL: not copied); err_msg: receives the reason of a failure (may be NULL).
  * The first call on a device looks up the scratch address (cudaGetSymbolAddress, which may initialize the CUDA
- * context): make it before any stream capture. Nothing in the scratch needs to start at zero. Calls on the same
- * device that overlap (from other threads, or on other streams before the previous one returned) share the scratch
- * and race: the library serializes calls within one process, other processes must not share a device this way. */
+ * context): make it before any stream capture. The address is kept per device and looked up again when the device's
+ * context changed (after cudaDeviceReset). Nothing in the scratch needs to start at zero. Calls on the same device
+ * that overlap (from other threads, or on other streams before the previous one returned) share the scratch and
+ * race: the library serializes calls within one process, other processes must not share a device this way. */
 #define B200Q_NOALLOC_MAX_N 16384
 B200Q_API int b200q_quantize_noalloc(int device, const float *x, unsigned n, unsigned format, const float *norm_w,
                                      float norm_eps, unsigned norm_flags, void *stream, int8_t *q, void *scales,
                                      int32_t *bsums, char *err_msg, unsigned err_len);
+
+/* ---- GGUF files and the CPU backend's Q4_0x8 layout (host only) ------------------------------------------------
+ * For callers that load weights without llama.cpp. The reference backend receives its weights from llama.cpp's GGUF
+ * loader as ggml tensors (ggml-xrt.cpp:642-653 keys them by tensor, data pointer, type, shape and bytes) and reads
+ * their rows back to GGUF blocks before its own repack (xrt_gguf, ggml-xrt.cpp:675-710); these functions give the
+ * same GGUF rows straight from a file.
+ * b200q_gguf_open maps the file read-only and parses the header, metadata and tensor table (GGUF v2 / v3); every
+ * length and offset is checked against the file size, and a truncated or corrupt file returns B200Q_ERR_ARG with the
+ * reason in err. Pointers handed out (names, keys, values, tensor data) stay valid until b200q_gguf_close. */
+typedef struct b200q_gguf b200q_gguf;
+typedef struct b200q_gguf_tensor_info {
+    const char *name;    /* NUL-terminated */
+    uint32_t type;       /* ggml type id (B200Q_Q4_0, ..., 0 F32, 1 F16) */
+    uint32_t n_dims;
+    uint64_t ne[4];      /* ne[0] elements per row (columns), ne[1] rows; 1 past n_dims */
+    uint64_t offset;     /* byte offset of the data in the file */
+    uint64_t bytes;      /* bytes of the data (0 for a type this reader does not size) */
+    const void *data;    /* the data in the read-only mapping (NULL when bytes is 0) */
+} b200q_gguf_tensor_info;
+typedef struct b200q_gguf_kv_info {
+    const char *key;
+    uint32_t type;        /* GGUF value type: 0 u8, 1 i8, 2 u16, 3 i16, 4 u32, 5 i32, 6 f32, 7 bool, 8 string,
+                           * 9 array, 10 u64, 11 i64, 12 f64 */
+    uint32_t array_type;  /* arrays: the element type */
+    uint64_t count;       /* arrays: elements; else 1 */
+    const void *value;    /* scalars: the value's bytes; strings: the bytes (str_len of them, not NUL-terminated);
+                           * arrays of scalars: the first element; arrays of strings: the first string's 8-byte length */
+    uint64_t str_len;
+} b200q_gguf_kv_info;
+B200Q_API int b200q_gguf_open(const char *path, b200q_gguf **out, char *err, unsigned err_len);
+B200Q_API void b200q_gguf_close(b200q_gguf *g);
+B200Q_API uint32_t b200q_gguf_version(const b200q_gguf *g);
+B200Q_API uint64_t b200q_gguf_n_tensors(const b200q_gguf *g);
+B200Q_API uint64_t b200q_gguf_n_kv(const b200q_gguf *g);
+B200Q_API int b200q_gguf_tensor(const b200q_gguf *g, uint64_t index, b200q_gguf_tensor_info *out);
+B200Q_API int b200q_gguf_find_tensor(const b200q_gguf *g, const char *name, uint64_t *index);
+B200Q_API int b200q_gguf_kv(const b200q_gguf *g, uint64_t index, b200q_gguf_kv_info *out);
+B200Q_API int b200q_gguf_find_kv(const b200q_gguf *g, const char *key, uint64_t *index);
+/* integer (any integer or bool type) / floating (f32, f64 or an integer) metadata value of `key` */
+B200Q_API int b200q_gguf_get_int(const b200q_gguf *g, const char *key, int64_t *value);
+B200Q_API int b200q_gguf_get_float(const b200q_gguf *g, const char *key, double *value);
+/* b200q_upload_weight_ex of tensor `index` (a 2-D matrix: ne[0] columns, ne[1] rows) straight from the mapping. */
+B200Q_API int b200q_upload_gguf_tensor(b200q_ctx *ctx, const b200q_gguf *g, uint64_t index, unsigned block_cols,
+                                       unsigned flags, uint64_t *w_off);
+/* Q4_0 rows back from ggml's CPU_REPACK block_q4_0x8 layout (rows a multiple of 8, cols of 32), bit for bit the
+ * original GGUF rows (reference: ggml-xrt.cpp:675-710, xrt_gguf). dst: rows x cols / 32 x 18 bytes. */
+B200Q_API int b200q_q4_0x8_to_q4_0(const void *src, unsigned rows, unsigned cols, void *dst);
 
 /* ---- multi-GPU (one process per GPU, NCCL over NVLink) ------------------------------------------------------- */
 #define B200Q_UNIQUE_ID_BYTES 128
