@@ -42,7 +42,7 @@ def UPLOAD_PASS_ROWS(n: int) -> int:
     return int(n) << 8
 
 ERR = {-1: "bad argument", -2: "CUDA failure", -3: "out of memory", -4: "context disabled", -5: "NCCL failure",
-       -6: "call out of order", -7: "bounded wait ran out"}
+       -6: "call out of order", -7: "bounded wait ran out", -8: "runtime verification failed"}
 
 
 class B200QError(RuntimeError):
@@ -149,6 +149,22 @@ PASS_KINDS = {1: "gemv", 2: "elementwise", 3: "gdn", 4: "nop", 5: "ext"}
 _lib = None
 
 
+class VerifyView(ctypes.Structure):
+    """b200q_verify_view: what a runtime-verification checker receives."""
+    _fields_ = [("cmds", ctypes.POINTER(ctypes.c_uint32)), ("n_cmds", ctypes.c_uint), ("status", ctypes.c_int),
+                ("act_before", ctypes.POINTER(ctypes.c_float)), ("act_after", ctypes.POINTER(ctypes.c_float)),
+                ("act_floats", ctypes.c_size_t), ("state_before", ctypes.POINTER(ctypes.c_float)),
+                ("state_after", ctypes.POINTER(ctypes.c_float)), ("state_rows", ctypes.c_size_t),
+                ("kv_before", ctypes.c_void_p), ("kv_after", ctypes.c_void_p), ("kv_bytes", ctypes.c_size_t),
+                ("kv_ctx", ctypes.c_uint)]
+
+
+VERIFY_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(VerifyView), ctypes.c_void_p, ctypes.c_uint)
+MASK_GROUPS, MASK_DEFER_NORM, MASK_GDN_OUT = 1 << 3, 1 << 9, 1 << 15
+MASK_X_IMAGE, MASK_NORM_PARTIALS, MASK_PDL, MASK_ROW_OPS, MASK_ATTN_GATE = 1 << 16, 1 << 17, 1 << 18, 1 << 19, 1 << 20
+ERR_VERIFY = -8
+
+
 def lib() -> ctypes.CDLL:
     """The loaded libb200q.so; raises if it has not been built (there is no fallback path)."""
     global _lib
@@ -214,6 +230,9 @@ def lib() -> ctypes.CDLL:
         "b200q_gguf_get_float": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
         "b200q_upload_gguf_tensor": (I, [P, P, ctypes.c_uint64, U, U, ctypes.POINTER(ctypes.c_uint64)]),
         "b200q_q4_0x8_to_q4_0": (I, [P, U, U, P]),
+        "b200q_set_feature_mask": (I, [P, U32]),
+        "b200q_feature_mask": (U32, [P]),
+        "b200q_set_verify": (I, [P, VERIFY_FN, P, I]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -236,7 +255,8 @@ EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream",
             "b200q_comm_world", "b200q_row_slice", "b200q_layout", "b200q_layout_ex", "b200q_repack_host", "b200q_unpack_row_host",
             "b200q_gguf_open", "b200q_gguf_close", "b200q_gguf_version", "b200q_gguf_n_tensors", "b200q_gguf_n_kv",
             "b200q_gguf_tensor", "b200q_gguf_find_tensor", "b200q_gguf_kv", "b200q_gguf_find_kv", "b200q_gguf_get_int",
-            "b200q_gguf_get_float", "b200q_upload_gguf_tensor", "b200q_q4_0x8_to_q4_0"]
+            "b200q_gguf_get_float", "b200q_upload_gguf_tensor", "b200q_q4_0x8_to_q4_0", "b200q_set_feature_mask",
+            "b200q_feature_mask", "b200q_set_verify"]
 
 
 class _LayoutInfo(ctypes.Structure):
@@ -537,6 +557,36 @@ class Context:
 
     def reset_weights(self):
         self._check(lib().b200q_weights_reset(self.h))
+
+    def set_feature_mask(self, mask: int) -> None:
+        """b200q_set_feature_mask: hide fused forms from the feature probe and switch the executor's fusions off."""
+        self._check(lib().b200q_set_feature_mask(self.h, mask & 0xFFFFFFFF))
+
+    @property
+    def feature_mask(self) -> int:
+        return int(lib().b200q_feature_mask(self.h))
+
+    def set_verify(self, checker, n_calls: int) -> None:
+        """b200q_set_verify: checker(view: VerifyView) -> (ok: bool, message: str) is called after each of the next
+        n_calls lists (b200q_run or graph replays) with host copies of act / state / KV before and after; checker None
+        turns verification off."""
+        if checker is None:
+            self._verify_cb = None
+            self._check(lib().b200q_set_verify(self.h, VERIFY_FN(), None, 0))
+            return
+
+        def cb(_user, view, msg, msg_len):
+            try:
+                ok, text = checker(view.contents)
+            except Exception as e:  # a checker that raises counts as a disagreement
+                ok, text = False, f"checker raised {e!r}"
+            if not ok:
+                data = text.encode()[: max(0, msg_len - 1)] + b"\0"
+                ctypes.memmove(msg, data, len(data))
+            return 0 if ok else 1
+
+        self._verify_cb = VERIFY_FN(cb)  # kept alive as long as the context may call it
+        self._check(lib().b200q_set_verify(self.h, self._verify_cb, None, n_calls))
 
     def write(self, off: int, x) -> None:
         a = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)

@@ -75,6 +75,14 @@ constexpr unsigned kMaxTraceEvents = 4096;
 constexpr unsigned kSyncAttnWord = 256, kSyncArgmaxWord = 512;
 constexpr size_t kAttnPartFloats = size_t(1) << 22;  // ATTN chunk outputs (16 MiB)
 
+// B200Q_FEATURE_MASK bits that switch the executor's fusions off (include/b200q.h): the reference's feature bits
+// of the fused forms this library also fuses internally, then this library's own
+constexpr uint32_t kMaskGroups = 1u << 3, kMaskDeferNorm = 1u << 9, kMaskGdnOut = 1u << 15;
+constexpr uint32_t kMaskImage = 1u << 16, kMaskNsq = 1u << 17, kMaskPdl = 1u << 18, kMaskRowOps = 1u << 19,
+                   kMaskAttnGate = 1u << 20;
+// feature bits a mask never hides: the weight formats and the Q6_K layout (reference ggml-xrt.cpp:1298)
+constexpr uint32_t kFeatureKeep = 0xFFFF0000u | 1u | 2u | 4u | (1u << 13);
+
 }  // namespace
 
 struct b200q_ctx {
@@ -122,6 +130,12 @@ struct b200q_ctx {
     unsigned slot_next = 0;
     PeerWait pending;          // sharded launches whose rows no kernel has waited for yet
     bool pdl = true;
+    bool pdl_env = true;       // B200Q_NO_PDL=1 turns programmatic dependent launch off for the context's life
+    uint32_t feature_mask = 0xFFFFFFFFu;  // B200Q_FEATURE_MASK (b200q_set_feature_mask)
+    // runtime verification of the first verify_left lists against the caller's checker (b200q_set_verify)
+    b200q_verify_fn verify_fn = nullptr;
+    void *verify_user = nullptr;
+    int verify_left = 0;
     unsigned launches = 0;  // kernels launched by the last executed list
     std::mutex mu;
 };
@@ -131,6 +145,7 @@ struct b200q_graph {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     unsigned kernels = 0;
+    std::vector<uint32_t> cmds;  // the list, for runtime verification of its launches
 };
 
 namespace {
@@ -388,10 +403,11 @@ int exec_gemv(b200q_ctx *c, const Member *mem, unsigned nm, unsigned x_off, unsi
             const unsigned fa = a.m[a.unit_member[i]].w.format, fb = pr >= 0 ? a.m[pr].w.format : 0u;
             GemvArgs g = a;
             unsigned gu = 0, gi = 0;
+            const bool one_unit = !(c->feature_mask & kMaskGroups);  // multi-output passes off: a launch per unit
             for (unsigned k = i; k < a.n_units; ++k) {
                 const int pk = a.unit_pair[k];
                 const unsigned ka = a.m[a.unit_member[k]].w.format, kb = pk >= 0 ? a.m[pk].w.format : 0u;
-                if (done[k] || ka != fa || kb != fb) continue;
+                if (done[k] || ka != fa || kb != fb || (one_unit && k != i)) continue;
                 if (pk >= 0) {
                     const MatrixView &gw = a.m[a.unit_member[k]].w, &uw = a.m[pk].w;
                     if (gw.rt != uw.rt || gw.kc != uw.kc || gw.rows != uw.rows)
@@ -570,7 +586,7 @@ int exec_gdn(b200q_ctx *c, const Pass &p, const ImageLink &nsq_link) {
     // the ssm_out GEMV of a WITH_OUT step reads y: the GDN kernel hands it over quantized (Q8_0 / Q8_1 formats)
     ImageLink out_link;
     if (p.gdn_with_out && act_type(p.gdn_out.format) != 2 && p.gdn_out.cols == g.hv * S &&
-        size_t(g.hv) * S * 3 / 2 <= kQImageBytes) {
+        size_t(g.hv) * S * 3 / 2 <= kQImageBytes && (c->feature_mask & kMaskGdnOut)) {
         g.img = c->qimg[0];
         g.img_act = act_type(p.gdn_out.format);
         out_link.in = c->qimg[0];
@@ -762,12 +778,12 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
             nsq_in = nullptr;
             size_t qi = pi + 1;  // the next pass that launches work (a deferred RMSNORM's own pass launches none)
             while (qi < plan.passes.size() && plan.passes[qi].kind == PassKind::Nop && !plan.passes[qi].nd_store) ++qi;
-            if (qi < plan.passes.size() && link_image(c, p, plan.passes[qi], link) >= 0) {
+            if (qi < plan.passes.size() && (c->feature_mask & kMaskImage) && link_image(c, p, plan.passes[qi], link) >= 0) {
                 link.out = c->qimg[img_turn];
                 img_in = c->qimg[img_turn];
                 img_turn ^= 1u;
             }
-            if (qi < plan.passes.size() && link_nsq(c, p, plan.passes[qi], link) >= 0) {
+            if (qi < plan.passes.size() && (c->feature_mask & kMaskNsq) && link_nsq(c, p, plan.passes[qi], link) >= 0) {
                 link.nsq_out = c->nsq[nsq_turn];
                 nsq_in = c->nsq[nsq_turn];
                 nsq_in_n = link.nsq_out_n;
@@ -782,7 +798,7 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
             ImageLink nl;
             size_t qi = pi + 1;
             while (qi < plan.passes.size() && plan.passes[qi].kind == PassKind::Nop && !plan.passes[qi].nd_store) ++qi;
-            if (qi < plan.passes.size() && link_nsq(c, p, plan.passes[qi], nl) >= 0) {
+            if (qi < plan.passes.size() && (c->feature_mask & kMaskNsq) && link_nsq(c, p, plan.passes[qi], nl) >= 0) {
                 nl.nsq_out = c->nsq[nsq_turn];
                 nsq_in = c->nsq[nsq_turn];
                 nsq_in_n = nl.nsq_out_n;
@@ -827,6 +843,9 @@ Limits limits_of(const b200q_ctx *c) {
     L.kv_ctx = c->kv_ctx;
     L.check_weights = true;
     L.weights = &c->weights;
+    L.defer_norms = (c->feature_mask & kMaskDeferNorm) != 0;
+    L.fuse_rowops = (c->feature_mask & kMaskRowOps) != 0;
+    L.fuse_attn_gate = (c->feature_mask & kMaskAttnGate) != 0;
     return L;
 }
 
@@ -928,7 +947,10 @@ int b200q_create(const b200q_config *cfg, b200q_ctx **out) {
     c->nsq[0] = nq;
     c->nsq[1] = nq + kMaxNsqPanels;
     const char *pdl = getenv("B200Q_NO_PDL");
-    c->pdl = !(pdl && pdl[0] == '1');
+    c->pdl_env = !(pdl && pdl[0] == '1');
+    const char *mask = getenv("B200Q_FEATURE_MASK");
+    c->feature_mask = mask && mask[0] ? uint32_t(strtoul(mask, nullptr, 0)) : 0xFFFFFFFFu;
+    c->pdl = c->pdl_env && (c->feature_mask & kMaskPdl);
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return fail(e, "init");
     *out = c;
     return 0;
@@ -1127,9 +1149,10 @@ int b200q_run_async(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
     int rc = check_ctx(c);
     if (rc) return rc;
     std::lock_guard<std::mutex> lock(c->mu);
-    if (n_cmds == 0) {  // feature probe (gemvqc16.h:124-134)
+    if (n_cmds == 0) {  // feature probe (gemvqc16.h:124-134); the mask hides fused forms (ggml-xrt.cpp:1294-1299)
         uint32_t f[3];
         b200q_features(f);
+        f[0] &= c->feature_mask | kFeatureKeep;
         CUDA_TRY(c, cudaMemcpyAsync(c->act, f, sizeof(f), cudaMemcpyHostToDevice, c->stream));
         CUDA_TRY(c, cudaStreamSynchronize(c->stream));
         return 0;
@@ -1142,13 +1165,95 @@ int b200q_run_async(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
     return plan.status;
 }
 
+namespace {
+// Host copies of the device buffers a list reads and writes (runtime verification).
+struct HostSnap {
+    std::vector<float> act, state;
+    std::vector<uint8_t> kv;
+};
+
+bool verifying(const b200q_ctx *c) { return c && !c->disabled && c->verify_fn && c->verify_left > 0; }
+
+int snapshot(b200q_ctx *c, HostSnap &s) {
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    s.act.resize(c->act_floats);
+    CUDA_TRY(c, cudaMemcpy(s.act.data(), c->act, c->act_floats * sizeof(float), cudaMemcpyDeviceToHost));
+    s.state.resize(c->state_rows * 128);
+    if (c->state_rows)
+        CUDA_TRY(c, cudaMemcpy(s.state.data(), c->state, s.state.size() * sizeof(float), cudaMemcpyDeviceToHost));
+    s.kv.resize(c->kv_bytes);
+    if (c->kv_bytes) CUDA_TRY(c, cudaMemcpy(s.kv.data(), c->kv, c->kv_bytes, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// After a verified list ran (and the stream was synchronized): hands the buffers before and after to the caller's
+// checker, which recomputes the list on the host (reference: GGML_XRT_VERIFY_CALLS, ggml-xrt.cpp:1153-1202). A
+// disagreement disables the context, as the reference backend disables itself when a check throws.
+int verify_after(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds, int status, const HostSnap &before) {
+    HostSnap after;
+    int rc = snapshot(c, after);
+    if (rc) return rc;
+    b200q_verify_view v;
+    v.cmds = cmds;
+    v.n_cmds = n_cmds;
+    v.status = status;
+    v.act_before = before.act.data();
+    v.act_after = after.act.data();
+    v.act_floats = c->act_floats;
+    v.state_before = before.state.data();
+    v.state_after = after.state.data();
+    v.state_rows = c->state_rows;
+    v.kv_before = before.kv.data();
+    v.kv_after = after.kv.data();
+    v.kv_bytes = c->kv_bytes;
+    v.kv_ctx = c->kv_ctx;
+    --c->verify_left;
+    char msg[512] = "";
+    if (c->verify_fn(c->verify_user, &v, msg, sizeof(msg)) != 0) {
+        c->disabled = true;
+        return set_err(c, B200Q_ERR_VERIFY, "verify: the list's results differ from the checker's: %s", msg);
+    }
+    return 0;
+}
+}  // namespace
+
+int b200q_set_verify(b200q_ctx *c, b200q_verify_fn fn, void *user, int n_calls) {
+    if (!c) return B200Q_ERR_ARG;
+    std::lock_guard<std::mutex> lock(c->mu);
+    if (n_calls < 0) {
+        const char *v = getenv("B200Q_VERIFY_CALLS");
+        n_calls = v && v[0] ? std::max(0, atoi(v)) : 0;
+    }
+    c->verify_fn = fn;
+    c->verify_user = user;
+    c->verify_left = fn ? n_calls : 0;
+    return 0;
+}
+
+int b200q_set_feature_mask(b200q_ctx *c, uint32_t mask) {
+    if (!c) return B200Q_ERR_ARG;
+    std::lock_guard<std::mutex> lock(c->mu);
+    c->feature_mask = mask;
+    c->pdl = c->pdl_env && (mask & kMaskPdl);
+    return 0;
+}
+
+uint32_t b200q_feature_mask(const b200q_ctx *c) { return c ? c->feature_mask : 0u; }
+
 int b200q_run(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
+    const bool verify = verifying(c) && n_cmds > 0 && cmds;
+    HostSnap before;
+    if (verify) {
+        int rc = check_ctx(c);
+        if (rc || (rc = snapshot(c, before))) return rc;
+    }
     const int status = b200q_run_async(c, cmds, n_cmds);
     if (status < 0) return status;
     int rc = check_ctx(c);
     if (rc) return rc;
     CUDA_TRY(c, cudaStreamSynchronize(c->stream));
     if ((rc = check_device_status(c))) return rc;
+    if (verify && (rc = verify_after(c, cmds, n_cmds, status, before))) return rc;
     return status;
 }
 
@@ -1176,6 +1281,7 @@ int b200q_graph_create(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds, b200
     }
     g->graph = graph;
     g->kernels = c->launches;
+    g->cmds.assign(cmds, cmds + size_t(n_cmds) * B200Q_CMD_WORDS);
     const cudaError_t ie = cudaGraphInstantiate(&g->exec, graph, 0);
     if (ie != cudaSuccess) {
         cudaGraphDestroy(graph);
@@ -1186,12 +1292,28 @@ int b200q_graph_create(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds, b200
     return 0;
 }
 
+namespace {
+// One replay; under runtime verification a synchronous one, checked like b200q_run.
+int launch_one(b200q_ctx *c, b200q_graph *g) {
+    if (!verifying(c)) {
+        CUDA_TRY(c, cudaGraphLaunch(g->exec, c->stream));
+        return 0;
+    }
+    HostSnap before;
+    int rc = snapshot(c, before);
+    if (rc) return rc;
+    CUDA_TRY(c, cudaGraphLaunch(g->exec, c->stream));
+    CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+    if ((rc = check_device_status(c))) return rc;
+    return verify_after(c, g->cmds.data(), unsigned(g->cmds.size() / B200Q_CMD_WORDS), 0, before);
+}
+}  // namespace
+
 int b200q_graph_launch(b200q_ctx *c, b200q_graph *g) {
     int rc = check_ctx(c);
     if (rc) return rc;
     if (!g || g->ctx != c) return B200Q_ERR_STATE;
-    CUDA_TRY(c, cudaGraphLaunch(g->exec, c->stream));
-    return 0;
+    return launch_one(c, g);
 }
 
 int b200q_graph_launch_many(b200q_ctx *c, b200q_graph *const *graphs, unsigned n_graphs, unsigned launches) {
@@ -1200,7 +1322,8 @@ int b200q_graph_launch_many(b200q_ctx *c, b200q_graph *const *graphs, unsigned n
     if (!graphs || n_graphs == 0) return B200Q_ERR_ARG;
     for (unsigned i = 0; i < n_graphs; ++i)
         if (!graphs[i] || graphs[i]->ctx != c) return B200Q_ERR_STATE;
-    for (unsigned i = 0; i < launches; ++i) CUDA_TRY(c, cudaGraphLaunch(graphs[i % n_graphs]->exec, c->stream));
+    for (unsigned i = 0; i < launches; ++i)
+        if ((rc = launch_one(c, graphs[i % n_graphs]))) return rc;
     return 0;
 }
 

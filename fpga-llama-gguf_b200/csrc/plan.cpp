@@ -568,7 +568,7 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
             for (const auto &w : writes)
                 hits = hits || ranges_meet(w.first, w.second, nd.x_off, nd.n) ||
                        ((nd.flags & 2u) == 0 && ranges_meet(w.first, w.second, nd.w_off, nd.n));
-            if (p.kind == PassKind::Gemv && p.from_nd && (nd_dirty || hits)) {
+            if (p.kind == PassKind::Gemv && p.from_nd && (nd_dirty || hits || !lim.defer_norms)) {
                 nd.materialize = true;
                 plan.passes[size_t(nd_pass)].nd_store = true;
                 plan.passes[size_t(nd_pass)].nd = nd;
@@ -586,8 +586,8 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
                 if (q.kind == PassKind::Nop && q.op == 2 && q.nd.cmd == p.nd.cmd && q.nd_store) p.nd.materialize = true;
         }
     }
-    fuse_rowops(plan.passes);
-    fuse_attn_gate(plan.passes);
+    if (lim.fuse_rowops) fuse_rowops(plan.passes);
+    if (lim.fuse_attn_gate) fuse_attn_gate(plan.passes);
     return plan;
 }
 

@@ -40,6 +40,10 @@ struct Limits {
     unsigned kv_ctx = 0;
     bool check_weights = false;                // planning without a context: no weight table
     const std::vector<WeightInfo> *weights = nullptr;
+    // executor fusions that a feature mask can switch off (results are the same either way): deferred norms
+    // computed in the consumers' prologue (off: stored at the RMSNORM command), runs of RMSNORM / ROPE in one launch,
+    // the attention gate applied in the attention merge
+    bool defer_norms = true, fuse_rowops = true, fuse_attn_gate = true;
 };
 
 constexpr unsigned kMaxRowJobs = 8;  // jobs of one RowOps launch

@@ -119,6 +119,7 @@ extern "C" {
 #define B200Q_ERR_COMM (-5)     /* NCCL failure or missing communicator */
 #define B200Q_ERR_STATE (-6)    /* call out of order (e.g. graph launch on another context) */
 #define B200Q_ERR_TIMEOUT (-7)  /* a kernel's bounded wait ran out (reported by b200q_run / b200q_synchronize) */
+#define B200Q_ERR_VERIFY (-8)   /* runtime verification: the caller's checker disagreed; the context is disabled */
 
 typedef struct b200q_ctx b200q_ctx;
 typedef struct b200q_graph b200q_graph;
@@ -207,6 +208,55 @@ B200Q_API int b200q_graph_launch_many(b200q_ctx *ctx, b200q_graph *const *graphs
                                       unsigned launches);
 /* kernels one replay of the graph launches */
 B200Q_API unsigned b200q_graph_kernel_count(const b200q_graph *graph);
+
+/* ---- diagnostics: feature mask and runtime verification ------------------------------------------------------
+ * Feature mask (reference: GGML_XRT_FEATURE_MASK, ggml-xrt.cpp:1294-1299). The environment variable
+ * B200Q_FEATURE_MASK=<bits> (read at b200q_create) or b200q_set_feature_mask sets it; all bits set by default.
+ *   bits 0..15: the reference feature word. A cleared bit hides that fused form from the feature probe (a zero-command
+ *     b200q_run), so a list builder emits the plain command sequence instead; the weight-format and layout bits
+ *     (0, 1, 2, 13) always stay. Where this library also fuses internally, the cleared bit turns that off too:
+ *     bit 3 multi-output passes (each GEMV or SwiGLU pair of a group then runs as its own launch), bit 9 deferred
+ *     RMSNORM in the GEMV prologue (the norm row is then stored at its command), bit 15 the DeltaNet step handing
+ *     its ssm_out GEMV the quantized y.
+ *   bits 16..20: this library's own fusions: 16 a GEMV pass handing the next pass its quantized x, 17 per-panel
+ *     sums of squares handed to the next deferred norm, 18 programmatic dependent launch, 19 runs of RMSNORM / ROPE
+ *     in one launch, 20 the attention gate applied in the attention merge.
+ * Every fused form gives the same values as its plain form, so results do not depend on the mask (bit for bit, but
+ * for the deferred norm's FP64 sum of squares, which is added in a different fixed order when stored; both round to
+ * the same FP32 scale unless the exact sum lies within ~1e-13, relative, of an FP32 rounding boundary). The mask is
+ * for A/B measurements and for checking exactly that. Graphs keep the mask they were captured with. */
+#define B200Q_MASK_GROUPS (1u << 3)
+#define B200Q_MASK_DEFER_NORM (1u << 9)
+#define B200Q_MASK_GDN_OUT (1u << 15)
+#define B200Q_MASK_X_IMAGE (1u << 16)
+#define B200Q_MASK_NORM_PARTIALS (1u << 17)
+#define B200Q_MASK_PDL (1u << 18)
+#define B200Q_MASK_ROW_OPS (1u << 19)
+#define B200Q_MASK_ATTN_GATE (1u << 20)
+B200Q_API int b200q_set_feature_mask(b200q_ctx *ctx, uint32_t mask);
+B200Q_API uint32_t b200q_feature_mask(const b200q_ctx *ctx);
+
+/* Runtime verification (reference: GGML_XRT_VERIFY_CALLS=<n>, ggml-xrt.cpp:62-66, 1153-1202): the next n_calls lists
+ * run by b200q_run or replayed by b200q_graph_launch(_many) run synchronously, with act, the state rows and the KV
+ * cache copied to host memory before and after; the checker gets both copies and the list and returns 0 when the
+ * results agree with its own computation of the list (the library links no checker of its own; a caller supplies
+ * the CPU reference). A non-zero return makes the call return B200Q_ERR_VERIFY with the checker's message and
+ * disables the context, as the reference backend disables itself. n_calls < 0: the count is taken from the
+ * environment variable B200Q_VERIFY_CALLS (0 when unset); fn NULL turns verification off. */
+typedef struct b200q_verify_view {
+    const uint32_t *cmds;
+    unsigned n_cmds;
+    int status;                 /* the list's status (0, or the 1-based index of its first invalid command) */
+    const float *act_before, *act_after;
+    size_t act_floats;
+    const float *state_before, *state_after;
+    size_t state_rows;
+    const void *kv_before, *kv_after;
+    size_t kv_bytes;
+    unsigned kv_ctx;
+} b200q_verify_view;
+typedef int (*b200q_verify_fn)(void *user, const b200q_verify_view *view, char *msg, unsigned msg_len);
+B200Q_API int b200q_set_verify(b200q_ctx *ctx, b200q_verify_fn fn, void *user, int n_calls);
 
 /* ---- host-only planning (no GPU needed) ---------------------------------------------------------------------- */
 typedef struct b200q_pass_info {
