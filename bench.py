@@ -42,6 +42,7 @@ sys.path.insert(0, ROOT)
 H, F = 2560, 9216
 EPS = 1e-6
 XIN, GAIN, XN, FF, OUT = 0, H, 2 * H, 4 * H, 4 * H + F
+PART = 5 * H + F  # tensor parallel: this rank's partial output of the down projection
 RES = (XIN, OUT)  # the residual stream alternates between these two rows, layer by layer
 ACT_FLOATS = 1 << 16
 L2_BYTES = 126 << 20
@@ -76,21 +77,37 @@ def gen_block(synth, seed: int):
     return synth.q8_0(r, F, H), synth.q8_0(r, F, H), synth.q8_0(r, H, F)
 
 
-def block_list(b2, hg, hu, hd, xin=XIN, out=OUT):
-    return b2.cmd_list(
-        b2.rmsnorm(H, xin, GAIN, XN, EPS, flags=b2.NORM_DEFER),
-        b2.gemv(b2.Q8_0, F, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(b2.Q8_0, F, H, hu, XN, FF),
-        b2.gemv(b2.Q8_0, H, F, hd, FF, out, b2.GEMV_ADD), b2.add(H, out, xin, out))
+def block_list(b2, hg, hu, hd, xin=XIN, out=OUT, world=1, rank=0):
+    """One FFN block. Tensor parallel (world > 1): this rank's F / world rows of gate and up and the same columns of
+    down give a partial output; rank 0 adds the residual, one ALLREDUCE sums the partials into `out`."""
+    f = F // world
+    head = [b2.rmsnorm(H, xin, GAIN, XN, EPS, flags=b2.NORM_DEFER),
+            b2.gemv(b2.Q8_0, f, H, hg, XN, FF, b2.GEMV_SWIGLU), b2.gemv(b2.Q8_0, f, H, hu, XN, FF)]
+    if world == 1:
+        return b2.cmd_list(*head, b2.gemv(b2.Q8_0, H, F, hd, FF, out, b2.GEMV_ADD), b2.add(H, out, xin, out))
+    down = ([b2.gemv(b2.Q8_0, H, f, hd, FF, PART, b2.GEMV_ADD), b2.add(H, PART, xin, PART)] if rank == 0
+            else [b2.gemv(b2.Q8_0, H, f, hd, FF, PART)])
+    return b2.cmd_list(*head, *down, b2.allreduce(H, PART, out))
 
 
-def stack_list(b2, layers, upto=None):
+def stack_list(b2, layers, upto=None, world=1, rank=0):
     """Command list of the layer stack (layer c: residual RES[c % 2] -> RES[(c + 1) % 2]); `upto` keeps only the
     first `upto` commands of each block (8 words each)."""
     parts = []
     for c, (hg, hu, hd) in enumerate(layers):
-        cl = block_list(b2, hg, hu, hd, RES[c % 2], RES[(c + 1) % 2])
+        cl = block_list(b2, hg, hu, hd, RES[c % 2], RES[(c + 1) % 2], world, rank)
         parts.append(cl[: upto * 8] if upto else cl)
     return np.concatenate(parts)
+
+
+def block_slices(mats, world: int, rank: int):
+    """This rank's gate / up rows and down columns of the block's matrices (GGUF Q8_0 bytes)."""
+    if world == 1:
+        return [(mats[0], F, H), (mats[1], F, H), (mats[2], H, F)]
+    f = F // world
+    rows = slice(rank * f, (rank + 1) * f)
+    down = np.ascontiguousarray(mats[2].reshape(H, F // 32, 34)[:, rank * f // 32:(rank + 1) * f // 32])
+    return [(mats[0].reshape(F, -1)[rows], f, H), (mats[1].reshape(F, -1)[rows], f, H), (down.reshape(H, -1), H, f)]
 
 
 class ClockSampler:
@@ -407,7 +424,7 @@ def kquant_bench(b2, torch, synth, dev: int, world: int, max_over_ranks, barrier
 
 
 def decode_bench(b2, torch, dist, dev: int, world: int, rank: int, shape, label: str, tokens: int, warm: int,
-                 max_over_ranks, barrier):
+                 max_over_ranks, barrier, mp: str = "tp"):
     """Batch-1 greedy decode of the synthetic hybrid model: `tokens` tokens at positions prefill ..
     prefill + tokens - 1, each one stream-ordered record write (position + RoPE row, page-locked), the replay of the
     token's lists (one CUDA Graph each) and a stream-ordered read of the argmax token; the device chains the tokens
@@ -415,12 +432,13 @@ def decode_bench(b2, torch, dist, dev: int, world: int, rank: int, shape, label:
     the host waiting for every token (a host-side sampler's pattern), wall clock."""
     import fpga_llama_gguf_b200.decode as D
     t_setup = time.perf_counter()
-    m = D.HybridDecoder(shape)
+    tp = world > 1 and mp == "tp"
+    m = D.HybridDecoder(shape, world=world, rank=rank) if tp else D.HybridDecoder(shape)
     ctx = b2.Context(device=dev, **m.context_config(world))
     if world > 1:
         obj = [b2.Context.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        ctx.comm_init(world, rank, obj[0])
+        ctx.comm_init(world, rank, obj[0], b2.COMM_EXPLICIT if tp else 0)
     m.load(ctx)
     graphs = [ctx.graph(cl) for cl in m.token_lists()]
     setup_s = time.perf_counter() - t_setup
@@ -484,6 +502,9 @@ def main():
     ap.add_argument("--decode-tokens", type=int, default=128)
     ap.add_argument("--no-kquant", action="store_true", help="skip the configs[2] K-quant GEMV measurement")
     ap.add_argument("--no-extras", action="store_true", help="skip the configs[0] / configs[3] objects")
+    ap.add_argument("--mp", default="tp", choices=["tp", "rows"],
+                    help="multi-GPU split: tp = each rank its own heads / FFN rows / column slices with one ALLREDUCE "
+                    "per projection (default); rows = every matrix row-sharded by the library, outputs all-gathered")
     ap.add_argument("--decode-only", action="store_true", help="run only the decode measurement (for profiling "
                     "runs); the line then carries the decode object and no GEMV metric")
     args = ap.parse_args()
@@ -493,7 +514,9 @@ def main():
     config = {"workload": "configs[1] fused FFN block: deferred RMSNorm -> Q8_0 gate+up (SwiGLU) -> Q8_0 down "
                           "(+residual), hidden 2560, FFN 9216, stacked as the layers of one decode step",
               "global_batch": 1, "seq_len": 1,
-              "parallelism": f"row-sharded x{world}" if world > 1 else "1 GPU"}
+              "parallelism": ("1 GPU" if world == 1 else
+                              f"tensor parallel x{world} (FFN rows / down columns, one ALLREDUCE per block)"
+                              if args.mp == "tp" else f"row-sharded x{world} (outputs all-gathered)")}
 
     per_layer = weight_bytes() // world
     n_layers = min(40, max(2, int(np.ceil(3 * L2_BYTES / max(per_layer, 1)))))
@@ -548,7 +571,7 @@ def main():
         for key in [k for k in args.decode.split(",") if k]:
             shape, label = shapes[key]
             out[key] = decode_bench(b2, torch, dist, dev, world, rank, shape, label, args.decode_tokens,
-                                    max(3, min(args.warmup, 16)), max_over_ranks, barrier)
+                                    max(3, min(args.warmup, 16)), max_over_ranks, barrier, args.mp)
         return out
 
     if args.decode_only:
@@ -562,15 +585,16 @@ def main():
 
     # n_layers: enough layers that one step reads more than 3x the L2
     ctx = b2.Context(device=dev, weight_bytes=n_layers * (per_layer + (8 << 20)) + (64 << 20), act_floats=ACT_FLOATS)
+    tp = world > 1 and args.mp == "tp"
+    tw, tr = (world, rank) if tp else (1, 0)  # the lists' tensor-parallel split (rows mode: one-rank lists)
     if world > 1:
         obj = [b2.Context.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        ctx.comm_init(world, rank, obj[0])
+        ctx.comm_init(world, rank, obj[0], b2.COMM_EXPLICIT if tp else 0)
     mats = gen_block(synth, 0)
-    layers = [tuple(ctx.upload(m, rows, cols, b2.Q8_0) for m, rows, cols in ((mats[0], F, H), (mats[1], F, H),
-                                                                           (mats[2], H, F)))
+    layers = [tuple(ctx.upload(m, rows, cols, b2.Q8_0) for m, rows, cols in block_slices(mats, tw, tr))
               for _ in range(n_layers)]
-    stack = ctx.graph(stack_list(b2, layers))
+    stack = ctx.graph(stack_list(b2, layers, world=tw, rank=tr))
     r = synth.rng(1, 99)
     x = synth.activation(r, H)
     gain = r.normal(1, 0.1, H).astype(np.float32)
@@ -599,7 +623,7 @@ def main():
 
     # roofline of the dominant kernel (the gate+up pass): the stack's gate+up passes alone, one graph, CUDA events
     peak, peak_kind = measured_peak()
-    ru = ctx.graph(stack_list(b2, layers, upto=3))  # per layer: deferred norm + gate/up pair = one GEMV kernel
+    ru = ctx.graph(stack_list(b2, layers, upto=3, world=tw, rank=tr))  # per layer: norm + gate/up = one GEMV kernel
     ctx.launch_many([ru], 5)
     ctx.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -609,7 +633,7 @@ def main():
     e2.record(stream)
     e2.synchronize()
     ru_ms = max_over_ranks(s2.elapsed_time(e2) / (n_ru * n_layers))
-    ru_bytes = 2 * F * (H // 32) * 34 + 4 * (H + H)
+    ru_bytes = 2 * F * (H // 32) * 34 // world + 4 * (H + H)  # one rank's launch: its share of the rows
     achieved = ru_bytes / (ru_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": None,
@@ -672,7 +696,7 @@ def main():
         line = {"metric": "GEMV HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": DATA, "config": config,
-                "frac_of_peak": round(value / peak, 4), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "frac_of_peak": round(value / (peak * world), 4), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks, "q4_0": q40, "kquant": kquant, "gdn_step": gdn,
                 "decode": decode}
         print(json.dumps(line), flush=True)

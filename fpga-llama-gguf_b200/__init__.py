@@ -25,14 +25,15 @@ CMD_WORDS = 8
 MAX_CMDS = 128
 OP_GEMV, OP_RMSNORM, OP_ADD, OP_SILU_MUL, OP_MUL, OP_UNARY, OP_GDN, OP_CONV = 1, 2, 3, 4, 5, 6, 7, 8
 OP_STATE_LOAD, OP_ROPE, OP_TRACE = 9, 10, 11
-OP_ATTN, OP_ARGMAX, OP_GET_ROW = 12, 13, 14  # extensions of this library
+OP_ATTN, OP_ARGMAX, OP_GET_ROW, OP_ALLREDUCE, OP_ALLGATHER = 12, 13, 14, 15, 16  # extensions of this library
 GEMV_SWIGLU, GEMV_CONV, GEMV_ADD = 0x100, 0x200, 0x400
 GDN_WITH_GEMV, GDN_L2_QK, GDN_GATED, GDN_GATES, GDN_WITH_OUT = 1, 2, 4, 8, 16
 NORM_L2, NORM_NO_WEIGHT, NORM_DEFER = 1, 2, 4
 UNARY_SILU, UNARY_SIGMOID, UNARY_SOFTPLUS, UNARY_COPY = 1, 2, 3, 4
 SILU_MUL_SIGMOID = 1
 Q4_0, Q4_1, Q8_0, Q5_K, Q6_K = 2, 3, 8, 13, 14
-FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53000F)
+FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53001F)
+COMM_EXPLICIT = 1
 UPLOAD_REPLICATE = 1
 UPLOAD_SRC_Q4_0X8 = 2
 
@@ -133,6 +134,16 @@ def get_row(fmt: int, cols: int, w_off: int, idx_off: int, y_off: int) -> np.nda
     return cmd(OP_GET_ROW, fmt, cols, w_off & 0xFFFFFFFF, w_off >> 32, idx_off, y_off)
 
 
+def allreduce(n: int, x_off: int, y_off: int) -> np.ndarray:
+    """ALLREDUCE extension: y = the sum over the communicator's ranks of their x (one rank: y = x)."""
+    return cmd(OP_ALLREDUCE, n, x_off, y_off)
+
+
+def allgather(n: int, x_off: int, y_off: int) -> np.ndarray:
+    """ALLGATHER extension: y[r n .. r n + n) = x of rank r (one rank: y = x)."""
+    return cmd(OP_ALLGATHER, n, x_off, y_off)
+
+
 # ---- library ---------------------------------------------------------------------------------------------------
 class _Config(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("weight_bytes", ctypes.c_size_t), ("act_floats", ctypes.c_size_t),
@@ -211,6 +222,7 @@ def lib() -> ctypes.CDLL:
         "b200q_quantize_noalloc": (I, [I, P, U, U, P, ctypes.c_float, U, P, P, P, P, ctypes.c_char_p, U]),
         "b200q_comm_unique_id": (I, [P]),
         "b200q_comm_init": (I, [P, I, I, P]),
+        "b200q_comm_init_ex": (I, [P, I, I, P, U]),
         "b200q_comm_world": (I, [P]),
         "b200q_row_slice": (I, [U, U, I, I, ctypes.POINTER(U), ctypes.POINTER(U)]),
         "b200q_layout": (I, [U, U, U, U, P]),
@@ -256,7 +268,7 @@ EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream",
             "b200q_gguf_open", "b200q_gguf_close", "b200q_gguf_version", "b200q_gguf_n_tensors", "b200q_gguf_n_kv",
             "b200q_gguf_tensor", "b200q_gguf_find_tensor", "b200q_gguf_kv", "b200q_gguf_find_kv", "b200q_gguf_get_int",
             "b200q_gguf_get_float", "b200q_upload_gguf_tensor", "b200q_q4_0x8_to_q4_0", "b200q_set_feature_mask",
-            "b200q_feature_mask", "b200q_set_verify"]
+            "b200q_feature_mask", "b200q_set_verify", "b200q_comm_init_ex"]
 
 
 class _LayoutInfo(ctypes.Structure):
@@ -677,6 +689,8 @@ class Context:
             raise B200QError(rc, "ncclGetUniqueId failed")
         return bytes(buf)
 
-    def comm_init(self, world: int, rank: int, uid: bytes) -> None:
+    def comm_init(self, world: int, rank: int, uid: bytes, flags: int = 0) -> None:
+        """b200q_comm_init_ex: flags 0 row-shards uploads and gathers outputs by itself; COMM_EXPLICIT takes each
+        rank's own lists (ALLREDUCE / ALLGATHER commands)."""
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
-        self._check(lib().b200q_comm_init(self.h, world, rank, buf))
+        self._check(lib().b200q_comm_init_ex(self.h, world, rank, buf, flags))

@@ -37,12 +37,13 @@ struct NcclApi {
     nccl_result (*get_unique_id)(NcclUniqueId *) = nullptr;
     nccl_result (*comm_init_rank)(nccl_comm *, int, NcclUniqueId, int) = nullptr;
     nccl_result (*all_gather)(const void *, void *, size_t, int, nccl_comm, cudaStream_t) = nullptr;
+    nccl_result (*all_reduce)(const void *, void *, size_t, int, int, nccl_comm, cudaStream_t) = nullptr;
     nccl_result (*comm_destroy)(nccl_comm) = nullptr;
     const char *(*get_error_string)(nccl_result) = nullptr;
 };
 NcclApi g_nccl;
 std::mutex g_nccl_mu;
-constexpr int kNcclFloat32 = 7;
+constexpr int kNcclFloat32 = 7, kNcclSum = 0;
 
 bool load_nccl(std::string &err) {
     std::lock_guard<std::mutex> lock(g_nccl_mu);
@@ -59,9 +60,11 @@ bool load_nccl(std::string &err) {
     g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(g_nccl.h, "ncclGetUniqueId"));
     g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(g_nccl.h, "ncclCommInitRank"));
     g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(g_nccl.h, "ncclAllGather"));
+    g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(g_nccl.h, "ncclAllReduce"));
     g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(g_nccl.h, "ncclCommDestroy"));
     g_nccl.get_error_string = reinterpret_cast<decltype(g_nccl.get_error_string)>(dlsym(g_nccl.h, "ncclGetErrorString"));
-    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.all_gather || !g_nccl.comm_destroy) {
+    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.all_gather || !g_nccl.all_reduce ||
+        !g_nccl.comm_destroy) {
         err = "libnccl.so.2 lacks an entry point";
         return false;
     }
@@ -129,6 +132,14 @@ struct b200q_ctx {
     unsigned *sync = nullptr;  // kSyncWords: ready and data words per (slot, rank), CTA and launch counts per slot
     unsigned slot_next = 0;
     PeerWait pending;          // sharded launches whose rows no kernel has waited for yet
+    // explicit (tensor-parallel) lists: the caller's own slices, exchanges only by ALLREDUCE / ALLGATHER commands;
+    // with coll_peer, ALLREDUCE runs as the peer kernel (coll.cu) on these buffers, one slot per ALLREDUCE of a list
+    bool explicit_comm = false, coll_peer = false;
+    float *coll_recv = nullptr;
+    unsigned *coll_flags = nullptr;
+    float *peer_coll_recv[kMaxPeers] = {};
+    unsigned *peer_coll_flags[kMaxPeers] = {};
+    unsigned coll_slot_next = 0;
     bool pdl = true;
     bool pdl_env = true;       // B200Q_NO_PDL=1 turns programmatic dependent launch off for the context's life
     uint32_t feature_mask = 0xFFFFFFFFu;  // B200Q_FEATURE_MASK (b200q_set_feature_mask)
@@ -665,6 +676,41 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         const float *idx = snap_if(c, A + cmd[5], 1, wr, nullptr, rc);
         if (rc) return rc;
         CUDA_TRY(c, launch_get_row(view_of(c, *w), cmd[2], idx, y, c->dstatus, take_wait(c), c->stream, c->pdl));
+    } else if (p.op == 15 || p.op == 16) {
+        const size_t n = cmd[1];
+        const float *x = A + cmd[2];
+        float *y = A + cmd[3];
+        if (c->world <= 1) {  // one rank: y = x
+            if (x != y) CUDA_TRY(c, cudaMemcpyAsync(y, x, n * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+            return 0;
+        }
+        if ((rc = flush_wait(c))) return rc;
+        if (p.op == 15 && c->coll_peer && n <= kCollMaxN) {
+            if (c->coll_slot_next >= kCollSlots)
+                return set_err(c, B200Q_ERR_ARG, "more than %u peer ALLREDUCE commands in a list", kCollSlots);
+            const unsigned slot = c->coll_slot_next++;
+            CollArgs a;
+            a.x = x;
+            a.y = y;
+            a.n = unsigned(n);
+            a.world = unsigned(c->world);
+            a.rank = unsigned(c->rank);
+            const size_t rs = size_t(2) * c->world * kCollMaxN, fs = size_t(c->world) * kCollMaxCtas;
+            for (int r = 0; r < c->world; ++r) {
+                a.recv[r] = (r == c->rank ? c->coll_recv : c->peer_coll_recv[r]) + slot * rs;
+                a.flags[r] = (r == c->rank ? c->coll_flags : c->peer_coll_flags[r]) + slot * fs;
+            }
+            a.flag_local = a.flags[c->rank];
+            a.err = c->dstatus + 1;
+            CUDA_TRY(c, launch_allreduce_peer(a, c->stream, c->pdl));
+        } else {
+            const int r = p.op == 15 ? g_nccl.all_reduce(x, y, n, kNcclFloat32, kNcclSum, c->comm, c->stream)
+                                     : g_nccl.all_gather(x, y, n, kNcclFloat32, c->comm, c->stream);
+            if (r != 0)
+                return set_err(c, B200Q_ERR_COMM, "%s: %s", p.op == 15 ? "ncclAllReduce" : "ncclAllGather",
+                               g_nccl.get_error_string ? g_nccl.get_error_string(r) : "?");
+            return 0;  // not one of this library's kernels
+        }
     }
     ++c->launches;
     return 0;
@@ -747,6 +793,7 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
     c->launches = 0;
     c->slot_next = 0;
+    c->coll_slot_next = 0;
     c->pending.n = 0;
     c->n_events = 0;
     c->host_tags.clear();
@@ -846,6 +893,7 @@ Limits limits_of(const b200q_ctx *c) {
     L.defer_norms = (c->feature_mask & kMaskDeferNorm) != 0;
     L.fuse_rowops = (c->feature_mask & kMaskRowOps) != 0;
     L.fuse_attn_gate = (c->feature_mask & kMaskAttnGate) != 0;
+    L.world = unsigned(c->world);
     return L;
 }
 
@@ -963,8 +1011,12 @@ void b200q_destroy(b200q_ctx *c) {
     for (unsigned p = 0; p < kMaxPeers; ++p) {
         if (c->peer_act[p]) cudaIpcCloseMemHandle(c->peer_act[p]);
         if (c->peer_sync[p]) cudaIpcCloseMemHandle(c->peer_sync[p]);
+        if (c->peer_coll_recv[p]) cudaIpcCloseMemHandle(c->peer_coll_recv[p]);
+        if (c->peer_coll_flags[p]) cudaIpcCloseMemHandle(c->peer_coll_flags[p]);
     }
     cudaFree(c->sync);
+    cudaFree(c->coll_recv);
+    cudaFree(c->coll_flags);
     if (c->comm && g_nccl.comm_destroy) g_nccl.comm_destroy(c->comm);
     cudaFree(c->warena);
     cudaFree(c->qimg[0]);
@@ -1024,7 +1076,7 @@ int b200q_upload_weight_ex(b200q_ctx *c, const void *gguf, unsigned rows, unsign
         (block_cols != 0 && block_cols != 256))
         return set_err(c, B200Q_ERR_ARG, "upload: bad shape or format");
     unsigned r0 = 0, r1 = rows;
-    b200q_row_slice(rows, flags, c->world, c->rank, &r0, &r1);
+    if (!c->explicit_comm) b200q_row_slice(rows, flags, c->world, c->rank, &r0, &r1);
     // the pass hint, scaled to this rank's share when the matrix is sharded
     const unsigned pass_rows = unsigned(uint64_t(flags >> 8) * (r1 - r0) / rows);
     const DeviceLayout L = device_layout(r1 - r0, cols, format, unsigned(c->sms), pass_rows);
@@ -1490,6 +1542,43 @@ int setup_peers(b200q_ctx *c) {
     c->peer_ok = true;
     return 0;
 }
+
+// Receive buffers and flag words of the peer ALLREDUCE (coll.cu), mapped into every peer (CUDA IPC; the handles
+// travel through one NCCL all-gather).
+int setup_coll_peers(b200q_ctx *c) {
+    const size_t recv_bytes = size_t(kCollSlots) * 2 * c->world * kCollMaxN * sizeof(float);
+    const size_t flag_bytes = size_t(kCollSlots) * c->world * kCollMaxCtas * sizeof(unsigned);
+    CUDA_TRY(c, cudaMalloc(&c->coll_recv, recv_bytes));
+    CUDA_TRY(c, cudaMalloc(&c->coll_flags, flag_bytes));
+    CUDA_TRY(c, cudaMemset(c->coll_recv, 0, recv_bytes));
+    CUDA_TRY(c, cudaMemset(c->coll_flags, 0, flag_bytes));
+    cudaIpcMemHandle_t mine[2];
+    CUDA_TRY(c, cudaIpcGetMemHandle(&mine[0], c->coll_recv));
+    CUDA_TRY(c, cudaIpcGetMemHandle(&mine[1], c->coll_flags));
+    const size_t n = sizeof(mine) / (sizeof(float));
+    float *dev = nullptr;
+    CUDA_TRY(c, cudaMalloc(&dev, sizeof(mine) * (size_t(c->world) + 1)));
+    CUDA_TRY(c, cudaMemcpy(dev, mine, sizeof(mine), cudaMemcpyHostToDevice));
+    const int r = g_nccl.all_gather(dev, dev + n, n, kNcclFloat32, c->comm, c->stream);
+    std::vector<cudaIpcMemHandle_t> all(2 * size_t(c->world));
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), dev + n, sizeof(mine) * size_t(c->world), cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (r != 0) return set_err(c, B200Q_ERR_COMM, "ncclAllGather of the IPC handles: %d", r);
+    if (e != cudaSuccess) return set_err(c, B200Q_ERR_CUDA, "IPC handle exchange: %s", cudaGetErrorString(e));
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        void *pr = nullptr, *pf = nullptr;
+        CUDA_TRY(c, cudaIpcOpenMemHandle(&pr, all[2 * size_t(p)], cudaIpcMemLazyEnablePeerAccess));
+        CUDA_TRY(c, cudaIpcOpenMemHandle(&pf, all[2 * size_t(p) + 1], cudaIpcMemLazyEnablePeerAccess));
+        c->peer_coll_recv[p] = static_cast<float *>(pr);
+        c->peer_coll_flags[p] = static_cast<unsigned *>(pf);
+    }
+    // every rank's buffers are mapped before any rank pushes
+    CUDA_TRY(c, cudaDeviceSynchronize());
+    c->coll_peer = true;
+    return 0;
+}
 }  // namespace
 
 int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]) {
@@ -1502,6 +1591,10 @@ int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]) {
 }
 
 int b200q_comm_init(b200q_ctx *c, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]) {
+    return b200q_comm_init_ex(c, world, rank, id, 0);
+}
+
+int b200q_comm_init_ex(b200q_ctx *c, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES], unsigned flags) {
     int rc = check_ctx(c);
     if (rc) return rc;
     if (world < 1 || rank < 0 || rank >= world || !id) return B200Q_ERR_ARG;
@@ -1515,10 +1608,14 @@ int b200q_comm_init(b200q_ctx *c, int world, int rank, const uint8_t id[B200Q_UN
     if (r != 0) return set_err(c, B200Q_ERR_COMM, "ncclCommInitRank: %d", r);
     c->world = world;
     c->rank = rank;
+    c->explicit_comm = (flags & B200Q_COMM_EXPLICIT) != 0;
     // outputs exchanged by peer stores (B200Q_PEER=1) or by an NCCL all-gather per sharded member (default: at the
-    // sizes measured so far the peer path's per-pass synchronisation costs more than the all-gather)
+    // sizes measured so far the peer path's per-pass synchronisation costs more than the all-gather); explicit lists:
+    // ALLREDUCE by the peer kernel (B200Q_PEER=1) or NCCL
     const char *pe = getenv("B200Q_PEER");
-    if (world <= int(kMaxPeers) && pe && pe[0] == '1') return setup_peers(c);
+    const bool peer = world <= int(kMaxPeers) && pe && pe[0] == '1';
+    if (c->explicit_comm) return peer ? setup_coll_peers(c) : 0;
+    if (peer) return setup_peers(c);
     return 0;
 }
 

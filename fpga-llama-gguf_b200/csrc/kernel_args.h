@@ -60,6 +60,20 @@ struct PeerWait {
     unsigned *err = nullptr;
 };
 
+// ALLREDUCE of explicit lists over NVLink peer memory (coll.cu): one slot per ALLREDUCE of a list; per slot and rank
+// a receive buffer [2 parities][world][kCollMaxN] floats and flag words [world][kCollMaxCtas]; a CTA per chunk.
+constexpr unsigned kCollMaxN = 4096, kCollChunk = 512, kCollMaxCtas = kCollMaxN / kCollChunk, kCollSlots = 64;
+struct CollArgs {
+    const float *x = nullptr;
+    float *y = nullptr;
+    unsigned n = 0;                      // floats, a multiple of 16, at most kCollMaxN
+    float *recv[kMaxPeers] = {};         // per rank: that rank's receive buffer of the slot (this rank's own included)
+    unsigned *flags[kMaxPeers] = {};     // per rank: that rank's flag words of the slot
+    unsigned *flag_local = nullptr;      // this rank's flag words of the slot (flags[rank])
+    unsigned world = 1, rank = 0;
+    unsigned *err = nullptr;             // set when a bounded wait runs out
+};
+
 constexpr unsigned kMaxUnits = 4;
 // bytes of a quantized x image of up to 16384 values (quants + meta words)
 constexpr unsigned kQImageBytes = 16384 + 16384 / 32 * 16;

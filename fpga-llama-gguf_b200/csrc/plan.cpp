@@ -133,6 +133,8 @@ void pass_writes(const Pass &p, std::vector<std::pair<size_t, size_t>> &w) {
         if (p.op == 12) w.push_back({c[5], size_t(c[1] & 0xffu) * ((c[1] >> 16) * 16u)});
         else if (p.op == 13) w.push_back({c[3], 2});
         else if (p.op == 14) w.push_back({c[6], c[2]});
+        else if (p.op == 15) w.push_back({c[3], c[1]});
+        else if (p.op == 16) w.push_back({c[3], size_t(c[1]) * kMaxRanks});
         break;
     default: break;
     }
@@ -550,6 +552,19 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
             }
             if (!ok) {
                 reject(c, "invalid GET_ROW");
+                break;
+            }
+            p.kind = PassKind::Ext;
+        } else if (op == 15 || op == 16) {
+            // ---- ALLREDUCE / ALLGATHER extensions: y = sum of the ranks' x / y = the ranks' x side by side
+            const size_t n = cmd[1], yn = op == 15 ? n : n * lim.world;
+            const size_t x = cmd[2], y = cmd[3];
+            bool ok = n != 0 && n % 16 == 0 && x % 16 == 0 && y % 16 == 0 && (cmd[4] | cmd[5] | cmd[6] | cmd[7]) == 0 &&
+                      C.act(x, n) && C.act(y, yn);
+            if (ok && op == 15) ok = x == y || !ranges_meet(x, n, y, n);
+            if (ok && op == 16) ok = !ranges_meet(x, n, y, yn) || (x >= y && (x - y) % n == 0 && x + n <= y + yn);
+            if (!ok) {
+                reject(c, op == 15 ? "invalid ALLREDUCE" : "invalid ALLGATHER");
                 break;
             }
             p.kind = PassKind::Ext;

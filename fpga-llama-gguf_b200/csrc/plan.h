@@ -20,6 +20,7 @@ constexpr unsigned kMaxRows = 65536, kMaxCols = 16384, kPairRows = 16384, kAddRo
 constexpr unsigned kBufWords = 4096, kMaxNormRows = 4096, kMaxConvChannels = 16384, kNxFloats = 16384;
 constexpr unsigned kMaxHeads = 32, kStateUnits = 4, kHead = 128, kMaxBlockedRows = 512 * 20;
 constexpr unsigned kMaxRopeDims = 128;
+constexpr unsigned kMaxRanks = 8;  // ranks of a communicator (ALLREDUCE / ALLGATHER)
 // TRACE log: a 16-float header word and up to 512 events of 64 bits (8 per 16-float word)
 constexpr unsigned kTraceEntries = 512, kTraceFloats = 16 + kTraceEntries * 2;
 
@@ -44,6 +45,7 @@ struct Limits {
     // computed in the consumers' prologue (off: stored at the RMSNORM command), runs of RMSNORM / ROPE in one launch,
     // the attention gate applied in the attention merge
     bool defer_norms = true, fuse_rowops = true, fuse_attn_gate = true;
+    unsigned world = 1;                        // ranks of the communicator (ALLGATHER's output is n x world floats)
 };
 
 constexpr unsigned kMaxRowJobs = 8;  // jobs of one RowOps launch
@@ -53,7 +55,7 @@ enum class PassKind : uint32_t {
     Elementwise,    // RMSNORM (stored), ADD, MUL, SILU_MUL, UNARY, CONV, ROPE
     Gdn,            // GDN step (+ WITH_GEMV GEMV, + WITH_OUT GEMV with ADD)
     Nop,            // STATE_LOAD, TRACE, deferred RMSNORM (no launch of its own)
-    Ext,            // ATTN, ARGMAX, GET_ROW
+    Ext,            // ATTN, ARGMAX, GET_ROW, ALLREDUCE, ALLGATHER
     RowOps,         // consecutive RMSNORM (stored) / ROPE commands run as one launch (reported as Elementwise)
 };
 

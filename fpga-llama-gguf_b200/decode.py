@@ -24,13 +24,13 @@ Layer i is an attention layer when i % attn_every == attn_every - 1, else a Gate
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import numpy as np
 
 from . import (CMD_WORDS, GDN_GATED, GDN_GATES, GDN_L2_QK, GDN_WITH_OUT, GEMV_ADD, GEMV_CONV, GEMV_SWIGLU, MAX_CMDS, NORM_DEFER,
-               Q4_0, Q6_K, UPLOAD_PASS_ROWS, UPLOAD_REPLICATE, add, argmax, attn, cmd_list, conv, gdn, gemv, get_row, gguf_row_bytes,
-               rmsnorm, rope, silu_mul)
+               Q4_0, Q6_K, UPLOAD_PASS_ROWS, UPLOAD_REPLICATE, add, allgather, allreduce, argmax, attn, cmd_list, conv, gdn,
+               gemv, get_row, gguf_row_bytes, rmsnorm, rope, silu_mul)
 from . import synth
 
 GDN_DIM = 128  # DeltaNet head size of the command ISA (state rows of 128 floats)
@@ -139,44 +139,151 @@ class ActLayout:
         return off
 
 
-class HybridDecoder:
-    """The synthetic model: seeded weights and resident parameters, the per-token lists and host records."""
+def local_shape(s: Shape, world: int) -> Shape:
+    """The dimensions one rank of a world-way tensor-parallel run holds: DeltaNet heads, query heads, FFN rows and
+    vocabulary rows divided by world (KV heads too, or one KV head shared by world / n_kv_head ranks); the hidden size
+    and the full vocabulary (the gathered logits) stay."""
+    if world == 1:
+        return s
+    ok = (s.gdn_heads % world == 0 and s.n_head % world == 0 and s.ffn % (128 * world) == 0 and
+          s.vocab % (16 * world) == 0 and (s.n_kv_head % world == 0 or world % s.n_kv_head == 0) and
+          (s.n_head // world) * s.head_dim % 128 == 0 and (s.gdn_heads // world) * GDN_DIM % 256 == 0)
+    if not ok:
+        raise ValueError(f"shape does not split over {world} ranks")
+    return replace(s, ffn=s.ffn // world, gdn_heads=s.gdn_heads // world, n_head=s.n_head // world,
+                   n_kv_head=max(1, s.n_kv_head // world))
 
-    def __init__(self, shape: Shape = SHAPE_4B, seed: int = 4, first_token: int = 1):
+
+def _rows(g: np.ndarray, rows: int, idx) -> np.ndarray:
+    return g.reshape(rows, -1)[idx]
+
+
+def _cols(g: np.ndarray, rows: int, cols: int, fmt: int, c0: int, c1: int) -> np.ndarray:
+    """Columns [c0, c1) (multiples of 32) of a Q4_0 / Q8_0 / Q4_1 matrix: a byte range of every GGUF row."""
+    bs = gguf_row_bytes(32, fmt)
+    return np.ascontiguousarray(g.reshape(rows, cols // 32, bs)[:, c0 // 32:c1 // 32]).reshape(rows, -1)
+
+
+class HybridDecoder:
+    """The synthetic model: seeded weights and resident parameters, the per-token lists and host records.
+
+    world > 1: rank `rank` of a tensor-parallel run (a context joined with COMM_EXPLICIT). The rank holds its own
+    slices of the one model every rank generates from the same seeds: DeltaNet heads (their qkv / z / beta / alpha
+    rows, conv channels and states), query heads and their KV heads (K / V rows and KV cache), FFN rows, and
+    vocabulary rows of the head; the projections back to the hidden size (ssm_out, wo, down) are split by columns, so
+    each rank produces a partial hidden vector, rank 0 adds the residual, and one ALLREDUCE per projection sums them
+    into the residual stream (two per layer). The head's logits meet in one ALLGATHER before ARGMAX."""
+
+    def __init__(self, shape: Shape = SHAPE_4B, seed: int = 4, first_token: int = 1, world: int = 1, rank: int = 0):
         self.s = shape
         self.seed = seed
         self.first_token = first_token
-        self.L = ActLayout(shape)
+        self.world, self.rank = world, rank
+        self.ls = local_shape(shape, world)
+        self.L = ActLayout(self.ls)
         self.handles: dict = {}
+
+    # ---- this rank's slices --------------------------------------------------------------------------------------
+    def _gdn_heads(self):
+        h = self.ls.gdn_heads
+        return self.rank * h, (self.rank + 1) * h
+
+    def _qkv_channels(self) -> np.ndarray:
+        """Rows of the qkv projection (= conv channels) of this rank's DeltaNet heads: its q, k and v rows."""
+        h0, h1 = self._gdn_heads()
+        d = self.s.gdn_rows
+        one = np.arange(h0 * GDN_DIM, h1 * GDN_DIM)
+        return np.concatenate([one, d + one, 2 * d + one])
+
+    def _kv_head0(self) -> int:
+        """The first KV head of this rank's query heads."""
+        return self.rank * self.ls.n_head // (self.s.n_head // self.s.n_kv_head)
+
+    def head_pieces(self):
+        """(first row within this rank's vocabulary slice, rows) of each head GEMV."""
+        v_l = self.s.vocab // self.world
+        out, r0 = [], 0
+        while r0 < v_l:
+            n = min(self.s.head_piece, v_l - r0)
+            out.append((r0, n))
+            r0 += n
+        return out
 
     # ---- weights -------------------------------------------------------------------------------------------------
     def matrices(self):
-        """(name, fmt, rows, cols, block_cols, flags, generator) for every matrix, in upload order; the generator
-        draws the GGUF bytes from a stream seeded by (seed, matrix index), so each rank of a sharded run sees the
-        same model."""
-        s = self.s
+        """(name, fmt, rows, cols, block_cols, flags, generator) for every matrix this rank uploads, in upload order;
+        the generator draws the full matrix's GGUF bytes from a stream seeded by (seed, matrix index) and returns
+        this rank's slice of it, so every rank holds slices of the same model."""
+        s, ls, r = self.s, self.ls, self.rank
         H, F, d = s.hidden, s.ffn, s.gdn_rows
         att, kvd = s.n_head * s.head_dim, s.n_kv_head * s.head_dim
+        att_l, kvd_l, d_l, F_l = ls.n_head * s.head_dim, ls.n_kv_head * s.head_dim, ls.gdn_rows, ls.ffn
+        tp = self.world > 1
         # members of one multi-output pass are told the pass's rows, so their panels make one wave of CTAs
-        qkv_pass = UPLOAD_PASS_ROWS(2 * att + 2 * kvd)
-        gdn_pass = UPLOAD_PASS_ROWS(4 * d + 2 * s.gdn_heads)
-        out = [("tok_embd", Q4_0, s.vocab, H, 0, UPLOAD_REPLICATE)]
+        qkv_pass = UPLOAD_PASS_ROWS(2 * att_l + 2 * kvd_l)
+        gdn_pass = UPLOAD_PASS_ROWS(4 * d_l + 2 * ls.gdn_heads)
+        h0, h1 = self._gdn_heads()
+        q0 = r * att_l  # this rank's query heads start at q|gate row 2 q0 ([q; gate] row pairs per head)
+        kv0 = self._kv_head0() * s.head_dim
+        full = [("tok_embd", Q4_0, s.vocab, H, 0, UPLOAD_REPLICATE, None)]
         for i in range(s.n_layers):
             if s.is_attn(i):
-                out += [(f"{i}.wq_gate", Q4_0, 2 * att, H, 0, qkv_pass), (f"{i}.wk", Q4_0, kvd, H, 0, qkv_pass),
-                        (f"{i}.wv", Q4_0, kvd, H, 0, qkv_pass), (f"{i}.wo", Q4_0, H, att, 0, 0)]
+                full += [(f"{i}.wq_gate", Q4_0, 2 * att, H, 0, qkv_pass, ("rows", slice(2 * q0, 2 * q0 + 2 * att_l))),
+                         (f"{i}.wk", Q4_0, kvd, H, 0, qkv_pass, ("rows", slice(kv0, kv0 + kvd_l))),
+                         (f"{i}.wv", Q4_0, kvd, H, 0, qkv_pass, ("rows", slice(kv0, kv0 + kvd_l))),
+                         (f"{i}.wo", Q4_0, H, att, 0, 0, ("cols", r * att_l, (r + 1) * att_l))]
             else:
-                out += [(f"{i}.wqkv", Q4_0, 3 * d, H, 0, gdn_pass), (f"{i}.wz", Q4_0, d, H, 0, gdn_pass),
-                        (f"{i}.wbeta", Q4_0, s.gdn_heads, H, 0, gdn_pass),
-                        (f"{i}.walpha", Q4_0, s.gdn_heads, H, 0, gdn_pass), (f"{i}.ssm_out", Q4_0, H, d, 256, 0)]
-            out += [(f"{i}.gate", Q4_0, F, H, 0, 0), (f"{i}.up", Q4_0, F, H, 0, 0), (f"{i}.down", Q4_0, H, F, 0, 0)]
-        for j, (r0, n) in enumerate(s.head_pieces()):
-            out.append((f"output.{j}", Q6_K, n, H, 0, 0))
-        return [(name, fmt, rows, cols, bc, fl, self._gen(k, fmt, rows, cols))
-                for k, (name, fmt, rows, cols, bc, fl) in enumerate(out)]
+                full += [(f"{i}.wqkv", Q4_0, 3 * d, H, 0, gdn_pass, ("rows", self._qkv_channels())),
+                         (f"{i}.wz", Q4_0, d, H, 0, gdn_pass, ("rows", slice(h0 * GDN_DIM, h1 * GDN_DIM))),
+                         (f"{i}.wbeta", Q4_0, s.gdn_heads, H, 0, gdn_pass, ("rows", slice(h0, h1))),
+                         (f"{i}.walpha", Q4_0, s.gdn_heads, H, 0, gdn_pass, ("rows", slice(h0, h1))),
+                         (f"{i}.ssm_out", Q4_0, H, d, 256, 0, ("cols", h0 * GDN_DIM, h1 * GDN_DIM))]
+            full += [(f"{i}.gate", Q4_0, F, H, 0, 0, ("rows", slice(r * F_l, (r + 1) * F_l))),
+                     (f"{i}.up", Q4_0, F, H, 0, 0, ("rows", slice(r * F_l, (r + 1) * F_l))),
+                     (f"{i}.down", Q4_0, H, F, 0, 0, ("cols", r * F_l, (r + 1) * F_l))]
+        v0 = r * (s.vocab // self.world)
+        full_pieces = [(v0 + a, n) for a, n in self.head_pieces()] if tp else s.head_pieces()
+        for j, (a, n) in enumerate(full_pieces):
+            full.append((f"output.{j}", Q6_K, n, H, 0, 0, ("head", a, n)))
+        out = []
+        for k, (name, fmt, rows, cols, bc, fl, cut) in enumerate(full):
+            if name.startswith("output."):
+                k = len(full)  # the head: one matrix [vocab x hidden], sliced into pieces
+                rows_l, cols_l, gen = self._head_piece(cut[1], cut[2], cols)
+            elif not tp or cut is None:
+                rows_l, cols_l, gen = rows, cols, self._gen(k, fmt, rows, cols)
+            elif cut[0] == "rows":
+                rows_l = len(np.arange(rows)[cut[1]])
+                cols_l, gen = cols, self._sliced(k, fmt, rows, cols, lambda g, rr=rows, c=cut[1]: _rows(g, rr, c))
+            else:
+                rows_l, cols_l = rows, cut[2] - cut[1]
+                gen = self._sliced(k, fmt, rows, cols,
+                                   lambda g, rr=rows, cc=cols, f=fmt, c=cut: _cols(g, rr, cc, f, c[1], c[2]))
+            out.append((name, fmt, rows_l, cols_l, bc, fl, gen))
+        return out
 
     def _gen(self, k: int, fmt: int, rows: int, cols: int):
         return lambda: synth.matrix(fmt, np.random.default_rng([synth.SEED, 40, self.seed, k]), rows, cols)
+
+    def _sliced(self, k: int, fmt: int, rows: int, cols: int, cut):
+        full = self._gen(k, fmt, rows, cols)
+        return lambda: np.ascontiguousarray(cut(full()))
+
+    def _head_piece(self, r0: int, n: int, cols: int):
+        """Rows [r0, r0 + n) of the Q6_K head. Each piece of the one-rank model is generated on its own (seeded by its
+        place in the upload order), so a rank's piece is cut from the one-rank pieces it overlaps."""
+        pieces = self.s.head_pieces()
+        n_before = 1 + self.s.n_layers * 3 + self.s.n_attn * 4 + self.s.n_gdn * 5  # matrices before the head
+
+        def gen():
+            parts = []
+            for j, (a, m) in enumerate(pieces):
+                lo, hi = max(a, r0), min(a + m, r0 + n)
+                if lo < hi:
+                    g = self._gen(n_before + j, Q6_K, m, cols)()
+                    parts.append(g.reshape(m, -1)[lo - a:hi - a])
+            return np.ascontiguousarray(np.concatenate(parts))
+        return n, cols, gen
 
     def upload(self, upload_fn, keep: dict | None = None) -> None:
         """upload_fn(gguf, rows, cols, fmt, block_cols, flags) -> handle. keep: filled {handle: (gguf, rows, cols,
@@ -190,11 +297,15 @@ class HybridDecoder:
 
     # ---- resident state ------------------------------------------------------------------------------------------
     def initial_act(self) -> np.ndarray:
+        """act of this rank: the norm weights (whole), and this rank's conv channels and gate parameters; drawn in the
+        one-rank order from the full model's values."""
         s, L = self.s, self.L
         r = np.random.default_rng([synth.SEED, 41, self.seed])
         act = np.zeros(L.size, np.float32)
         act[L.TOK] = np.array([self.first_token], np.uint32).view(np.float32)[0]
         act[L.ONORM:L.ONORM + s.hidden] = r.normal(1, 0.1, s.hidden)
+        ch_idx = self._qkv_channels() if self.world > 1 else slice(None)
+        h0, h1 = self._gdn_heads()
         for i, p in enumerate(L.layer):
             for key in ("attn_norm", "ffn_norm"):
                 act[p[key]:p[key] + s.hidden] = r.normal(1, 0.1, s.hidden)
@@ -203,24 +314,38 @@ class HybridDecoder:
                     act[p[key]:p[key] + s.head_dim] = r.normal(1, 0.1, s.head_dim)
             else:
                 ch = 3 * s.gdn_rows
-                act[p["conv_w"]:p["conv_w"] + 4 * ch] = r.normal(0, 0.5, 4 * ch)
-                act[p["conv_hist"]:p["conv_hist"] + 3 * ch] = r.normal(0, 1, 3 * ch)
-                act[p["dt"]:p["dt"] + s.gdn_heads] = r.normal(0, 1, s.gdn_heads)
-                act[p["a"]:p["a"] + s.gdn_heads] = -np.exp(r.normal(0, 0.5, s.gdn_heads))
+                cw = r.normal(0, 0.5, 4 * ch).reshape(ch, 4)[ch_idx].reshape(-1)
+                hist = r.normal(0, 1, 3 * ch).reshape(ch, 3)[ch_idx].reshape(-1)
+                dt = r.normal(0, 1, s.gdn_heads)[h0:h1]
+                a = -np.exp(r.normal(0, 0.5, s.gdn_heads))[h0:h1]
+                act[p["conv_w"]:p["conv_w"] + cw.size] = cw
+                act[p["conv_hist"]:p["conv_hist"] + hist.size] = hist
+                act[p["dt"]:p["dt"] + dt.size] = dt
+                act[p["a"]:p["a"] + a.size] = a
                 act[p["gdn_norm"]:p["gdn_norm"] + GDN_DIM] = r.normal(1, 0.1, GDN_DIM)
         return act
 
     def initial_state(self) -> np.ndarray:
-        """DeltaNet state of every GDN layer, fp32 N(0, 0.1), rows of 128 floats (layer j at row j * gdn_rows)."""
+        """DeltaNet state of this rank's heads of every GDN layer, fp32 N(0, 0.1), rows of 128 floats (layer j at row
+        j * local rows)."""
         r = np.random.default_rng([synth.SEED, 42, self.seed])
-        return r.normal(0, 0.1, self.s.n_gdn * self.s.gdn_rows * GDN_DIM).astype(np.float32)
+        st = r.normal(0, 0.1, self.s.n_gdn * self.s.gdn_rows * GDN_DIM).astype(np.float32)
+        if self.world == 1:
+            return st
+        h0, h1 = self._gdn_heads()
+        st = st.reshape(self.s.n_gdn, self.s.gdn_heads, GDN_DIM * GDN_DIM)[:, h0:h1]
+        return np.ascontiguousarray(st).reshape(-1)
 
     def initial_kv(self) -> np.ndarray:
-        """F16 KV slots of the attention layers, positions below the prefill length N(0, 1), the rest zero."""
+        """F16 KV slots of the attention layers (this rank's KV heads), positions below the prefill length N(0, 1),
+        the rest zero."""
         s = self.s
         r = np.random.default_rng([synth.SEED, 43, self.seed])
         kv = np.zeros((s.n_attn, 2, s.n_kv_head, s.kv_ctx, s.head_dim), np.float16)
         kv[..., :s.prefill, :] = r.normal(0, 1, kv[..., :s.prefill, :].shape).astype(np.float16)
+        if self.world > 1:
+            k0 = self._kv_head0()
+            kv = np.ascontiguousarray(kv[:, :, k0:k0 + self.ls.n_kv_head])
         return kv.view(np.uint16).reshape(-1)
 
     def record(self, pos: int) -> np.ndarray:
@@ -236,57 +361,73 @@ class HybridDecoder:
         return rec
 
     # ---- command lists -------------------------------------------------------------------------------------------
+    def _project_out(self, fmt: int, cols: int, w: int, x_off: int, flags_extra=0):
+        """The projection back to the hidden size with the residual: one rank adds it in the GEMV's epilogue
+        (X += W x); tensor parallel: each rank's column slice gives a partial, rank 0 adds the residual, and one
+        ALLREDUCE sums the partials into X."""
+        s, L = self.s, self.L
+        H = s.hidden
+        if self.world == 1:
+            return [gemv(fmt, H, cols, w, x_off, L.OUT, GEMV_ADD), add(H, L.OUT, L.X, L.X)]
+        if self.rank == 0:
+            head = [gemv(fmt, H, cols, w, x_off, L.OUT, GEMV_ADD), add(H, L.OUT, L.X, L.OUT)]
+        else:
+            head = [gemv(fmt, H, cols, w, x_off, L.OUT)]
+        return head + [allreduce(H, L.OUT, L.X)]
+
     def _gdn_layer(self, i: int, j: int):
-        s, L, h = self.s, self.L, self.handles
-        H, d = s.hidden, s.gdn_rows
+        s, ls, L, h = self.s, self.ls, self.L, self.handles
+        H, d = s.hidden, ls.gdn_rows
         p = L.layer[i]
         return [
             rmsnorm(H, L.X, p["attn_norm"], L.XN, s.eps, flags=NORM_DEFER),
             gemv(Q4_0, 3 * d, H, h[f"{i}.wqkv"], L.XN, L.QKV, GEMV_CONV),
             conv(3 * d, L.QKV, p["conv_w"], L.QKVC, p["conv_hist"], p["conv_hist"], True),
             gemv(Q4_0, d, H, h[f"{i}.wz"], L.XN, L.Z),
-            gemv(Q4_0, s.gdn_heads, H, h[f"{i}.wbeta"], L.XN, L.BETA),
-            gemv(Q4_0, s.gdn_heads, H, h[f"{i}.walpha"], L.XN, L.ALPHA),
-            gdn(s.gdn_heads, s.gdn_heads, L.QKVC, L.QKVC + d, L.QKVC + 2 * d, L.ALPHA, L.BETA, L.Y,
+            gemv(Q4_0, ls.gdn_heads, H, h[f"{i}.wbeta"], L.XN, L.BETA),
+            gemv(Q4_0, ls.gdn_heads, H, h[f"{i}.walpha"], L.XN, L.ALPHA),
+            gdn(ls.gdn_heads, ls.gdn_heads, L.QKVC, L.QKVC + d, L.QKVC + 2 * d, L.ALPHA, L.BETA, L.Y,
                 j * d, j * d, GDN_DIM ** -0.5, flags=GDN_L2_QK | GDN_GATED | GDN_GATES | GDN_WITH_OUT,
                 l2_eps=s.eps, rms_eps=s.eps, w_off=p["gdn_norm"], z_off=L.Z, dt_off=p["dt"], a_off=p["a"]),
-            gemv(Q4_0, H, d, h[f"{i}.ssm_out"], L.Y, L.OUT, GEMV_ADD), add(H, L.OUT, L.X, L.X),
-        ] + self._ffn(i)
+        ] + self._project_out(Q4_0, d, h[f"{i}.ssm_out"], L.Y) + self._ffn(i)
 
     def _attn_layer(self, i: int, slot: int):
-        s, L, h = self.s, self.L, self.handles
+        s, ls, L, h = self.s, self.ls, self.L, self.handles
         H, hd = s.hidden, s.head_dim
-        att, kvd = s.n_head * hd, s.n_kv_head * hd
+        att, kvd = ls.n_head * hd, ls.n_kv_head * hd
         p = L.layer[i]
         return [
             rmsnorm(H, L.X, p["attn_norm"], L.XN, s.eps, flags=NORM_DEFER),
             gemv(Q4_0, 2 * att, H, h[f"{i}.wq_gate"], L.XN, L.QG),
             gemv(Q4_0, kvd, H, h[f"{i}.wk"], L.XN, L.K),
             gemv(Q4_0, kvd, H, h[f"{i}.wv"], L.XN, L.V),
-            rmsnorm(hd, L.QG, p["q_norm"], L.QN, s.eps, rows=s.n_head, stride_words=2 * hd // 16),
-            rmsnorm(hd, L.K, p["k_norm"], L.KN, s.eps, rows=s.n_kv_head),
-            rope(s.rope_dims, L.QN, L.CS, L.QR, hd, s.n_head),
-            rope(s.rope_dims, L.KN, L.CS, L.KR, hd, s.n_kv_head),
-            attn(s.n_head, s.n_kv_head, hd, L.QR, L.KR, L.V, L.YA, L.POS, slot),
+            rmsnorm(hd, L.QG, p["q_norm"], L.QN, s.eps, rows=ls.n_head, stride_words=2 * hd // 16),
+            rmsnorm(hd, L.K, p["k_norm"], L.KN, s.eps, rows=ls.n_kv_head),
+            rope(s.rope_dims, L.QN, L.CS, L.QR, hd, ls.n_head),
+            rope(s.rope_dims, L.KN, L.CS, L.KR, hd, ls.n_kv_head),
+            attn(ls.n_head, ls.n_kv_head, hd, L.QR, L.KR, L.V, L.YA, L.POS, slot),
             silu_mul(att, L.QG + hd, L.YA, L.YG, sigmoid=True, row=hd, stride=2 * hd),
-            gemv(Q4_0, H, att, h[f"{i}.wo"], L.YG, L.OUT, GEMV_ADD), add(H, L.OUT, L.X, L.X),
-        ] + self._ffn(i)
+        ] + self._project_out(Q4_0, att, h[f"{i}.wo"], L.YG) + self._ffn(i)
 
     def _ffn(self, i: int):
-        s, L, h = self.s, self.L, self.handles
-        H, F = s.hidden, s.ffn
+        s, ls, L, h = self.s, self.ls, self.L, self.handles
+        H, F = s.hidden, ls.ffn
         return [
             rmsnorm(H, L.X, L.layer[i]["ffn_norm"], L.XN, s.eps, flags=NORM_DEFER),
             gemv(Q4_0, F, H, h[f"{i}.gate"], L.XN, L.FF, GEMV_SWIGLU), gemv(Q4_0, F, H, h[f"{i}.up"], L.XN, L.FF),
-            gemv(Q4_0, H, F, h[f"{i}.down"], L.FF, L.OUT, GEMV_ADD), add(H, L.OUT, L.X, L.X),
-        ]
+        ] + self._project_out(Q4_0, F, h[f"{i}.down"], L.FF)
 
     def _head(self):
         s, L, h = self.s, self.L, self.handles
         H = s.hidden
+        v_l = s.vocab // self.world
+        base = L.LOGITS + self.rank * v_l  # this rank's vocabulary rows (all rows for one rank)
+        pieces = self.head_pieces() if self.world > 1 else s.head_pieces()
         cmds = [rmsnorm(H, L.X, L.ONORM, L.XN, s.eps, flags=NORM_DEFER)]
-        for j, (r0, n) in enumerate(s.head_pieces()):
-            cmds.append(gemv(Q6_K, n, H, h[f"output.{j}"], L.XN, L.LOGITS + r0))
+        for j, (r0, n) in enumerate(pieces):
+            cmds.append(gemv(Q6_K, n, H, h[f"output.{j}"], L.XN, base + r0))
+        if self.world > 1:
+            cmds.append(allgather(v_l, base, L.LOGITS))
         cmds.append(argmax(s.vocab, L.LOGITS, L.TOK))
         return cmds
 
@@ -315,16 +456,17 @@ class HybridDecoder:
 
     # ---- running on a context ------------------------------------------------------------------------------------
     def context_config(self, world: int = 1) -> dict:
-        """Context arguments that fit this model on one rank of a world-way row-sharded run."""
-        s = self.s
+        """Context arguments that fit this model on one rank: of a world-way row-sharded run (the library shards
+        the one-rank model's uploads), or of this tensor-parallel rank (its own slices)."""
+        s, ls = self.s, self.ls
         from . import row_slice, weight_device_bytes
         wb = 0
         for name, fmt, rows, cols, bc, fl, _ in self.matrices():
-            r0, r1 = row_slice(rows, world, 0, fl)
+            r0, r1 = row_slice(rows, world, 0, fl) if self.world == 1 else (0, rows)
             fl_rank = (fl & 0xFF) | UPLOAD_PASS_ROWS((fl >> 8) * (r1 - r0) // rows)  # the hint as the upload scales it
             wb += (weight_device_bytes(r1 - r0, cols, fmt, fl_rank) + 255) // 256 * 256
-        return dict(weight_bytes=wb + (64 << 20), act_floats=self.L.size, state_rows=s.n_gdn * s.gdn_rows,
-                    kv_bytes=s.n_attn * s.kv_slot_bytes, kv_ctx=s.kv_ctx)
+        return dict(weight_bytes=wb + (64 << 20), act_floats=self.L.size, state_rows=s.n_gdn * ls.gdn_rows,
+                    kv_bytes=s.n_attn * ls.kv_slot_bytes, kv_ctx=s.kv_ctx)
 
     def load(self, ctx, keep: dict | None = None) -> None:
         """Uploads the weights and writes act, the DeltaNet states and the KV cache."""

@@ -72,6 +72,15 @@ extern "C" {
 /* [14, format (Q4_0 / Q8_0), cols, w_off lo, w_off hi, idx_off, y_off, 0]: y = dequantized row act[idx_off]
  * (uint32 bits) of the matrix, as ggml get_rows */
 #define B200Q_OP_GET_ROW 14u
+/* [15, n, x_off, y_off, 0, 0, 0, 0]: y = the sum over the ranks of a communicator of their x (n floats; every rank runs
+ * the command; the ranks' x are added in rank order, so every rank gets the same bits). Without a communicator, or
+ * with one rank: y = x. x and y are the same range or disjoint. For lists built per rank (tensor parallel: each
+ * rank multiplies its own column slice of a matrix and the partial outputs are summed), with b200q_comm_init_ex and
+ * B200Q_COMM_EXPLICIT. */
+#define B200Q_OP_ALLREDUCE 15u
+/* [16, n, x_off, y_off, 0, 0, 0, 0]: y[r n .. r n + n) = x of rank r, for every rank r (y: n x world floats); with one
+ * rank y = x. x and y are disjoint, or x is rank r's own part of y. */
+#define B200Q_OP_ALLGATHER 16u
 
 #define B200Q_GEMV_SWIGLU 0x100u
 #define B200Q_GEMV_CONV 0x200u
@@ -105,10 +114,10 @@ extern "C" {
 /* feature words written by a zero-command b200q_run() into act[0], act[1] (reference gemvqc16.h:126-134): the
  * reference's marker and bit meanings, all bits set (Q5_K, Q6_K, Q4_1, every fusion, ROPE, TRACE). act[2] holds
  * this library's own word: marker 0x6B53 in the high half, bit 0 ATTN, bit 1 ARGMAX, bit 2 GET_ROW, bit 3
- * row-sharded multi-GPU lists. */
+ * row-sharded multi-GPU lists, bit 4 ALLREDUCE / ALLGATHER. */
 #define B200Q_FEATURES 0x6B51FFFFu
 #define B200Q_FEATURES2 0x6B520001u
-#define B200Q_FEATURES3 0x6B53000Fu
+#define B200Q_FEATURES3 0x6B53001Fu
 
 /* ---- status codes ------------------------------------------------------------------------------------------ */
 #define B200Q_OK 0
@@ -383,6 +392,14 @@ B200Q_API int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]);
  * environment variable B200Q_PEER=1 the GEMV kernels store their rows straight into every peer's act over NVLink
  * (CUDA IPC mappings made here) and the next kernel waits for the peers' flags (bounded waits). */
 B200Q_API int b200q_comm_init(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]);
+/* As b200q_comm_init; flags B200Q_COMM_EXPLICIT: the caller builds each rank's own lists (tensor parallel: its own
+ * row or column slices of the matrices, uploaded as they are, and ALLREDUCE / ALLGATHER commands where partial
+ * results meet). Uploads then keep all rows and no pass gathers anything by itself. The collectives run on NCCL, or
+ * with the environment variable B200Q_PEER=1 as one kernel that pushes this rank's part into every peer's receive
+ * buffer over NVLink (CUDA IPC mappings made here) and sums the parts in rank order after bounded flag waits. */
+#define B200Q_COMM_EXPLICIT 1u
+B200Q_API int b200q_comm_init_ex(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES],
+                                 unsigned flags);
 /* The rows [*r0, *r1) of a rows-row matrix that rank `rank` of `world` keeps at upload (host only): a slice of
  * rows / world when rows divide by 16 x world and flags has no B200Q_UPLOAD_REPLICATE, else all rows. */
 B200Q_API int b200q_row_slice(unsigned rows, unsigned flags, int world, int rank, unsigned *r0, unsigned *r1);

@@ -941,6 +941,18 @@ ORC_API int orc_run_list(float *act, size_t act_floats, float *state, size_t sta
                 break;
             }
             orc_dequantize_row(w->data + (size_t)row * orc_row_bytes(cols, fmt), cols, fmt, M.act + c[6]);
+        } else if (op == 15 || op == 16) { /* ALLREDUCE / ALLGATHER extensions, one rank: y = x (a test that runs
+                                             * several ranks' lists performs the collectives itself, between lists) */
+            const unsigned n = c[1];
+            const size_t x = c[2], y = c[3];
+            int ok = n != 0 && n % 16 == 0 && x % 16 == 0 && y % 16 == 0 && (c[4] | c[5] | c[6] | c[7]) == 0 &&
+                     in_act(&M, c[2], n) && in_act(&M, c[3], n);
+            if (ok && (x != y)) ok = x + n <= y || y + n <= x;
+            if (!ok) {
+                status = (int)i + 1;
+                break;
+            }
+            memmove(M.act + y, M.act + x, sizeof(float) * n);
         } else {
             status = (int)i + 1;
             break;

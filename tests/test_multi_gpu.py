@@ -1,7 +1,14 @@
-"""Row-sharded decode on two GPUs (each rank stores its GEMV rows into the peer's act over NVLink, no collective)
-against the same decode on one GPU: every row is computed by the same arithmetic on whichever rank holds it, so the
-greedy tokens, the act buffer and the DeltaNet states are bit-identical. Needs two GPUs; skipped otherwise (the
-single-GPU round-end run skips it)."""
+"""Decode on two (and four) GPUs against the same decode on one GPU. Needs two GPUs; skipped otherwise (the
+single-GPU round-end run skips it).
+
+Row-sharded (each rank's GEMV rows gathered by NCCL or stored into the peer's act over NVLink): every row is computed
+by the same arithmetic on whichever rank holds it, so the greedy tokens, the act buffer and the DeltaNet states are
+bit-identical to one GPU whose deferred norms also sum x's squares from x itself (the feature mask switches off the
+per-panel partials a one-GPU run hands between passes, whose sum takes another fixed order).
+
+Tensor parallel (each rank its own heads, FFN rows and column slices; ALLREDUCE per projection, by NCCL or by the
+peer kernel): the same greedy tokens, logits within 1e-4 of the largest, the residual stream within 1e-4 (relative,
+floor 1e-3), rank 0's DeltaNet states within 1e-4 of the one-GPU rows of its heads."""
 import os
 import socket
 import subprocess
@@ -54,8 +61,28 @@ def test_two_gpu_sharded_decode_is_bit_identical_to_one_gpu(scratch, mode):
     one, two = os.path.join(scratch, "one"), os.path.join(scratch, "two")
     os.makedirs(one)
     os.makedirs(two)
-    a = _run(1, str(one), 6)
+    a = _run(1, str(one), 6, {"B200Q_FEATURE_MASK": str(0xFFFFFFFF & ~(1 << 17))})
     b = _run(2, str(two), 6, {"B200Q_PEER": "1" if mode == "peer" else "0"})
     assert list(a["toks"]) == list(b["toks"])
     assert np.array_equal(a["act"].view(np.uint32), b["act"].view(np.uint32))
     assert np.array_equal(a["state"].view(np.uint32), b["state"].view(np.uint32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,mode", [(2, "peer"), (2, "nccl"), (4, "peer")])
+def test_tensor_parallel_decode_matches_one_gpu(scratch, world, mode):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    one, many = os.path.join(scratch, "one"), os.path.join(scratch, "many")
+    os.makedirs(one)
+    os.makedirs(many)
+    env = {"MGPU_SHAPE": "small8"}
+    a = _run(1, str(one), 6, env)
+    b = _run(world, str(many), 6, dict(env, MGPU_MODE="tp", B200Q_PEER="1" if mode == "peer" else "0"))
+    assert list(a["toks"]) == list(b["toks"])
+    assert np.abs(a["logits"] - b["logits"]).max() <= 1e-4 * np.abs(a["logits"]).max()
+    assert (np.abs(a["x"] - b["x"]) <= 1e-4 * np.maximum(np.abs(a["x"]), 1e-3)).all()
+    # rank 0 holds the first heads of every DeltaNet layer
+    n_gdn, heads, S = 3, 8, 128 * 128
+    want = a["state"].reshape(n_gdn, heads, S)[:, :heads // world].reshape(-1)
+    assert (np.abs(b["state"] - want) <= 1e-4 * np.maximum(np.abs(want), 1e-3)).all()
