@@ -173,6 +173,8 @@ class VerifyView(ctypes.Structure):
 VERIFY_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(VerifyView), ctypes.c_void_p, ctypes.c_uint)
 MASK_GROUPS, MASK_DEFER_NORM, MASK_GDN_OUT = 1 << 3, 1 << 9, 1 << 15
 MASK_X_IMAGE, MASK_NORM_PARTIALS, MASK_PDL, MASK_ROW_OPS, MASK_ATTN_GATE = 1 << 16, 1 << 17, 1 << 18, 1 << 19, 1 << 20
+MASK_CHAINS = 1 << 21
+DEFAULT_FEATURE_MASK = 0xFFFFFFFF & ~MASK_CHAINS
 ERR_VERIFY = -8
 
 

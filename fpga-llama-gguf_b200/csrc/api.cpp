@@ -82,7 +82,11 @@ constexpr size_t kAttnPartFloats = size_t(1) << 22;  // ATTN chunk outputs (16 M
 // of the fused forms this library also fuses internally, then this library's own
 constexpr uint32_t kMaskGroups = 1u << 3, kMaskDeferNorm = 1u << 9, kMaskGdnOut = 1u << 15;
 constexpr uint32_t kMaskImage = 1u << 16, kMaskNsq = 1u << 17, kMaskPdl = 1u << 18, kMaskRowOps = 1u << 19,
-                   kMaskAttnGate = 1u << 20;
+                   kMaskAttnGate = 1u << 20, kMaskChains = 1u << 21;
+constexpr unsigned kMaxChains = 64;  // persistent GEMV chains per list (each has its own counter block)
+// every fusion on but the persistent chains: measured slower than the chained passes' own kernels (one CTA per SM
+// cannot hide the x preparation and the uneven end of each pass; 171 vs 139 us per 6-layer stack step)
+constexpr uint32_t kDefaultFeatureMask = 0xFFFFFFFFu & ~kMaskChains;
 // feature bits a mask never hides: the weight formats and the Q6_K layout (reference ggml-xrt.cpp:1298)
 constexpr uint32_t kFeatureKeep = 0xFFFF0000u | 1u | 2u | 4u | (1u << 13);
 
@@ -140,9 +144,11 @@ struct b200q_ctx {
     float *peer_coll_recv[kMaxPeers] = {};
     unsigned *peer_coll_flags[kMaxPeers] = {};
     unsigned coll_slot_next = 0;
+    unsigned *chain_counters = nullptr;  // kMaxChains x kChainCounters words, zero between launches
+    unsigned chain_next = 0;             // the next chain's counter block in the list being executed
     bool pdl = true;
     bool pdl_env = true;       // B200Q_NO_PDL=1 turns programmatic dependent launch off for the context's life
-    uint32_t feature_mask = 0xFFFFFFFFu;  // B200Q_FEATURE_MASK (b200q_set_feature_mask)
+    uint32_t feature_mask = 0xFFFFFFFFu;  // B200Q_FEATURE_MASK (b200q_set_feature_mask), set at create
     // runtime verification of the first verify_left lists against the caller's checker (b200q_set_verify)
     b200q_verify_fn verify_fn = nullptr;
     void *verify_user = nullptr;
@@ -788,12 +794,110 @@ int link_nsq(const b200q_ctx *c, const Pass &p, const Pass &q, ImageLink &link) 
     return -1;
 }
 
+// ---- persistent GEMV chains ----------------------------------------------------------------------------------------
+// Pass p as one pass of a chain (gemv_chain_kernel), after `prev` (null: the chain's first pass). Chainable: a GEMV
+// pass of one Q4_0 / Q8_0 matrix or a SwiGLU pair of two, its output plain or residual-ADD, unsharded, x not
+// quantized ahead (prequant), no output overlapping the pass's own inputs (x, norm weight, residual other than in
+// place). Its x: the previous pass's image when it reads exactly that output (32-row panels), a deferred norm, or
+// act x.
+bool chain_pass(const b200q_ctx *c, const Pass &p, const ChainPass *prev, ChainPass &cp) {
+    if (p.kind != PassKind::Gemv || p.prequant || (p.from_nd && p.nd.materialize)) return false;
+    const bool pair = p.n_members == 2 && p.m[0].epi == EpiSwigluG && p.m[1].epi == EpiSwigluU;
+    if (!(p.n_members == 1 || pair)) return false;
+    const Member &mo = p.m[p.n_members - 1];
+    if (!pair && mo.epi != EpiNone && mo.epi != EpiAdd) return false;
+    const unsigned fmt = p.m[0].format;
+    if ((fmt != B200Q_Q4_0 && fmt != B200Q_Q8_0) || (pair && p.m[1].format != fmt)) return false;
+    const WeightInfo *wa = p.m[0].w ? p.m[0].w : find_w(c, p.m[0].handle);
+    const WeightInfo *wb = pair ? (p.m[1].w ? p.m[1].w : find_w(c, p.m[1].handle)) : nullptr;
+    if (!wa || wa->row_begin != 0 || wa->row_end != wa->rows) return false;
+    if (pair && (!wb || wb->row_begin != 0 || wb->row_end != wb->rows || wb->rt != wa->rt || wb->kc != wa->kc ||
+                 wb->rows != wa->rows))
+        return false;
+    cp = ChainPass();
+    cp.wa = view_of(c, *wa);
+    if (pair) cp.wb = view_of(c, *wb);
+    cp.fmt = fmt;
+    cp.pair = pair ? 1u : 0u;
+    cp.cols = p.cols;
+    GemvMemberArgs &o = cp.out;
+    o.w = cp.wa;
+    o.epi = mo.epi;
+    o.total_rows = mo.rows;
+    o.y = c->act + mo.y_off;
+    if (mo.epi == EpiAdd) o.res = c->act + mo.r_off;
+    const size_t yn = mo.epi == EpiAdd ? mo.rows : round16(mo.rows);
+    if (p.from_nd) {
+        cp.x_kind = 1;
+        cp.x = c->act + p.nd.x_off;
+        cp.norm_w = c->act + p.nd.w_off;
+        cp.norm_eps = p.nd.eps;
+        cp.norm_mode = 8u | p.nd.flags;
+    } else if (prev && prev->out.y == c->act + p.x_off && prev->out.total_rows == p.cols && prev->wa.rt == 32 &&
+               p.cols % 32 == 0 && (c->feature_mask & kMaskImage)) {
+        cp.x_kind = 2;
+    } else {
+        cp.x_kind = 0;
+        cp.x = c->act + p.x_off;
+    }
+    // the pass's output does not meet its own inputs (a residual read in place, row by row, is fine)
+    if (cp.x_kind != 2 && meet(cp.x, p.cols, o.y, yn)) return false;
+    if (cp.x_kind == 1 && !(p.nd.flags & 2u) && meet(cp.norm_w, p.cols, o.y, yn)) return false;
+    if (o.res && o.res != o.y && meet(o.res, mo.rows, o.y, yn)) return false;
+    return true;
+}
+
+// The run of passes from plan.passes[pi] that one chain launch executes (>= 2 GEMV passes, skipping deferred-norm
+// markers that launch nothing); returns the index after the run, or pi when no chain starts here.
+size_t build_chain(b200q_ctx *c, const Plan &plan, size_t pi, ChainArgs &a) {
+    if (!(c->feature_mask & kMaskChains) || plan.has_trace || c->pending.n || c->chain_next >= kMaxChains ||
+        (c->world > 1 && !c->explicit_comm))
+        return pi;
+    a = ChainArgs();
+    size_t qi = pi, end = pi;
+    unsigned items = 0;
+    while (qi < plan.passes.size() && a.n_passes < kMaxChainPasses) {
+        const Pass &p = plan.passes[qi];
+        if (p.kind == PassKind::Nop && !p.nd_store && p.op == 2) {  // a deferred norm's marker: no launch
+            ++qi;
+            continue;
+        }
+        ChainPass &cp = a.p[a.n_passes];
+        if (!chain_pass(c, p, a.n_passes ? &a.p[a.n_passes - 1] : nullptr, cp)) break;
+        cp.item0 = items;
+        items += cp.wa.n_rt;
+        ++a.n_passes;
+        end = ++qi;
+    }
+    if (a.n_passes < 2) return pi;
+    // a pass whose successor reads its output as an image writes one (alternating buffers)
+    for (unsigned k = 0; k + 1 < a.n_passes; ++k) {
+        if (a.p[k + 1].x_kind != 2) continue;
+        a.p[k].qout = c->qimg[k & 1u];
+        a.p[k].qout_act = 0;
+        a.p[k + 1].qin = c->qimg[k & 1u];
+    }
+    a.total_items = items;
+    return end;
+}
+
+int exec_chain(b200q_ctx *c, ChainArgs &a) {
+    size_t smem = 0;
+    if (!plan_gemv_chain(a, smem)) return set_err(c, B200Q_ERR_ARG, "GEMV chain: shared-memory plan failed");
+    a.counters = c->chain_counters + size_t(c->chain_next++) * kChainCounters;
+    a.err = c->dstatus + 1;
+    CUDA_TRY(c, launch_gemv_chain(a, unsigned(c->sms), smem, c->stream, c->pdl));
+    ++c->launches;
+    return 0;
+}
+
 // Executes the passes of a plan on the context stream (no synchronization).
 int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
     c->launches = 0;
     c->slot_next = 0;
     c->coll_slot_next = 0;
+    c->chain_next = 0;
     c->pending.n = 0;
     c->n_events = 0;
     c->host_tags.clear();
@@ -812,6 +916,17 @@ int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
         if ((rc = stamp(c, tr, p.first, 0))) return rc;
         const bool is_pass = p.kind == PassKind::Gemv || p.kind == PassKind::Gdn;
         if (is_pass && (rc = stamp(c, tr, p.first, 1))) return rc;
+        if (p.kind == PassKind::Gemv && !tr) {
+            ChainArgs ca;
+            const size_t end = build_chain(c, plan, pi, ca);
+            if (end > pi) {
+                if ((rc = exec_chain(c, ca))) return rc;
+                img_in = nullptr;
+                nsq_in = nullptr;
+                pi = end - 1;
+                continue;
+            }
+        }
         switch (p.kind) {
         case PassKind::Gemv:
         {
@@ -994,10 +1109,13 @@ int b200q_create(const b200q_config *cfg, b200q_ctx **out) {
     if ((e = cudaMalloc(&nq, 2 * kMaxNsqPanels * sizeof(double))) != cudaSuccess) return fail(e, "norm partials");
     c->nsq[0] = nq;
     c->nsq[1] = nq + kMaxNsqPanels;
+    if ((e = cudaMalloc(&c->chain_counters, kMaxChains * kChainCounters * sizeof(unsigned))) != cudaSuccess)
+        return fail(e, "chain counters");
+    cudaMemset(c->chain_counters, 0, kMaxChains * kChainCounters * sizeof(unsigned));
     const char *pdl = getenv("B200Q_NO_PDL");
     c->pdl_env = !(pdl && pdl[0] == '1');
     const char *mask = getenv("B200Q_FEATURE_MASK");
-    c->feature_mask = mask && mask[0] ? uint32_t(strtoul(mask, nullptr, 0)) : 0xFFFFFFFFu;
+    c->feature_mask = mask && mask[0] ? uint32_t(strtoul(mask, nullptr, 0)) : kDefaultFeatureMask;
     c->pdl = c->pdl_env && (c->feature_mask & kMaskPdl);
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return fail(e, "init");
     *out = c;
@@ -1021,6 +1139,7 @@ void b200q_destroy(b200q_ctx *c) {
     cudaFree(c->warena);
     cudaFree(c->qimg[0]);
     cudaFree(c->nsq[0]);
+    cudaFree(c->chain_counters);
     cudaFree(c->act);
     cudaFree(c->state);
     cudaFree(c->kv);

@@ -772,4 +772,475 @@ cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+
+// ==== persistent GEMV chain =========================================================================================
+// One launch runs a chain of consecutive Q4_0 / Q8_0 passes (ChainArgs): the layer stack's norm -> gate+up (SwiGLU)
+// -> down (+residual) -> norm -> ..., without a kernel boundary between the passes. One CTA per SM (any grid works:
+// work is taken, not assigned, so no CTA waits for one that is not resident), 11 warps:
+//   warp 8 (producer): takes the chain's items (row panels, numbered pass by pass) one at a time from a global
+//     counter and streams each item's steps (one 32-unit tile per matrix), 8 consecutive steps of a pair or 16 of a
+//     single matrix per stage (one bulk copy per matrix), into a ring of shared-memory stages. Weights never change, so it runs ahead into the
+//     next pass while that pass still waits for its x: HBM keeps streaming through every dependency between passes
+//     (the stall a kernel boundary costs).
+//   warps 9, 10 (fold): per item, add each row's terms in block order (the CPU's FP32 sum, bit for bit; warp 10 a
+//     pair's u terms) and write the row, while the consumers already fill the other of two term buffers;
+//   warps 0-7 (consumers): per item, warp w takes steps w, w + 8, ... of every stage (lane = unit: the exact
+//     integer block dot and the FP32 block term, as gemv_q8_kernel) into a term buffer; before an item of a new pass
+//     they wait until every item of the previous pass is finished (a global counter per pass) and prepare that pass's
+//     x: the previous pass's quantized image, or act x (through the deferred RMSNORM) quantized by the same
+//     arithmetic as the single-pass kernel.
+// Stage / queue hand-offs are mbarriers; every wait is bounded (kWaitLimitNs): on expiry the CTA sets the error word,
+// stops, and lets its own bulk copies land before it exits. The launch's last CTA leaves the counters at zero. The
+// kernel never triggers the next kernel's early launch, so the next chain launch finds its counters reset.
+// Activations written inside the launch (x, the residual, the images) are read through L2 only (ld.global.cg).
+constexpr unsigned kChainConsumers = 8, kChainThreads = 32 * (kChainConsumers + 3), kChainQueue = 8;
+constexpr unsigned kChainEnd = 0xffffffffu;
+constexpr unsigned kChainBarBytes = 2048;  // mbarriers, the item queue and words, the abort flag, 2 x 32 u sums
+static_assert(sizeof(ChainArgs) <= 32000, "the chain's arguments fit the kernel parameter space");
+
+// the consumer warps' barrier (named barrier 1; the producer warp never joins it)
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kChainConsumers) : "memory");
+}
+// ... and the same barrier returning, to every consumer thread, whether any of them passed true
+__device__ __forceinline__ bool consumers_any(bool v) {
+    uint32_t r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+                 : "=r"(r)
+                 : "r"(unsigned(v)), "n"(32 * kChainConsumers)
+                 : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void fold_pair_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
+
+__device__ __forceinline__ void red_release_gpu(unsigned *p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// A stage holds the consecutive steps of one item: kChainConsumers of a SwiGLU pair ([g steps][u steps at
+// chain_pair_offset]) or twice as many of a single matrix, so that both fill the same bytes (each consumer warp
+// takes one pair step or two single steps of a stage).
+constexpr unsigned kChainPairSteps = kChainConsumers;
+__host__ __device__ inline unsigned chain_stage_steps(unsigned pair) { return pair ? kChainPairSteps : 2 * kChainPairSteps; }
+__host__ __device__ inline unsigned chain_pair_offset(unsigned tile_bytes) {
+    return (kChainPairSteps * tile_bytes + 127u) & ~127u;
+}
+
+__device__ __forceinline__ unsigned chain_pass_of(const ChainArgs &a, unsigned g) {
+    unsigned k = 0;
+    while (k + 1 < a.n_passes && g >= a.p[k + 1].item0) ++k;
+    return k;
+}
+__device__ __forceinline__ unsigned chain_items(const ChainArgs &a, unsigned k) {
+    return (k + 1 < a.n_passes ? a.p[k + 1].item0 : a.total_items) - a.p[k].item0;
+}
+
+// The RMSNORM scale from each consumer thread's FP64 partial: the order of norm_scale (a shuffle tree per warp, then
+// the warps in order), with the consumers' barrier.
+__device__ __forceinline__ float chain_norm_scale(double acc, unsigned n, float eps, unsigned l2, double *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
+    consumers_sync();
+    double sum = 0.0;
+    for (unsigned w = 0; w < kChainConsumers; ++w) sum += red[w];
+    if (l2) return fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(sum)), eps));
+    return fdiv(1.0f, __fsqrt_rn(fadd(__double2float_rn(__ddiv_rn(sum, double(n))), eps)));
+}
+
+// x of pass P into the image (quants at q, meta words at q + cols), by the 256 consumer threads (x_kind 0 / 1): per
+// 32-block the arithmetic of prepare_x_cluster (the same per-thread ownership of 16 values, the same FP64 norm sum
+// order), every block by this CTA.
+__device__ __forceinline__ void chain_prepare_x(const ChainPass &P, uint8_t *q, double *red) {
+    const unsigned n = P.cols, nb = n / 32, t = threadIdx.x, h = t & 1u;
+    uint4 *meta = reinterpret_cast<uint4 *>(q + n);
+    const bool norm = P.x_kind == 1, weighted = (P.norm_mode & 2u) == 0;
+    // round 0's x and weight values stay in registers from the one load both the norm sum and the quantizer use
+    // (thread t owns the same 16 values in both); later rounds (more than 4096 columns) load again
+    float4 x0[4], w0[4];
+#pragma unroll
+    for (unsigned i = 0; i < 4; ++i) {
+        const unsigned b = t >> 1;
+        x0[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        w0[i] = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (b < nb) {
+            x0[i] = __ldcg(reinterpret_cast<const float4 *>(P.x + b * 32 + h * 16) + i);
+            if (norm && weighted) w0[i] = __ldcg(reinterpret_cast<const float4 *>(P.norm_w + b * 32 + h * 16) + i);
+        }
+    }
+    float scale = 1.0f;
+    if (norm) {
+        double acc = sumsq16(x0);
+        for (unsigned r = 1; r * (kPanelThreads / 2) < nb; ++r) {
+            float4 nv[4];
+            load16(P.x, n, r, true, nv);
+            acc += sumsq16(nv);
+        }
+        scale = chain_norm_scale(acc, n, P.norm_eps, P.norm_mode & 1u, red);
+    }
+    for (unsigned r = 0; r * (kPanelThreads / 2) < nb; ++r) {
+        const unsigned b = r * (kPanelThreads / 2) + (t >> 1);
+        const bool live = b < nb;
+        float v[16];
+#pragma unroll
+        for (unsigned i = 0; i < 4; ++i) {
+            float4 xv = x0[i], wv = w0[i];
+            if (r > 0) {
+                xv = make_float4(0.f, 0.f, 0.f, 0.f);
+                wv = make_float4(1.f, 1.f, 1.f, 1.f);
+                if (live) {
+                    xv = __ldcg(reinterpret_cast<const float4 *>(P.x + b * 32 + h * 16) + i);
+                    if (norm && weighted)
+                        wv = __ldcg(reinterpret_cast<const float4 *>(P.norm_w + b * 32 + h * 16) + i);
+                }
+            }
+            const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (unsigned e = 0; e < 4; ++e)
+                v[4 * i + e] = !norm ? xs[e] : (weighted ? fmul(fmul(xs[e], scale), ws[e]) : fmul(xs[e], scale));
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        const float s = fdiv(amax, 127.0f);
+        const float id = s != 0.0f ? fdiv(1.0f, s) : 0.0f;
+        int sum = 0;
+        uint32_t word[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int qv = int(roundf(fmul(v[e], id)));
+            sum += qv;
+            word[e / 4] |= uint32_t(qv & 0xff) << (8 * (e % 4));
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (live) {
+            *reinterpret_cast<uint4 *>(q + h * (n / 2) + b * 16) = make_uint4(word[0], word[1], word[2], word[3]);
+            if (h == 0) {
+                const float dh = half_bits_to_float(float_to_half_bits(s));
+                meta[b] = make_uint4(__float_as_uint(dh), 0u, uint32_t(sum), 0u);
+            }
+        }
+    }
+}
+
+// The image the previous pass wrote (x_kind 2): quants, then the meta words, as they lie in shared memory.
+__device__ __forceinline__ void chain_copy_image(const ChainPass &P, uint8_t *q) {
+    const unsigned n = P.cols, words = (n + n / 32 * 16) / 16;
+    const uint4 *src = reinterpret_cast<const uint4 *>(P.qin);
+    uint4 *dst = reinterpret_cast<uint4 *>(q);
+    for (unsigned i = threadIdx.x; i < words; i += 32 * kChainConsumers) dst[i] = __ldcg(src + i);
+}
+
+// Warp `warp`'s steps of one item: stage (s_base + c) % S holds steps M c .. M c + M - 1 (M = chain_stage_steps),
+// and the warp takes steps M c + warp (+ 8) of each (every warp releases every stage once, as soon as its loads are
+// in registers): steps warp, warp + 8, ... of the item. False if a wait gave up.
+template <unsigned FMT, bool PAIR>
+__device__ __forceinline__ bool chain_steps(const ChainPass &P, const XSmem &xs, unsigned warp, unsigned lane,
+                                            const uint8_t *stages, unsigned stage_bytes, unsigned S, uint64_t *full,
+                                            uint64_t *empty, unsigned s_base, float *term_a, float *term_b,
+                                            volatile unsigned *abort) {
+    constexpr unsigned M = PAIR ? kChainPairSteps : 2 * kChainPairSteps, R = M / kChainConsumers;
+    const MatrixView &w = P.wa;
+    const unsigned J = w.ct, K = w.kc, nb = P.cols / 32, TS = term_stride(K * J);
+    const unsigned j = lane & (J - 1u), tslot = (lane / J) * TS + j;
+    const unsigned boff = chain_pair_offset(w.tile_bytes);
+    for (unsigned c = 0; c * M < K; ++c) {
+        const unsigned gs = s_base + c, st = gs % S;
+        if (!role_wait(full + st, (gs / S) & 1u, abort)) return false;
+        const uint8_t *stage = stages + size_t(st) * stage_bytes;
+        Step<FMT> ca[R], cb[R];
+#pragma unroll
+        for (unsigned r = 0; r < R; ++r) {
+            const unsigned m = warp + kChainConsumers * r;
+            if (c * M + m < K) {
+                load_step_smem<FMT>(ca[r], stage + m * w.tile_bytes, lane);
+                if (PAIR) load_step_smem<FMT>(cb[r], stage + boff + m * P.wb.tile_bytes, lane);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + st);
+#pragma unroll
+        for (unsigned r = 0; r < R; ++r) {
+            const unsigned i = c * M + warp + kChainConsumers * r;
+            if (i >= K) break;
+            const unsigned b = i * J + j, bc = b < nb ? b : 0u;
+            const XBlock x = load_xblock(xs, bc);
+            int sumi;
+            term_a[tslot + i * J] = block_term<FMT>(ca[r], x, sumi);
+            if (PAIR) {
+                int su;
+                term_b[tslot + i * J] = block_term<FMT>(cb[r], x, su);
+            }
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool chain_steps_any(const ChainPass &P, const XSmem &xs, unsigned warp, unsigned lane,
+                                                const uint8_t *stages, unsigned stage_bytes, unsigned S,
+                                                uint64_t *full, uint64_t *empty, unsigned s_base, float *term_a,
+                                                float *term_b, volatile unsigned *abort) {
+    if (P.fmt == 8)
+        return P.pair ? chain_steps<8, true>(P, xs, warp, lane, stages, stage_bytes, S, full, empty, s_base, term_a,
+                                             term_b, abort)
+                      : chain_steps<8, false>(P, xs, warp, lane, stages, stage_bytes, S, full, empty, s_base, term_a,
+                                              term_b, abort);
+    return P.pair ? chain_steps<2, true>(P, xs, warp, lane, stages, stage_bytes, S, full, empty, s_base, term_a,
+                                         term_b, abort)
+                  : chain_steps<2, false>(P, xs, warp, lane, stages, stage_bytes, S, full, empty, s_base, term_a,
+                                          term_b, abort);
+}
+
+// Bounded wait until a pass's items are all finished (one thread).
+__device__ __forceinline__ bool chain_wait_pass(const unsigned *done, unsigned items) {
+    unsigned long long t0 = 0;
+    for (unsigned i = 0; ld_acquire_gpu(done) < items; ++i) {
+        if ((i & 255u) == 255u) {
+            const unsigned long long now = global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > kWaitLimitNs) return false;
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __grid_constant__ ChainArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const unsigned S = a.n_stages, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + S;
+    uint64_t *qfull = empty + S, *qempty = qfull + kChainQueue;
+    uint64_t *tready = qempty + kChainQueue, *tfree = tready + 2;  // per term buffer: terms written / folded
+    unsigned *queue = reinterpret_cast<unsigned *>(tfree + 2);
+    unsigned *info = queue + kChainQueue;  // per term buffer: the item whose terms it holds (kChainEnd: none left)
+    volatile unsigned *abort = info + 2;
+    float *usum = reinterpret_cast<float *>(smem + kChainBarBytes - 256);  // [2 buffers][32]
+    unsigned char *p = smem + kChainBarBytes;
+    double *red = reinterpret_cast<double *>(p);  // 256 bytes of norm partials, then the x image
+    uint8_t *xq = p + 256;
+    p += a.ximg_bytes;
+    float *terms = reinterpret_cast<float *>(p);  // [2 buffers][a, b] of term_bytes each
+    p += 4 * size_t(a.term_bytes);
+    uint8_t *stages = p;
+    if (threadIdx.x == 0) {
+        for (unsigned i = 0; i < S; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kChainConsumers);  // every consumer warp releases every stage
+        }
+        for (unsigned i = 0; i < kChainQueue; ++i) {
+            mbar_init(qfull + i, 1);
+            mbar_init(qempty + i, 1);
+        }
+        for (unsigned i = 0; i < 2; ++i) {
+            mbar_init(tready + i, kChainConsumers);
+            mbar_init(tfree + i, 1);
+        }
+        *abort = 0u;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    unsigned *taken = a.counters, *finished = a.counters + 1, *done = a.counters + 2;
+    const unsigned tw = a.term_bytes / 4;  // floats of one term buffer
+
+    if (warp == kChainConsumers) {
+        // ---- producer: weights only, so it starts before the wait on the previous kernel
+        if (lane == 0) {
+            const uint64_t pol = evict_first_policy();
+            unsigned s = 0;
+            bool ok = true;
+            for (unsigned n = 0;; ++n) {
+                const unsigned g = atomicAdd(taken, 1u);
+                const unsigned q = n % kChainQueue;
+                if (n >= kChainQueue && !role_wait(qempty + q, ((n / kChainQueue) - 1u) & 1u, abort)) ok = false;
+                queue[q] = ok && g < a.total_items ? g : kChainEnd;
+                mbar_arrive(qfull + q);
+                if (ok && g < a.total_items) {
+                    const ChainPass &P = a.p[chain_pass_of(a, g)];
+                    const unsigned t = g - P.item0, K = P.wa.kc, ta = P.wa.tile_bytes, tb = P.wb.tile_bytes;
+                    const uint8_t *src_a = P.wa.base + size_t(t) * K * ta;
+                    const uint8_t *src_b = P.pair ? P.wb.base + size_t(t) * K * tb : nullptr;
+                    const unsigned M = chain_stage_steps(P.pair);
+                    for (unsigned i = 0; i < K; i += M, ++s) {
+                        const unsigned st = s % S, m = min(M, K - i);
+                        if (s >= S && !role_wait(empty + st, ((s / S) - 1u) & 1u, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t *dst = stages + size_t(st) * a.stage_bytes;
+                        mbar_expect_tx(full + st, m * (P.pair ? ta + tb : ta));
+                        bulk_copy(dst, src_a + size_t(i) * ta, m * ta, full + st, pol);
+                        if (P.pair)
+                            bulk_copy(dst + chain_pair_offset(ta), src_b + size_t(i) * tb, m * tb, full + st, pol);
+                    }
+                }
+                if (!ok) {
+                    if (a.err) atomicExch(a.err, 1u);
+                    *abort = 1u;
+                    // the copies already issued land before the CTA's shared memory goes away
+                    for (unsigned k2 = s > S ? s - S : 0u; k2 < s; ++k2) mbar_spin(full + k2 % S, (k2 / S) & 1u);
+                    break;
+                }
+                if (g >= a.total_items) break;
+            }
+        }
+        return;
+    }
+
+    if (warp > kChainConsumers) {
+        // ---- fold warps: warp 9 adds each row's (g) terms in block order and writes the row, warp 10 a pair's u
+        // terms; per item, while the consumers already compute the next item's terms in the other buffer
+        const bool gw = warp == kChainConsumers + 1;
+        pdl_wait();
+        for (unsigned n = 0;; ++n) {
+            const unsigned b = n & 1u;
+            if (!role_wait(tready + b, (n >> 1) & 1u, abort)) break;
+            const unsigned g = info[b];
+            if (g == kChainEnd) break;
+            const unsigned k = chain_pass_of(a, g);
+            const ChainPass &P = a.p[k];
+            const unsigned t = g - P.item0, R = P.wa.rt, lrow = t * R + lane, nb = P.cols / 32;
+            const unsigned TS = term_stride(P.wa.kc * P.wa.ct);
+            const float *ta = terms + size_t(2 * b) * tw, *tb = ta + tw;
+            const bool mine = lane < R && lrow < P.wa.rows;
+            if (!gw) {
+                if (P.pair) {
+                    if (lane < R) usum[32 * b + lane] = fold_row(tb, lane, TS, nb);
+                    fold_pair_sync();
+                }
+                continue;
+            }
+            const GemvMemberArgs &O = P.out;
+            const bool image = P.qout != nullptr;  // 32-row panels: this panel is block t of the next pass's x
+            float acc = 0.0f, val = 0.0f;
+            if (mine || image) acc = fold_row(ta, lane, TS, nb);
+            if (P.pair) fold_pair_sync();
+            if (mine || image) {
+                if (P.pair) val = fmul(silu_f32(acc), usum[32 * b + lane]);
+                else if (O.epi == EpiAdd) val = fadd(acc, __ldcg(O.res + lrow));
+                else val = acc;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tfree + b);  // the terms (and u sums) of this buffer are read
+            if (mine) O.y[lrow] = val;
+            if (image) write_image_block(P.qout, O.total_rows, t, mine ? val : 0.0f, lane, P.qout_act);
+            const unsigned end = min((t + 1) * R, P.wa.rows);
+            if (end == P.wa.rows) write_padding(O, end, lane);
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) red_release_gpu(done + k, 1u);
+        }
+        // the launch's last CTA leaves the counters at zero for the next launch (the fold warp finishes last)
+        if (gw && lane == 0) {
+            __threadfence();
+            if (atomicAdd(finished, 1u) == gridDim.x - 1) {
+                for (unsigned i = 0; i < kChainCounters; ++i) a.counters[i] = 0u;
+                __threadfence();
+            }
+        }
+        return;
+    }
+
+    // ---- consumers
+    pdl_wait();
+    int cur = -1;
+    unsigned s_base = 0;
+    for (unsigned n = 0;; ++n) {
+        const unsigned q = n % kChainQueue, b = n & 1u;
+        bool bad = false;
+        if (threadIdx.x == 0) bad = !role_wait(qfull + q, (n / kChainQueue) & 1u, abort);
+        if (consumers_any(bad || *abort)) {
+            if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1u);
+            *abort = 1u;
+            break;
+        }
+        const unsigned g = queue[q];
+        consumers_sync();
+        if (threadIdx.x == 0) mbar_arrive(qempty + q);
+        if (g == kChainEnd) {
+            // the fold warps' last buffer: none left (the buffer's previous item was folded first)
+            const bool ok = n < 2 || role_wait(tfree + b, ((n >> 1) - 1u) & 1u, abort);
+            if (threadIdx.x == 0) info[b] = kChainEnd;
+            __syncwarp();
+            if (lane == 0 && ok) mbar_arrive(tready + b);
+            break;
+        }
+        const unsigned k = chain_pass_of(a, g);
+        const ChainPass &P = a.p[k];
+        if (int(k) != cur) {
+            // every item of the previous pass is finished (its rows, its image) before this pass's x is read
+            bad = false;
+            if (k > 0 && threadIdx.x == 0) bad = !chain_wait_pass(done + (k - 1), chain_items(a, k - 1));
+            if (consumers_any(bad)) {
+                if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1u);
+                *abort = 1u;
+                break;
+            }
+            if (P.x_kind == 2) chain_copy_image(P, xq);
+            else chain_prepare_x(P, xq, red);
+            consumers_sync();
+            cur = int(k);
+        }
+        // this buffer's previous item (n - 2) has been folded
+        bool ok = n < 2 || role_wait(tfree + b, ((n >> 1) - 1u) & 1u, abort);
+        const XSmem xs{reinterpret_cast<const uint4 *>(xq), reinterpret_cast<const uint4 *>(xq + P.cols / 2),
+                       reinterpret_cast<const uint4 *>(xq + P.cols)};
+        float *ta = terms + size_t(2 * b) * tw, *tb = ta + tw;
+        if (ok) ok = chain_steps_any(P, xs, warp, lane, stages, a.stage_bytes, S, full, empty, s_base, ta, tb, abort);
+        if (!ok) {
+            if (lane == 0 && a.err) atomicExch(a.err, 1u);
+            *abort = 1u;
+        }
+        if (threadIdx.x == 0) info[b] = g;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tready + b);  // this warp's terms of the item are written
+        if (consumers_any(!ok)) break;
+        s_base += (P.wa.kc + chain_stage_steps(P.pair) - 1) / chain_stage_steps(P.pair);
+    }
+}
+
+bool plan_gemv_chain(ChainArgs &a, size_t &smem) {
+    unsigned stage = 0, tb = 0, cols = 0;
+    for (unsigned k = 0; k < a.n_passes; ++k) {
+        const ChainPass &P = a.p[k];
+        const unsigned sb = P.pair ? chain_pair_offset(P.wa.tile_bytes) + kChainPairSteps * P.wb.tile_bytes
+                                   : chain_stage_steps(0) * P.wa.tile_bytes;
+        stage = std::max(stage, sb);
+        tb = std::max(tb, P.wa.rt * term_stride(P.wa.kc * P.wa.ct) * 4u);
+        cols = std::max(cols, P.cols);
+    }
+    a.stage_bytes = unsigned(align128(stage));
+    a.term_bytes = unsigned(align128(tb));
+    a.ximg_bytes = unsigned(align128(qimage_bytes(cols)));
+    const size_t fixed = kChainBarBytes + a.ximg_bytes + 4 * size_t(a.term_bytes);
+    const size_t room = 227 * 1024 > fixed ? 227 * 1024 - fixed : 0;
+    // full + empty mbarriers per stage; the queue's and the term buffers' mbarriers, the queue, the item words and the
+    // abort word; the u sums at the end
+    const unsigned max_stages = (kChainBarBytes - 256 - 16 * kChainQueue - 32 - 4 * (kChainQueue + 3)) / 16;
+    a.n_stages = unsigned(std::min<size_t>(room / a.stage_bytes, max_stages));
+    smem = fixed + size_t(a.n_stages) * a.stage_bytes;
+    return a.n_stages >= 4;
+}
+
+cudaError_t launch_gemv_chain(const ChainArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kChainThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, a);
+}
+
 }  // namespace b200q

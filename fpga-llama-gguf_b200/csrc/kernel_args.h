@@ -124,6 +124,37 @@ struct GemvArgs {
     PeerWait pw;                  // rows of earlier sharded launches this pass reads
 };
 
+// A run of consecutive Q4_0 / Q8_0 GEMV passes executed by one persistent kernel (gemv_q8.cu, gemv_chain_kernel):
+// each pass a single matrix or a SwiGLU pair, its output a plain or residual-ADD row writer, its x from act (quantized
+// in the kernel), a deferred RMSNORM of act, or the quantized image the previous pass of the chain wrote.
+constexpr unsigned kMaxChainPasses = 16;
+struct ChainPass {
+    MatrixView wa, wb;            // wa: the matrix (a pair's g); wb: a pair's u (base null otherwise)
+    GemvMemberArgs out;           // the output member (a pair: the u member, epilogue SwiGLU)
+    unsigned fmt = 0;             // 2 Q4_0 or 8 Q8_0 (a pair's two matrices alike)
+    unsigned pair = 0;
+    unsigned cols = 0;
+    unsigned x_kind = 0;          // 0: quantize act x; 1: deferred RMSNORM of act x; 2: the image in qin
+    const float *x = nullptr;
+    const float *norm_w = nullptr;
+    float norm_eps = 0.0f;
+    unsigned norm_mode = 0;       // 8 | RMSNORM flags (x_kind 1)
+    const uint8_t *qin = nullptr; // x_kind 2: written by the previous pass
+    uint8_t *qout = nullptr;      // this pass's output, quantized for the next pass (32-row panels), or null
+    unsigned qout_act = 0;
+    unsigned item0 = 0;           // the pass's first item (row panel) in the chain's item numbering
+};
+struct ChainArgs {
+    ChainPass p[kMaxChainPasses];
+    unsigned n_passes = 0, total_items = 0;
+    // [0] the next item to take, [1] CTAs finished, [2 + k] items of pass k finished; zero at the launch, left zero
+    // by the launch's last CTA
+    unsigned *counters = nullptr;
+    unsigned *err = nullptr;      // set when a bounded wait runs out
+    unsigned n_stages = 0, stage_bytes = 0, term_bytes = 0, ximg_bytes = 0;
+};
+constexpr unsigned kChainCounters = 2 + kMaxChainPasses;
+
 // Quantize x (optionally through the RMSNORM arithmetic) to scratch: the same device code as the GEMV prologue.
 struct QuantArgs {
     const float *x = nullptr;

@@ -103,6 +103,9 @@ cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
 unsigned attn_chunk(unsigned kv_ctx, unsigned n_kv_head, unsigned sms);
 size_t attn_smem_bytes(unsigned n_head, unsigned n_kv_head, unsigned head_dim, unsigned chunk, unsigned max_chunks);
 cudaError_t launch_allreduce_peer(const CollArgs &a, cudaStream_t st, bool pdl);
+// the chain's shared-memory plan (stages, term buffers, x image); false when a pass does not fit
+bool plan_gemv_chain(ChainArgs &a, size_t &smem);
+cudaError_t launch_gemv_chain(const ChainArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
 cudaError_t launch_trace_stamp(unsigned long long *slot, cudaStream_t st);
 cudaError_t launch_trace_write(const unsigned long long *stamps, const uint32_t *tags, unsigned n_events,
                                float *log, cudaStream_t st);

@@ -220,16 +220,18 @@ B200Q_API unsigned b200q_graph_kernel_count(const b200q_graph *graph);
 
 /* ---- diagnostics: feature mask and runtime verification ------------------------------------------------------
  * Feature mask (reference: GGML_XRT_FEATURE_MASK, ggml-xrt.cpp:1294-1299). The environment variable
- * B200Q_FEATURE_MASK=<bits> (read at b200q_create) or b200q_set_feature_mask sets it; all bits set by default.
+ * B200Q_FEATURE_MASK=<bits> (read at b200q_create) or b200q_set_feature_mask sets it; by default all bits are set but
+ * bit 21 (B200Q_DEFAULT_FEATURE_MASK).
  *   bits 0..15: the reference feature word. A cleared bit hides that fused form from the feature probe (a zero-command
  *     b200q_run), so a list builder emits the plain command sequence instead; the weight-format and layout bits
  *     (0, 1, 2, 13) always stay. Where this library also fuses internally, the cleared bit turns that off too:
  *     bit 3 multi-output passes (each GEMV or SwiGLU pair of a group then runs as its own launch), bit 9 deferred
  *     RMSNORM in the GEMV prologue (the norm row is then stored at its command), bit 15 the DeltaNet step handing
  *     its ssm_out GEMV the quantized y.
- *   bits 16..20: this library's own fusions: 16 a GEMV pass handing the next pass its quantized x, 17 per-panel
+ *   bits 16..21: this library's own fusions: 16 a GEMV pass handing the next pass its quantized x, 17 per-panel
  *     sums of squares handed to the next deferred norm, 18 programmatic dependent launch, 19 runs of RMSNORM / ROPE
- *     in one launch, 20 the attention gate applied in the attention merge.
+ *     in one launch, 20 the attention gate applied in the attention merge, 21 runs of Q4_0 / Q8_0 GEMV passes
+ *     (single matrices or SwiGLU pairs, plain or residual-ADD writers) executed by one persistent kernel.
  * Every fused form gives the same values as its plain form, so results do not depend on the mask (bit for bit, but
  * for the deferred norm's FP64 sum of squares, which is added in a different fixed order when stored; both round to
  * the same FP32 scale unless the exact sum lies within ~1e-13, relative, of an FP32 rounding boundary). The mask is
@@ -242,6 +244,8 @@ B200Q_API unsigned b200q_graph_kernel_count(const b200q_graph *graph);
 #define B200Q_MASK_PDL (1u << 18)
 #define B200Q_MASK_ROW_OPS (1u << 19)
 #define B200Q_MASK_ATTN_GATE (1u << 20)
+#define B200Q_MASK_CHAINS (1u << 21) /* off by default: measured slower than the passes' own kernels */
+#define B200Q_DEFAULT_FEATURE_MASK (0xFFFFFFFFu & ~B200Q_MASK_CHAINS)
 B200Q_API int b200q_set_feature_mask(b200q_ctx *ctx, uint32_t mask);
 B200Q_API uint32_t b200q_feature_mask(const b200q_ctx *ctx);
 

@@ -4,7 +4,7 @@ verification (B200Q_VERIFY_CALLS / b200q_set_verify).
 Feature mask: every fused form of this library gives the same values as its plain form, so a decode with any of the
 executor's fusions switched off (multi-output passes, deferred norms in the GEMV prologue, the DeltaNet y image, the
 pass-to-pass x image, the norm partials, programmatic dependent launch, fused norm / RoPE launches, the fused
-attention gate; one at a time and all at once) gives bit-identical tokens, logits, act and states. The feature probe
+attention gate, persistent GEMV chains; one at a time and all at once) gives bit-identical tokens, logits, act and states. The feature probe
 reports the masked word, the format bits kept.
 
 Runtime verification: a checker built on the CPU oracle sees the first n lists (direct runs and graph replays) with
@@ -52,22 +52,23 @@ def test_feature_probe_reports_the_mask(ctx, b2):
     finally:
         ctx.set_feature_mask(0xFFFFFFFF)
     assert ctx.feature_mask == 0xFFFFFFFF
+    ctx.set_feature_mask(b2.DEFAULT_FEATURE_MASK)
 
 
 def test_decode_is_bit_identical_under_every_feature_mask(b2):
     import fpga_llama_gguf_b200.decode as D
     m = D.HybridDecoder(_shape(D), seed=6)
-    base = _decode(b2, D, m, 0xFFFFFFFF)
+    base = _decode(b2, D, m, 0xFFFFFFFF)  # every fusion on, the persistent chains too
     masks = {"groups": b2.MASK_GROUPS, "defer_norm": b2.MASK_DEFER_NORM, "gdn_out": b2.MASK_GDN_OUT,
              "x_image": b2.MASK_X_IMAGE, "norm_partials": b2.MASK_NORM_PARTIALS, "pdl": b2.MASK_PDL,
-             "row_ops": b2.MASK_ROW_OPS, "attn_gate": b2.MASK_ATTN_GATE}
+             "row_ops": b2.MASK_ROW_OPS, "attn_gate": b2.MASK_ATTN_GATE, "chains": b2.MASK_CHAINS}
     masks["all"] = sum(masks.values())
     for name, bits in masks.items():
         got = _decode(b2, D, m, ~bits & 0xFFFFFFFF)
         assert got[0] == base[0], name
         assert np.array_equal(got[1].view(np.uint32), base[1].view(np.uint32)), name
         assert np.array_equal(got[2].view(np.uint32), base[2].view(np.uint32)), name
-        if name in ("groups", "defer_norm", "row_ops", "attn_gate", "all"):
+        if name in ("groups", "defer_norm", "row_ops", "attn_gate", "chains", "all"):
             assert got[3] > base[3], name  # the plain forms take more launches
 
 
