@@ -139,10 +139,9 @@ struct b200q_ctx {
     // explicit (tensor-parallel) lists: the caller's own slices, exchanges only by ALLREDUCE / ALLGATHER commands;
     // with coll_peer, ALLREDUCE runs as the peer kernel (coll.cu) on these buffers, one slot per ALLREDUCE of a list
     bool explicit_comm = false, coll_peer = false;
-    float *coll_recv = nullptr;
-    unsigned *coll_flags = nullptr;
-    float *peer_coll_recv[kMaxPeers] = {};
-    unsigned *peer_coll_flags[kMaxPeers] = {};
+    uint2 *coll_recv = nullptr;          // kCollSlots x [2][world][kCollMaxN] words, mapped into every peer
+    unsigned *coll_flags = nullptr;      // kCollSlots x kCollMaxCtas launch counters (this rank only)
+    uint2 *peer_coll_recv[kMaxPeers] = {};
     unsigned coll_slot_next = 0;
     unsigned *chain_counters = nullptr;  // kMaxChains x kChainCounters words, zero between launches
     unsigned chain_next = 0;             // the next chain's counter block in the list being executed
@@ -701,12 +700,10 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
             a.n = unsigned(n);
             a.world = unsigned(c->world);
             a.rank = unsigned(c->rank);
-            const size_t rs = size_t(2) * c->world * kCollMaxN, fs = size_t(c->world) * kCollMaxCtas;
-            for (int r = 0; r < c->world; ++r) {
+            const size_t rs = size_t(2) * c->world * kCollMaxN;
+            for (int r = 0; r < c->world; ++r)
                 a.recv[r] = (r == c->rank ? c->coll_recv : c->peer_coll_recv[r]) + slot * rs;
-                a.flags[r] = (r == c->rank ? c->coll_flags : c->peer_coll_flags[r]) + slot * fs;
-            }
-            a.flag_local = a.flags[c->rank];
+            a.flag_local = c->coll_flags + size_t(slot) * kCollMaxCtas;
             a.err = c->dstatus + 1;
             CUDA_TRY(c, launch_allreduce_peer(a, c->stream, c->pdl));
         } else {
@@ -1130,7 +1127,6 @@ void b200q_destroy(b200q_ctx *c) {
         if (c->peer_act[p]) cudaIpcCloseMemHandle(c->peer_act[p]);
         if (c->peer_sync[p]) cudaIpcCloseMemHandle(c->peer_sync[p]);
         if (c->peer_coll_recv[p]) cudaIpcCloseMemHandle(c->peer_coll_recv[p]);
-        if (c->peer_coll_flags[p]) cudaIpcCloseMemHandle(c->peer_coll_flags[p]);
     }
     cudaFree(c->sync);
     cudaFree(c->coll_recv);
@@ -1662,24 +1658,26 @@ int setup_peers(b200q_ctx *c) {
     return 0;
 }
 
-// Receive buffers and flag words of the peer ALLREDUCE (coll.cu), mapped into every peer (CUDA IPC; the handles
-// travel through one NCCL all-gather).
+// Receive buffers of the peer ALLREDUCE (coll.cu), mapped into every peer (CUDA IPC; the handles travel through one
+// NCCL all-gather), and this rank's launch counters.
 int setup_coll_peers(b200q_ctx *c) {
-    const size_t recv_bytes = size_t(kCollSlots) * 2 * c->world * kCollMaxN * sizeof(float);
-    const size_t flag_bytes = size_t(kCollSlots) * c->world * kCollMaxCtas * sizeof(unsigned);
+    const size_t recv_bytes = size_t(kCollSlots) * 2 * c->world * kCollMaxN * sizeof(uint2);
+    const size_t flag_bytes = size_t(kCollSlots) * kCollMaxCtas * sizeof(unsigned);
     CUDA_TRY(c, cudaMalloc(&c->coll_recv, recv_bytes));
     CUDA_TRY(c, cudaMalloc(&c->coll_flags, flag_bytes));
-    CUDA_TRY(c, cudaMemset(c->coll_recv, 0, recv_bytes));
-    CUDA_TRY(c, cudaMemset(c->coll_flags, 0, flag_bytes));
-    cudaIpcMemHandle_t mine[2];
-    CUDA_TRY(c, cudaIpcGetMemHandle(&mine[0], c->coll_recv));
-    CUDA_TRY(c, cudaIpcGetMemHandle(&mine[1], c->coll_flags));
+    // zeroed in stream order before the handle exchange: a peer's all-gather completes only after this rank's ran,
+    // so no peer writes into these words before they are zero (launch number 0 never matches a launch)
+    CUDA_TRY(c, cudaMemsetAsync(c->coll_recv, 0, recv_bytes, c->stream));
+    CUDA_TRY(c, cudaMemsetAsync(c->coll_flags, 0, flag_bytes, c->stream));
+    cudaIpcMemHandle_t mine;
+    CUDA_TRY(c, cudaIpcGetMemHandle(&mine, c->coll_recv));
+    static_assert(sizeof(mine) % sizeof(float) == 0, "handles travel as floats");
     const size_t n = sizeof(mine) / (sizeof(float));
     float *dev = nullptr;
     CUDA_TRY(c, cudaMalloc(&dev, sizeof(mine) * (size_t(c->world) + 1)));
-    CUDA_TRY(c, cudaMemcpy(dev, mine, sizeof(mine), cudaMemcpyHostToDevice));
+    CUDA_TRY(c, cudaMemcpy(dev, &mine, sizeof(mine), cudaMemcpyHostToDevice));
     const int r = g_nccl.all_gather(dev, dev + n, n, kNcclFloat32, c->comm, c->stream);
-    std::vector<cudaIpcMemHandle_t> all(2 * size_t(c->world));
+    std::vector<cudaIpcMemHandle_t> all(size_t(c->world));
     cudaError_t e = cudaStreamSynchronize(c->stream);
     if (e == cudaSuccess) e = cudaMemcpy(all.data(), dev + n, sizeof(mine) * size_t(c->world), cudaMemcpyDeviceToHost);
     cudaFree(dev);
@@ -1687,13 +1685,10 @@ int setup_coll_peers(b200q_ctx *c) {
     if (e != cudaSuccess) return set_err(c, B200Q_ERR_CUDA, "IPC handle exchange: %s", cudaGetErrorString(e));
     for (int p = 0; p < c->world; ++p) {
         if (p == c->rank) continue;
-        void *pr = nullptr, *pf = nullptr;
-        CUDA_TRY(c, cudaIpcOpenMemHandle(&pr, all[2 * size_t(p)], cudaIpcMemLazyEnablePeerAccess));
-        CUDA_TRY(c, cudaIpcOpenMemHandle(&pf, all[2 * size_t(p) + 1], cudaIpcMemLazyEnablePeerAccess));
-        c->peer_coll_recv[p] = static_cast<float *>(pr);
-        c->peer_coll_flags[p] = static_cast<unsigned *>(pf);
+        void *pr = nullptr;
+        CUDA_TRY(c, cudaIpcOpenMemHandle(&pr, all[size_t(p)], cudaIpcMemLazyEnablePeerAccess));
+        c->peer_coll_recv[p] = static_cast<uint2 *>(pr);
     }
-    // every rank's buffers are mapped before any rank pushes
     CUDA_TRY(c, cudaDeviceSynchronize());
     c->coll_peer = true;
     return 0;
@@ -1728,13 +1723,16 @@ int b200q_comm_init_ex(b200q_ctx *c, int world, int rank, const uint8_t id[B200Q
     c->world = world;
     c->rank = rank;
     c->explicit_comm = (flags & B200Q_COMM_EXPLICIT) != 0;
-    // outputs exchanged by peer stores (B200Q_PEER=1) or by an NCCL all-gather per sharded member (default: at the
-    // sizes measured so far the peer path's per-pass synchronisation costs more than the all-gather); explicit lists:
-    // ALLREDUCE by the peer kernel (B200Q_PEER=1) or NCCL
+    // row-sharded lists: outputs exchanged by peer stores (B200Q_PEER=1) or by an NCCL all-gather per sharded member
+    // (default: the peer path's per-pass synchronisation costs more than the all-gather); explicit lists: ALLREDUCE by
+    // the peer kernel (default: 3.8 us per 2560 floats on 2 GPUs against 10.3 us for ncclAllReduce in a graph) or by
+    // NCCL (B200Q_PEER=0)
     const char *pe = getenv("B200Q_PEER");
-    const bool peer = world <= int(kMaxPeers) && pe && pe[0] == '1';
-    if (c->explicit_comm) return peer ? setup_coll_peers(c) : 0;
-    if (peer) return setup_peers(c);
+    if (c->explicit_comm) {
+        const bool peer = world <= int(kMaxPeers) && !(pe && pe[0] == '0');
+        return peer ? setup_coll_peers(c) : 0;
+    }
+    if (world <= int(kMaxPeers) && pe && pe[0] == '1') return setup_peers(c);
     return 0;
 }
 

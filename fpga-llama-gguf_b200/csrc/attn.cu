@@ -60,17 +60,37 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     const AttnSmem S = attn_smem(attn_sm, G, hd, C, a.max_chunks);
     const unsigned chunk = blockIdx.x, kvh = blockIdx.y, c0 = chunk * C;
     const size_t row0 = size_t(kvh) * a.kv_ctx + c0;  // first cache row of the chunk
-    // The chunk's rows come in before the wait on the previous kernel: only ATTN itself writes the cache
-    // (the row at pos, which this CTA replaces after the copy), so the copy overlaps the previous kernel's end.
+    // The cache rows the token attends to in this chunk, [c0, pos) (row pos is the token's own k / v), come in before
+    // the wait on the previous kernel: only ATTN itself writes the cache (the row at pos, which this CTA replaces
+    // after the copy), so the copy overlaps the previous kernel's end. The position is read before the wait too; it
+    // is read again after the wait, and in the rare case that it changed in between (an earlier kernel of the stream
+    // wrote it), the rows are copied again for the position read after the wait. Any value read early gives a copy
+    // inside the slot; rows past pos are never copied, so the bytes follow the position, not the slot length.
+    auto rows_for = [&](unsigned p) -> unsigned {
+        if (p >= a.kv_ctx || p <= c0) return 0u;
+        const unsigned r = p - c0;
+        return r < C ? r : C;  // (c0 + C <= kv_ctx whenever p - c0 >= C, as p < kv_ctx)
+    };
+    unsigned copied = 0;  // thread 0: rows of the early copy (phase 0 of bar when non-zero)
+    const uint64_t pol = evict_first_policy();
+    auto issue = [&](unsigned rows) {
+        const unsigned bytes = rows * hd * 2;
+        mbar_expect_tx(&bar, 2 * bytes);
+        bulk_copy(S.k, a.kcache + row0 * hd, bytes, &bar, pol);
+        bulk_copy(S.v, a.vcache + row0 * hd, bytes, &bar, pol);
+    };
+    // thread 0: bounded wait for phase `parity`; after a timeout one more bounded wait, so that a copy still in
+    // flight lands before the CTA exits
+    auto land = [&](unsigned parity) -> bool {
+        if (mbar_wait(&bar, parity)) return true;
+        mbar_wait(&bar, parity);
+        return false;
+    };
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         mbar_fence_init();
-        const unsigned rows = a.kv_ctx - c0 < C ? a.kv_ctx - c0 : C;  // the slot's last chunk may be shorter
-        const unsigned bytes = rows * hd * 2;
-        mbar_expect_tx(&bar, 2 * bytes);
-        const uint64_t pol = evict_first_policy();
-        bulk_copy(S.k, a.kcache + row0 * hd, bytes, &bar, pol);
-        bulk_copy(S.v, a.vcache + row0 * hd, bytes, &bar, pol);
+        copied = rows_for(__float_as_uint(*reinterpret_cast<const volatile float *>(a.pos)));
+        if (copied) issue(copied);
     }
     pdl_wait();
     pdl_launch_dependents();  // the next kernel may stage its weights while this one runs
@@ -81,18 +101,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     if (!active) {  // outside the slot, or a chunk past pos: let the copies land, then leave
         if (pos >= a.kv_ctx && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status)
             atomicOr(a.status, 2u);
-        if (threadIdx.x == 0 && !mbar_wait(&bar, 0) && a.err) atomicExch(a.err, 1u);
+        if (threadIdx.x == 0 && copied && !land(0u) && a.err) atomicExch(a.err, 1u);
         return;
     }
     const unsigned n_chunks = (T + C - 1) / C, cn = T - c0 < C ? T - c0 : C;
     const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     for (unsigned e = threadIdx.x; e < G * hd; e += kAttnThreads) S.q[e] = a.q[size_t(kvh) * G * hd + e];
     if (threadIdx.x == 0) {
-        ok_s = mbar_wait(&bar, 0);
-        if (!ok_s) {
-            if (a.err) atomicExch(a.err, 1u);
-            mbar_wait(&bar, 0);  // let the copies land before the CTA exits
+        const unsigned need = rows_for(pos);
+        ok_s = copied == 0 || land(0u);
+        if (ok_s && need > copied) {  // the position changed after the early read: copy its rows again
+            issue(need);
+            ok_s = land(copied ? 1u : 0u);
         }
+        if (!ok_s && a.err) atomicExch(a.err, 1u);
     }
     __syncthreads();
     if (!ok_s) return;

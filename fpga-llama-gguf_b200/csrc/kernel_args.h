@@ -2,6 +2,7 @@
 // and sizes, passed by value as kernel parameters.
 #pragma once
 #include <cstdint>
+#include <vector_types.h>
 
 namespace b200q {
 
@@ -61,15 +62,15 @@ struct PeerWait {
 };
 
 // ALLREDUCE of explicit lists over NVLink peer memory (coll.cu): one slot per ALLREDUCE of a list; per slot and rank
-// a receive buffer [2 parities][world][kCollMaxN] floats and flag words [world][kCollMaxCtas]; a CTA per chunk.
+// a receive buffer [2 parities][world][kCollMaxN] 8-byte words {value, launch number}, and per slot this rank's launch
+// counters, one per CTA (a CTA per chunk of kCollChunk values).
 constexpr unsigned kCollMaxN = 4096, kCollChunk = 512, kCollMaxCtas = kCollMaxN / kCollChunk, kCollSlots = 64;
 struct CollArgs {
     const float *x = nullptr;
     float *y = nullptr;
     unsigned n = 0;                      // floats, a multiple of 16, at most kCollMaxN
-    float *recv[kMaxPeers] = {};         // per rank: that rank's receive buffer of the slot (this rank's own included)
-    unsigned *flags[kMaxPeers] = {};     // per rank: that rank's flag words of the slot
-    unsigned *flag_local = nullptr;      // this rank's flag words of the slot (flags[rank])
+    uint2 *recv[kMaxPeers] = {};         // per rank: that rank's receive buffer of the slot (this rank's own included)
+    unsigned *flag_local = nullptr;      // this rank's launch counters of the slot, one per CTA
     unsigned world = 1, rank = 0;
     unsigned *err = nullptr;             // set when a bounded wait runs out
 };

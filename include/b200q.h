@@ -398,9 +398,11 @@ B200Q_API int b200q_comm_unique_id(uint8_t id[B200Q_UNIQUE_ID_BYTES]);
 B200Q_API int b200q_comm_init(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES]);
 /* As b200q_comm_init; flags B200Q_COMM_EXPLICIT: the caller builds each rank's own lists (tensor parallel: its own
  * row or column slices of the matrices, uploaded as they are, and ALLREDUCE / ALLGATHER commands where partial
- * results meet). Uploads then keep all rows and no pass gathers anything by itself. The collectives run on NCCL, or
- * with the environment variable B200Q_PEER=1 as one kernel that pushes this rank's part into every peer's receive
- * buffer over NVLink (CUDA IPC mappings made here) and sums the parts in rank order after bounded flag waits. */
+ * results meet). Uploads then keep all rows and no pass gathers anything by itself. ALLREDUCE runs as one kernel that
+ * writes this rank's part into every peer's receive buffer over NVLink (CUDA IPC mappings made here; each value with
+ * its launch number in one 8-byte word, so no fence or flag is needed) and adds the parts in rank order after bounded
+ * waits (up to 8 ranks and 4096 floats; larger ones, ALLGATHER, and everything with the environment variable
+ * B200Q_PEER=0 run on NCCL). */
 #define B200Q_COMM_EXPLICIT 1u
 B200Q_API int b200q_comm_init_ex(b200q_ctx *ctx, int world, int rank, const uint8_t id[B200Q_UNIQUE_ID_BYTES],
                                  unsigned flags);
