@@ -312,6 +312,36 @@ def q4_0_bench(b2, torch, synth, dev: int, world: int) -> dict:
             "l2": f"{n} distinct copies ({n * w.nbytes >> 20} MiB) per list"}
 
 
+def batch_bench(b2, torch, synth, dev: int, world: int) -> dict:
+    """The GEMV_BATCH extension (the reference roadmap's batch path: one weight read for M activation rows) on the
+    configs[0] matrix, Q4_0 [9216 x 2560]: one list of 30 distinct copies (> 3x L2), each a GEMV_BATCH of M rows;
+    per M the time per command, the weight bytes per second and the activation rows per second (M / time)."""
+    if world > 1:
+        return {"note": "measured on one GPU only"}
+    peak, peak_kind = measured_peak()
+    rows, cols, n = 9216, H, 30
+    ctx = b2.Context(device=dev, weight_bytes=n * (b2.weight_device_bytes(rows, cols, b2.Q4_0) + (1 << 20)),
+                     act_floats=1 << 20)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+    r = synth.rng(0, 1)
+    w = synth.q4_0(r, rows, cols)
+    xs = np.concatenate([synth.activation(r, cols) for _ in range(b2.BATCH_MAX)])
+    ctx.write(0, xs)
+    hs = [ctx.upload(w, rows, cols, b2.Q4_0) for _ in range(n)]
+    out = {"workload": "GEMV_BATCH of Q4_0 [9216x2560] (configs[0] matrix), M activation rows per weight read",
+           "copies": n, "peak_kind": peak_kind}
+    y0 = b2.BATCH_MAX * cols
+    for m in (1, 2, 4, 8):
+        cl = b2.cmd_list(*[b2.gemv_batch(b2.Q4_0, rows, cols, h, 0, y0 + (i % 2) * m * rows, m) for i, h in enumerate(hs)])
+        ms, kernels = timed_graph(ctx, torch, stream, cl, 30)
+        us = ms * 1e3 / n
+        gbs = w.nbytes / (us * 1e-6) / 1e9
+        out[f"m{m}"] = {"us_per_command": round(us, 3), "weight_gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+                        "rows_per_s": round(m / (us * 1e-6), 1), "kernels_per_command": kernels / n}
+    ctx.close()
+    return out
+
+
 def gdn_bench(b2, torch, synth, dev: int, world: int, steps: int = 128) -> dict:
     """128 sequential Gated DeltaNet decode steps (hidden 2560, 16 heads, d_k = d_v = 128): the causal
     conv1d (k = 4) over the qkv projection with its 3-token state, the step with L2-normalized q / k, the gates from
@@ -675,10 +705,11 @@ def main():
         g.close()
     ctx.close()
 
-    q40 = gdn = {}
+    q40 = gdn = batch = {}
     if not args.no_extras:
         q40 = q4_0_bench(b2, torch, synth, dev, world)
         gdn = gdn_bench(b2, torch, synth, dev, world)
+        batch = batch_bench(b2, torch, synth, dev, world)
     decode = run_decodes()
     kquant = kquant_bench(b2, torch, synth, dev, world, max_over_ranks, barrier) if not args.no_kquant else {}
     clk.__exit__(None, None, None)
@@ -697,7 +728,7 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": DATA, "config": config,
                 "frac_of_peak": round(value / (peak * world), 4), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": launches, "clocks": clocks, "q4_0": q40, "kquant": kquant, "gdn_step": gdn,
+                "gpu_launches": launches, "clocks": clocks, "q4_0": q40, "kquant": kquant, "gdn_step": gdn, "gemv_batch": batch,
                 "decode": decode}
         print(json.dumps(line), flush=True)
     return 0

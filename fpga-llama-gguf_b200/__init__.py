@@ -26,13 +26,15 @@ MAX_CMDS = 128
 OP_GEMV, OP_RMSNORM, OP_ADD, OP_SILU_MUL, OP_MUL, OP_UNARY, OP_GDN, OP_CONV = 1, 2, 3, 4, 5, 6, 7, 8
 OP_STATE_LOAD, OP_ROPE, OP_TRACE = 9, 10, 11
 OP_ATTN, OP_ARGMAX, OP_GET_ROW, OP_ALLREDUCE, OP_ALLGATHER = 12, 13, 14, 15, 16  # extensions of this library
+OP_GEMV_BATCH = 17
+BATCH_MAX = 8  # activation rows of one GEMV_BATCH
 GEMV_SWIGLU, GEMV_CONV, GEMV_ADD = 0x100, 0x200, 0x400
 GDN_WITH_GEMV, GDN_L2_QK, GDN_GATED, GDN_GATES, GDN_WITH_OUT = 1, 2, 4, 8, 16
 NORM_L2, NORM_NO_WEIGHT, NORM_DEFER = 1, 2, 4
 UNARY_SILU, UNARY_SIGMOID, UNARY_SOFTPLUS, UNARY_COPY = 1, 2, 3, 4
 SILU_MUL_SIGMOID = 1
 Q4_0, Q4_1, Q8_0, Q5_K, Q6_K = 2, 3, 8, 13, 14
-FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53001F)
+FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53003F)
 COMM_EXPLICIT = 1
 UPLOAD_REPLICATE = 1
 UPLOAD_SRC_Q4_0X8 = 2
@@ -142,6 +144,14 @@ def allreduce(n: int, x_off: int, y_off: int) -> np.ndarray:
 def allgather(n: int, x_off: int, y_off: int) -> np.ndarray:
     """ALLGATHER extension: y[r n .. r n + n) = x of rank r (one rank: y = x)."""
     return cmd(OP_ALLGATHER, n, x_off, y_off)
+
+
+def gemv_batch(fmt: int, rows: int, cols: int, w_off: int, x_off: int, y_off: int, batch: int,
+               flags: int = 0) -> np.ndarray:
+    """GEMV_BATCH extension: y_m = W x_m (flags GEMV_ADD: + y_m) for m < batch <= BATCH_MAX; x rows `cols` floats
+    apart from x_off, y rows round16(rows) floats apart from y_off; the weights are read once for all rows."""
+    return cmd(OP_GEMV_BATCH, fmt | flags | ((batch - 1) << 16), rows, cols, w_off & 0xFFFFFFFF, w_off >> 32,
+               x_off, y_off)
 
 
 # ---- library ---------------------------------------------------------------------------------------------------

@@ -626,6 +626,8 @@ int exec_gdn(b200q_ctx *c, const Pass &p, const ImageLink &nsq_link) {
     return 0;
 }
 
+static_assert(kBatchRows == kBatchMax, "the planner's and the kernel's GEMV_BATCH row limits agree");
+
 int exec_ext(b200q_ctx *c, const Pass &p) {
     const uint32_t *cmd = p.cmd[0];
     float *A = c->act;
@@ -681,6 +683,26 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         const float *idx = snap_if(c, A + cmd[5], 1, wr, nullptr, rc);
         if (rc) return rc;
         CUDA_TRY(c, launch_get_row(view_of(c, *w), cmd[2], idx, y, c->dstatus, take_wait(c), c->stream, c->pdl));
+    } else if (p.op == 17) {
+        const WeightInfo *w = find_w(c, uint64_t(cmd[4]) | (uint64_t(cmd[5]) << 32));
+        if (!w) return set_err(c, B200Q_ERR_ARG, "GEMV_BATCH: unknown weight");
+        if (c->world > 1 && !c->explicit_comm)
+            return set_err(c, B200Q_ERR_ARG, "GEMV_BATCH: not in a row-sharded context (its matrices hold a row slice)");
+        BatchArgs a;
+        a.w = view_of(c, *w);
+        a.cols = cmd[3];
+        a.batch = ((cmd[1] >> 16) & 0xffu) + 1u;
+        a.act = (cmd[1] & 0xffu) == 3u ? 1u : 0u;
+        a.x = A + cmd[6];
+        a.y = A + cmd[7];
+        a.ystride = (cmd[2] + 15u) & ~15u;
+        a.add = (cmd[1] & B200Q_GEMV_ADD) != 0;
+        a.err = c->dstatus + 1;
+        const unsigned per = gemv_batch_rows_per_launch(a.w, a.cols);
+        if (per == 0) return set_err(c, B200Q_ERR_ARG, "GEMV_BATCH: the matrix's panels do not fit shared memory");
+        if ((rc = flush_wait(c))) return rc;  // the kernel's producer warp runs apart: no in-kernel peer wait
+        CUDA_TRY(c, launch_gemv_batch(a, unsigned(c->sms), c->stream, c->pdl));
+        c->launches += (a.batch + per - 1) / per - 1;  // launches past the first (counted below)
     } else if (p.op == 15 || p.op == 16) {
         const size_t n = cmd[1];
         const float *x = A + cmd[2];

@@ -1243,4 +1243,304 @@ cudaError_t launch_gemv_chain(const ChainArgs &a, unsigned grid, size_t smem, cu
     return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, a);
 }
 
+
+// ==== GEMV_BATCH: y_m = W x_m for up to kBatchMax activation rows on one read of the weights =========================
+// The batch path of the reference's roadmap (docs/ROADMAP.md:80-96, P2: one weight word for M input vectors), for
+// speculative-decode checks and several sequences per pass. One launch, 8 consumer warps + 1 producer warp per CTA;
+// CTAs take the matrix's panels (P rows x all blocks) as gemv_q8_kernel does:
+//   producer   one bulk copy per round of 16 consecutive steps (tiles) of the CTA's panels into a ring of shared-memory
+//              stages (full / empty mbarriers, bounded waits); the first stages are issued before the wait on the
+//              previous kernel, as the weights never change within a list;
+//   consumers  after the wait, quantize the activation rows into shared-memory images (one thread per 32-value
+//              block, the arithmetic of the GEMV pass's quantizer), then per round: lane = unit, two steps per warp,
+//              the unit's exact integer block dot with the same block of every row and the FP32 block term
+//              float(sumi) * (d_w * d_x) into the round's term buffer; one barrier; then one thread per (activation
+//              row, panel row) adds the round's terms of its row in block order to its running sum (from 0 per panel).
+// Every output row has the bits of the single GEMV of its activation row: the same terms (block_term), added in the
+// same order (gemvq_ref.h:248-262). Roofline: HBM bandwidth (the weights once per launch); every CTA quantizes the
+// rows itself (batch x cols x 4 bytes from L2). When the images, term buffers and a ring of two stages do not fit
+// one CTA's shared memory, the host splits the rows over several launches (each reads the weights once).
+
+// One 32-value block of an activation row quantized to Q8_0 / Q8_1 by one thread from registers: the arithmetic of
+// quant_block_q80 (gemvq_ref.h:196-245), the image words of an XBlock (values 0..15, 16..31, {d, s, sum of q, 0}).
+__device__ __forceinline__ void batch_quant_block(const float *x32, bool q81, uint4 &q0, uint4 &q1, uint4 &meta) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = reinterpret_cast<const float4 *>(x32)[i];
+        v[4 * i] = f.x;
+        v[4 * i + 1] = f.y;
+        v[4 * i + 2] = f.z;
+        v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    const float sc = fdiv(amax, 127.0f);
+    const float id = sc != 0.0f ? fdiv(1.0f, sc) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int q = int(roundf(fmul(v[4 * k + e], id)));
+            sum += q;
+            word |= uint32_t(q & 0xff) << (8 * e);
+        }
+        w[k] = word;
+    }
+    q0 = make_uint4(w[0], w[1], w[2], w[3]);
+    q1 = make_uint4(w[4], w[5], w[6], w[7]);
+    const float d = half_bits_to_float(float_to_half_bits(sc));
+    const float s8 = q81 ? half_bits_to_float(float_to_half_bits(fmul(float(sum), sc))) : 0.0f;
+    meta = make_uint4(__float_as_uint(d), __float_as_uint(s8), uint32_t(sum), 0u);
+}
+
+constexpr unsigned kBatchChunk = 16;  // steps per round (one ring stage): two per consumer warp
+constexpr unsigned kBatchThreads = kPanelThreads + 32;  // 8 consumer warps + the producer warp
+constexpr unsigned kBatchBarBytes = 256;
+
+__host__ __device__ inline size_t batch_img_smem(unsigned cols, unsigned mn) {
+    return align128(size_t(mn) * (cols / 32) * kBatchImgBlockBytes);
+}
+// Term buffer of one round, per activation row: the round's blocks (kBatchChunk steps x C) x P rows, row fastest (a
+// step's 32 stores are 32 consecutive words), plus P words of padding so that the P-row groups of the activation rows
+// a warp folds at once start in different banks.
+__host__ __device__ inline unsigned batch_row_stride(unsigned p) { return kBatchChunk * 32 + p; }
+__host__ __device__ inline size_t batch_term_smem(const MatrixView &w, unsigned mn) {
+    return align128(2 * size_t(mn) * batch_row_stride(w.rt) * 4);  // two rounds in flight
+}
+__host__ __device__ inline size_t batch_stage_bytes(const MatrixView &w) {
+    return align128(size_t(kBatchChunk) * w.tile_bytes);
+}
+__host__ __device__ inline size_t batch_fixed_smem(const MatrixView &w, unsigned cols, unsigned mn) {
+    return kBatchBarBytes + batch_img_smem(cols, mn) + batch_term_smem(w, mn);
+}
+
+template <unsigned FMT>
+__global__ void __launch_bounds__(kBatchThreads) gemv_batch_kernel(const BatchArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const MatrixView &W = a.w;
+    const unsigned mn = a.mn, nb = a.cols / 32, P = W.rt, C = W.ct, KC = W.kc, NS = a.n_stages;
+    const unsigned rs = batch_row_stride(P);
+    const unsigned rounds = (KC + kBatchChunk - 1) / kBatchChunk;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem), *empty = full + NS;
+    uint8_t *img = smem + kBatchBarBytes;
+    float *terms = reinterpret_cast<float *>(img + batch_img_smem(a.cols, mn));
+    uint8_t *ring = reinterpret_cast<uint8_t *>(terms) + batch_term_smem(W, mn);
+    const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    // the CTA's work: rounds of its panels blockIdx.x, blockIdx.x + gridDim.x, ..., in order
+    const unsigned my_panels = blockIdx.x < W.n_rt ? (W.n_rt - blockIdx.x + gridDim.x - 1) / gridDim.x : 0u;
+    const unsigned items = my_panels * rounds;
+    if (threadIdx.x == kPanelThreads) {
+        for (unsigned s = 0; s < NS; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kPanelWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (warp == kPanelWarps) {
+        // ---- producer: one bulk copy per round (its steps are consecutive tiles of the panel). The weights never
+        // change within a list, so the first NS rounds are issued before the wait on the quantizer.
+        if (lane != 0) return;
+        const uint64_t pol = evict_first_policy();
+        auto issue = [&](unsigned it) {
+            const unsigned pnl = blockIdx.x + (it / rounds) * gridDim.x, k0 = (it % rounds) * kBatchChunk;
+            const unsigned bytes = min(kBatchChunk, KC - k0) * W.tile_bytes;
+            const unsigned s = it % NS;
+            mbar_expect_tx(full + s, bytes);
+            bulk_copy(ring + size_t(s) * a.stage_bytes, W.base + (size_t(pnl) * KC + k0) * W.tile_bytes, bytes,
+                      full + s, pol);
+        };
+        unsigned it = 0;
+        for (; it < items && it < NS; ++it) issue(it);
+        pdl_wait();
+        pdl_launch_dependents();
+        bool ok = true;
+        for (; it < items; ++it) {
+            // stage it % NS was filled for item it - NS; its consumers release it once per use
+            if (!mbar_wait(empty + it % NS, ((it / NS) - 1) & 1u)) {
+                ok = false;
+                break;
+            }
+            issue(it);
+        }
+        if (!ok) {
+            if (a.err) atomicExch(a.err, 1u);
+            // copies still in flight land before the CTA exits (bounded)
+            for (unsigned j = it > NS ? it - NS : 0u; j < it; ++j) mbar_wait(full + j % NS, (j / NS) & 1u);
+        }
+        return;
+    }
+    // ---- consumers (warps 0..7): the rows' images, quantized once per CTA while the ring fills
+    pdl_wait();
+    pdl_launch_dependents();
+    for (unsigned i = threadIdx.x; i < mn * nb; i += kPanelThreads) {
+        const unsigned m = i / nb, b = i % nb;
+        uint4 q0, q1, meta;
+        batch_quant_block(a.x + size_t(a.m0 + m) * a.cols + size_t(b) * 32, a.act == 1, q0, q1, meta);
+        uint4 *im = reinterpret_cast<uint4 *>(img + (size_t(m) * nb + b) * kBatchImgBlockBytes);
+        im[0] = q0;
+        im[1] = q1;
+        im[2] = meta;
+    }
+    consumers_sync();
+    // fold ownership: thread t < mn * P adds the terms of (activation row t / P, panel row t % P), in block order
+    const bool owner = threadIdx.x < mn * P;
+    const unsigned om = owner ? threadIdx.x / P : 0u, orow = threadIdx.x % P;
+    const unsigned r_in = lane / C, b_in = lane % C;  // the lane's unit: panel row, block within the step
+    float acc = 0.0f;
+    bool failed = false;
+    for (unsigned it = 0; it < items; ++it) {
+        const unsigned pnl = blockIdx.x + (it / rounds) * gridDim.x, rd = it % rounds, k0 = rd * kBatchChunk;
+        const unsigned s = it % NS;
+        if (rd == 0) acc = 0.0f;
+        const bool landed = mbar_wait(full + s, (it / NS) & 1u);
+        float *tb = terms + size_t(it & 1u) * mn * rs;
+        const uint8_t *stage = ring + size_t(s) * a.stage_bytes;
+        if (landed) {
+#pragma unroll
+            for (unsigned u = 0; u < 2; ++u) {
+                const unsigned j = warp + u * kPanelWarps;  // the step within the round
+                const unsigned k = k0 + j;
+                if (k >= KC) break;
+                const uint8_t *tile = stage + size_t(j) * W.tile_bytes;
+                Step<FMT> st;
+                st.q0 = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+                if (FMT == 8) {
+                    st.q1 = *reinterpret_cast<const uint4 *>(tile + 512 + lane * 16);
+                    st.d = *reinterpret_cast<const uint16_t *>(tile + 1024 + lane * 2);
+                } else if (FMT == 2) {
+                    st.d = *reinterpret_cast<const uint16_t *>(tile + 512 + lane * 2);
+                } else {
+                    st.d = *reinterpret_cast<const uint32_t *>(tile + 512 + lane * 4);
+                }
+                const unsigned b = k * C + b_in;
+                float *tslot = tb + (j * C + b_in) * P + r_in;
+                if (b >= nb) {  // a padding unit past the row's last block: its term is never folded
+                    continue;
+                }
+                // the unit's weight words, unpacked once for all rows (block_term's arithmetic, split)
+                uint4 wl, wh;
+                if (FMT == 8) {
+                    wl = st.q0;
+                    wh = st.q1;
+                } else {
+                    const uint32_t mk = 0x0F0F0F0Fu;
+                    wl = make_uint4(st.q0.x & mk, st.q0.y & mk, st.q0.z & mk, st.q0.w & mk);
+                    wh = make_uint4((st.q0.x >> 4) & mk, (st.q0.y >> 4) & mk, (st.q0.z >> 4) & mk, (st.q0.w >> 4) & mk);
+                }
+                const float dw = half_bits_to_float(uint16_t(st.d & 0xffffu));
+                const float mw = FMT == 3 ? half_bits_to_float(uint16_t(st.d >> 16)) : 0.0f;
+                const uint8_t *xb = img + size_t(b) * kBatchImgBlockBytes;
+#pragma unroll
+                for (unsigned m = 0; m < kBatchMax; ++m) {
+                    if (m >= mn) break;
+                    const uint8_t *xm = xb + size_t(m) * nb * kBatchImgBlockBytes;
+                    const uint4 x0 = *reinterpret_cast<const uint4 *>(xm);
+                    const uint4 x1 = *reinterpret_cast<const uint4 *>(xm + 16);
+                    const uint4 meta = *reinterpret_cast<const uint4 *>(xm + 32);
+                    int d0 = __dp4a(int(wl.x), int(x0.x), 0);
+                    int d1 = __dp4a(int(wh.x), int(x1.x), 0);
+                    d0 = __dp4a(int(wl.y), int(x0.y), d0);
+                    d1 = __dp4a(int(wh.y), int(x1.y), d1);
+                    d0 = __dp4a(int(wl.z), int(x0.z), d0);
+                    d1 = __dp4a(int(wh.z), int(x1.z), d1);
+                    d0 = __dp4a(int(wl.w), int(x0.w), d0);
+                    d1 = __dp4a(int(wh.w), int(x1.w), d1);
+                    const int sumi = d0 + d1 - (FMT == 2 ? 8 * int(meta.z) : 0);
+                    const float xd = __uint_as_float(meta.x);
+                    float t;
+                    if (FMT == 3) t = fadd(fmul(fmul(dw, xd), float(sumi)), fmul(mw, __uint_as_float(meta.y)));
+                    else t = fmul(float(sumi), fmul(dw, xd));
+                    tslot[m * rs] = t;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);  // this warp has read the stage
+        // one barrier (with a vote) per round: this round's terms before their fold; the buffer written above was
+        // last read by the fold of round it - 2, which every consumer finished before the barrier of round it - 1
+        if (consumers_any(!landed)) {
+            failed = true;
+            break;
+        }
+        if (owner) {
+            const unsigned j1 = min(kBatchChunk * C, nb > k0 * C ? nb - k0 * C : 0u);
+            const float *t = tb + om * rs + orow;
+            for (unsigned j = 0; j < j1; ++j) acc = fadd(acc, t[j * P]);
+            const unsigned row = pnl * P + orow;
+            if (rd + 1 == rounds && row < W.rows) {
+                float *y = a.y + size_t(a.m0 + om) * a.ystride + W.row0 + row;
+                *y = a.add ? fadd(acc, *y) : acc;
+            }
+        }
+    }
+    if (failed) {
+        if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1u);
+        return;
+    }
+    // zero padding of every output row up to a multiple of 16 floats (the GEMV's padding rule)
+    if (blockIdx.x == 0) {
+        const unsigned pad = a.ystride - W.rows;
+        for (unsigned i = threadIdx.x; i < mn * pad; i += kPanelThreads)
+            a.y[size_t(a.m0 + i / pad) * a.ystride + W.rows + i % pad] = 0.0f;
+    }
+}
+
+static void (*batch_kernel_for(unsigned fmt))(BatchArgs) {
+    switch (fmt) {
+    case 2: return gemv_batch_kernel<2>;
+    case 3: return gemv_batch_kernel<3>;
+    case 8: return gemv_batch_kernel<8>;
+    default: return nullptr;
+    }
+}
+
+// Rows per launch: as many as leave room for a ring of at least two stages in one CTA's shared memory.
+unsigned gemv_batch_rows_per_launch(const MatrixView &w, unsigned cols) {
+    for (unsigned mn = kBatchMax; mn >= 1; --mn)
+        if (batch_fixed_smem(w, cols, mn) + 2 * batch_stage_bytes(w) <= 227 * 1024) return mn;
+    return 0;
+}
+
+cudaError_t launch_gemv_batch(const BatchArgs &args, unsigned sms, cudaStream_t st, bool pdl) {
+    const auto k = batch_kernel_for(args.w.format);
+    const unsigned per = gemv_batch_rows_per_launch(args.w, args.cols);
+    if (!k || per == 0 || args.batch == 0 || args.batch > kBatchMax) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const size_t stage = batch_stage_bytes(args.w);
+    for (unsigned m0 = 0; m0 < args.batch; m0 += per) {
+        BatchArgs a = args;
+        a.m0 = m0;
+        a.mn = std::min(per, args.batch - m0);
+        a.stage_bytes = unsigned(stage);
+        const size_t fixed = batch_fixed_smem(a.w, a.cols, a.mn);
+        // two CTAs per SM when a ring of four stages still fits half the shared memory, else one with a deeper ring;
+        // at most 16 stages (the mbarriers' room)
+        const size_t half = 227 * 1024 / 2 - 1024;
+        const unsigned per_sm = fixed + 4 * stage <= half ? 2u : 1u;
+        const size_t budget = per_sm == 2 ? half : 227 * 1024;
+        a.n_stages = unsigned(std::min<size_t>((budget - fixed) / stage, kBatchBarBytes / 16));
+        const size_t smem = fixed + size_t(a.n_stages) * stage;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(std::min(a.w.n_rt, sms * per_sm));
+        cfg.blockDim = dim3(kBatchThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        e = cudaLaunchKernelEx(&cfg, k, a);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 }  // namespace b200q

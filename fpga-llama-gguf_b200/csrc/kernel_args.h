@@ -172,4 +172,21 @@ struct QuantArgs {
     PeerWait pw;
 };
 
+// GEMV_BATCH: y_m = W x_m (+ y_m) for the m < batch activation rows of one command, one read of W per launch. Each
+// CTA holds the quantized rows in shared memory: per row and 32-value block 48 bytes, the quants of values 0..15,
+// those of values 16..31, then {d, s, sum of q, 0} (the XBlock fields of a GEMV pass).
+constexpr unsigned kBatchMax = 8;
+constexpr unsigned kBatchImgBlockBytes = 48;
+struct BatchArgs {
+    MatrixView w;
+    const float *x = nullptr;     // row m at x + m * cols
+    unsigned cols = 0, batch = 0;
+    unsigned m0 = 0, mn = 0;      // the rows of this launch: [m0, m0 + mn)
+    unsigned act = 0;             // 0 Q8_0 (Q4_0, Q8_0 weights), 1 Q8_1 (Q4_1)
+    float *y = nullptr;           // row m at y + m * ystride
+    unsigned ystride = 0, add = 0;
+    unsigned n_stages = 0, stage_bytes = 0;  // the weight ring of gemv_batch_kernel (host-planned)
+    unsigned *err = nullptr;      // set when a bounded wait runs out
+};
+
 }  // namespace b200q

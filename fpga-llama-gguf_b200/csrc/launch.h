@@ -85,6 +85,10 @@ cudaError_t launch_gemv_q8(const GemvArgs &a, unsigned fa, unsigned fb, unsigned
                            bool pdl);
 cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl);
 cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st);
+// GEMV_BATCH: activation rows one launch of gemv_batch_kernel takes (0: the matrix's panels do not fit), and the
+// launches of one command (the quantizer, then one or more batch launches)
+unsigned gemv_batch_rows_per_launch(const MatrixView &w, unsigned cols);
+cudaError_t launch_gemv_batch(const BatchArgs &a, unsigned sms, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,
                            float eps, unsigned flags, const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl);

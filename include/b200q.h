@@ -81,6 +81,14 @@ extern "C" {
 /* [16, n, x_off, y_off, 0, 0, 0, 0]: y[r n .. r n + n) = x of rank r, for every rank r (y: n x world floats); with one
  * rank y = x. x and y are disjoint, or x is rank r's own part of y. */
 #define B200Q_OP_ALLGATHER 16u
+/* [17, format | flags | (batch - 1) << 16, rows, cols, w_off lo, w_off hi, x_off, y_off]: y_m = W x_m for m < batch
+ * (at most 8), x_m the cols floats at x_off + m cols, y_m the rows floats at y_off + m round16(rows) (zero padding up
+ * to a multiple of 16, as a GEMV's y); flags 0 or B200Q_GEMV_ADD (y_m = W x_m + y_m). Formats Q4_0, Q8_0, Q4_1;
+ * cols a multiple of 128; the x and y ranges disjoint; not in a row-sharded context. The weights are read once for
+ * all rows (when the rows' quantized images and term buffers do not fit one CTA's shared memory, once per group of
+ * rows), and every y_m has the bits of the GEMV command on x_m. A GEMV_BATCH does not consume a deferred RMSNORM:
+ * it reads x as act holds it. The batch path of the reference's roadmap (docs/ROADMAP.md:80-96, P2). */
+#define B200Q_OP_GEMV_BATCH 17u
 
 #define B200Q_GEMV_SWIGLU 0x100u
 #define B200Q_GEMV_CONV 0x200u
@@ -114,10 +122,10 @@ extern "C" {
 /* feature words written by a zero-command b200q_run() into act[0], act[1] (reference gemvqc16.h:126-134): the
  * reference's marker and bit meanings, all bits set (Q5_K, Q6_K, Q4_1, every fusion, ROPE, TRACE). act[2] holds
  * this library's own word: marker 0x6B53 in the high half, bit 0 ATTN, bit 1 ARGMAX, bit 2 GET_ROW, bit 3
- * row-sharded multi-GPU lists, bit 4 ALLREDUCE / ALLGATHER. */
+ * row-sharded multi-GPU lists, bit 4 ALLREDUCE / ALLGATHER, bit 5 GEMV_BATCH. */
 #define B200Q_FEATURES 0x6B51FFFFu
 #define B200Q_FEATURES2 0x6B520001u
-#define B200Q_FEATURES3 0x6B53001Fu
+#define B200Q_FEATURES3 0x6B53003Fu
 
 /* ---- status codes ------------------------------------------------------------------------------------------ */
 #define B200Q_OK 0

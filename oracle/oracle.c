@@ -621,7 +621,7 @@ ORC_API int orc_run_list(float *act, size_t act_floats, float *state, size_t sta
                          unsigned n_cmds) {
     if (n_cmds == 0) {
         /* feature probe (gemvqc16.h:124-134): the features this library reports */
-        const uint32_t f[3] = {0x6B51FFFFu, 0x6B520001u, 0x6B53000Fu};
+        const uint32_t f[3] = {0x6B51FFFFu, 0x6B520001u, 0x6B53003Fu};
         memcpy(act, f, sizeof(f));
         return 0;
     }
@@ -941,6 +941,27 @@ ORC_API int orc_run_list(float *act, size_t act_floats, float *state, size_t sta
                 break;
             }
             orc_dequantize_row(w->data + (size_t)row * orc_row_bytes(cols, fmt), cols, fmt, M.act + c[6]);
+        } else if (op == 17) { /* GEMV_BATCH extension: y_m = W x_m (+ y_m) for m < batch, as batch GEMV commands */
+            const unsigned fmt = c[1] & 0xffu, fl = c[1] & 0xff00u, batch = ((c[1] >> 16) & 0xffu) + 1u;
+            const unsigned rows = c[2], cols = c[3], ys = (rows + 15u) / 16u * 16u;
+            const uint64_t h = (uint64_t)c[4] | ((uint64_t)c[5] << 32);
+            const orc_weight *w = find_w(M.ws, M.nw, h);
+            const size_t xn = (size_t)batch * cols, yn = (size_t)batch * ys;
+            if ((fmt != 2 && fmt != 3 && fmt != 8) || (fl != 0 && fl != 0x400u) || (c[1] >> 24) != 0 || batch > 8 ||
+                rows == 0 || rows > 65536 || cols == 0 || cols > 16384 || cols % 128 || c[6] % 16 || c[7] % 16 ||
+                !in_act(&M, c[6], xn) || !in_act(&M, c[7], yn) || (c[6] < c[7] + yn && c[7] < c[6] + xn) || !w ||
+                w->format != fmt || w->cols != cols || w->rows != rows) {
+                status = (int)i + 1;
+                break;
+            }
+            float *tmp = (float *)malloc(sizeof(float) * rows);
+            for (unsigned m = 0; m < batch; ++m) {
+                float *y = M.act + c[7] + (size_t)m * ys;
+                orc_gemv(w->data, M.act + c[6] + (size_t)m * cols, rows, cols, fmt, tmp, NULL);
+                for (unsigned r = 0; r < rows; ++r) y[r] = fl ? tmp[r] + y[r] : tmp[r];
+                for (unsigned r = rows; r < ys; ++r) y[r] = 0.0f;
+            }
+            free(tmp);
         } else if (op == 15 || op == 16) { /* ALLREDUCE / ALLGATHER extensions, one rank: y = x (a test that runs
                                              * several ranks' lists performs the collectives itself, between lists) */
             const unsigned n = c[1];
