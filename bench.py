@@ -670,7 +670,14 @@ def main():
                 "kernel": "gemv_q8_kernel (deferred RMSNorm + Q8_0 gate/up pair + SwiGLU)",
                 "algorithmic_bytes_per_launch": ru_bytes, "us_per_launch": round(ru_ms * 1e3, 3),
                 "peak_kind": peak_kind}
-    roofline["traffic"] = profiled_traffic(TOP_KERNEL)
+    traffic = profiled_traffic(TOP_KERNEL)
+    if traffic is not None and tw > 1:
+        # the capture is of the one-GPU launch (all 9216 rows); a tensor-parallel rank's launch streams its share of
+        # the rows, and the launch's traffic is its weight stream, so it scales with the rows
+        full_bytes = 2 * F * (H // 32) * 34 + 4 * (H + H)
+        traffic = int(round(traffic * ru_bytes / full_bytes))
+        roofline["traffic_note"] = "one-GPU capture scaled by this rank's share of the rows"
+    roofline["traffic"] = traffic
 
     # end to end through the public API with host buffers: every step copies its x in from page-locked host memory
     # (stream-ordered b200q_act_write_async), replays the stack and copies y out (b200q_act_read_async); the host
