@@ -9,9 +9,11 @@ import pytest
 import tp_emulation as tp
 
 
-def _shape(D):
-    # 8 DeltaNet heads and 8 query heads over 2 KV heads: at 4 ranks two heads each and one KV head per two ranks
-    return D.Shape(hidden=1024, ffn=2048, n_layers=4, vocab=4096, gdn_heads=8, n_head=8, n_kv_head=2, head_dim=128,
+def _shape(D, world: int = 2):
+    # 8 DeltaNet heads and 8 query heads over 2 KV heads: at 4 ranks two heads each and one KV head per two ranks;
+    # 8 ranks: 16 heads of each kind over 4 KV heads (the 4B-like head counts), two per rank, one KV head per two ranks
+    h, kv = (16, 4) if world == 8 else (8, 2)
+    return D.Shape(hidden=1024, ffn=2048, n_layers=4, vocab=4096, gdn_heads=h, n_head=h, n_kv_head=kv, head_dim=128,
                    rope_dims=32, kv_ctx=128, prefill=64, head_piece=1536)
 
 
@@ -21,10 +23,10 @@ def _decoder_state(m):
     return ws, m.initial_act(), m.initial_state(), m.initial_kv()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_lists_decode_as_one_rank(b2, orc, world):
     import fpga_llama_gguf_b200.decode as D
-    shape = _shape(D)
+    shape = _shape(D, world)
     one = D.HybridDecoder(shape, seed=7)
     ws1, act1, st1, kv1 = _decoder_state(one)
     ranks = [D.HybridDecoder(shape, seed=7, world=world, rank=r) for r in range(world)]
