@@ -294,11 +294,8 @@ size_t attn_smem_bytes(unsigned n_head, unsigned n_kv_head, unsigned head_dim, u
 }
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
-    }
+    const cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_kernel), 200 * 1024);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_chunks, a.n_kv_head);
     cfg.blockDim = dim3(kAttnThreads);

@@ -470,12 +470,10 @@ void plan_gemv_kq(GemvArgs &a, size_t &smem) {
 }
 
 cudaError_t launch_gemv_kq(const GemvArgs &a, unsigned grid, size_t smem, cudaStream_t st, bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(gemv_kq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(gemv_kq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        attr_set = true;
-    }
+    const void *k = a.ps.world > 1 ? reinterpret_cast<const void *>(gemv_kq_kernel<true>)
+                                   : reinterpret_cast<const void *>(gemv_kq_kernel<false>);
+    const cudaError_t e = ensure_smem_attr(k, 227 * 1024);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kPassThreads);

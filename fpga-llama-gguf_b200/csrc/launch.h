@@ -4,10 +4,29 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "kernel_args.h"
 #include "plan.h"
 
 namespace b200q {
+
+// Raise a kernel's dynamic shared-memory limit once per device (the attribute is per device and function). Callers
+// hold the current device; safe from several threads.
+inline cudaError_t ensure_smem_attr(const void *func, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void *>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({dev, func})) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({dev, func});
+    return e;
+}
 
 struct EwArgs {
     unsigned op = 0;      // 3 ADD, 4 SILU_MUL, 5 MUL, 6 UNARY
