@@ -257,6 +257,13 @@ def lib() -> ctypes.CDLL:
         "b200q_set_feature_mask": (I, [P, U32]),
         "b200q_feature_mask": (U32, [P]),
         "b200q_set_verify": (I, [P, VERIFY_FN, P, I]),
+        "b200q_lower": (I, [P, U, U32, ctypes.POINTER(P), ctypes.c_char_p, U]),
+        "b200q_lowering_free": (None, [P]),
+        "b200q_lowering_lists": (U, [P]),
+        "b200q_lowering_list": (ctypes.POINTER(U32), [P, U, ctypes.POINTER(U)]),
+        "b200q_lowering_offset": (SZ, [P, U]),
+        "b200q_lowering_act_floats": (SZ, [P]),
+        "b200q_node_supported": (I, [P, U]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -280,7 +287,9 @@ EXPORTED = ["b200q_create", "b200q_destroy", "b200q_last_error", "b200q_stream",
             "b200q_gguf_open", "b200q_gguf_close", "b200q_gguf_version", "b200q_gguf_n_tensors", "b200q_gguf_n_kv",
             "b200q_gguf_tensor", "b200q_gguf_find_tensor", "b200q_gguf_kv", "b200q_gguf_find_kv", "b200q_gguf_get_int",
             "b200q_gguf_get_float", "b200q_upload_gguf_tensor", "b200q_q4_0x8_to_q4_0", "b200q_set_feature_mask",
-            "b200q_feature_mask", "b200q_set_verify", "b200q_comm_init_ex"]
+            "b200q_feature_mask", "b200q_set_verify", "b200q_comm_init_ex", "b200q_lower", "b200q_lowering_free",
+            "b200q_lowering_lists", "b200q_lowering_list", "b200q_lowering_offset", "b200q_lowering_act_floats",
+            "b200q_node_supported"]
 
 
 class _LayoutInfo(ctypes.Structure):

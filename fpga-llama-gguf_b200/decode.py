@@ -454,6 +454,94 @@ class HybridDecoder:
         lists.append(cmd_list(*cur))
         return lists
 
+    # ---- the same token as an op graph, for the lowering -----------------------------------------------------------
+    def token_graph(self):
+        """One token as an op graph (graph.Graph) computing what token_lists computes, for b200q_lower to fuse and
+        place: the embedding row, the layers (norms as RMS_NORM and MUL by the weight, the DeltaNet gates and gated
+        norm as the ops they are made of, the attention q / gate rows as strided views), the head pieces writing into
+        one logits buffer and ARGMAX writing the next token's id. Returns (graph, names): names maps "rec", "tok",
+        "logits", "onorm" and (layer, parameter) to the node ids of the INPUT / PARAM tensors (one rank only)."""
+        from .graph import Graph
+        from . import UNARY_SIGMOID, UNARY_SILU, UNARY_SOFTPLUS
+        if self.world != 1:
+            raise ValueError("the graph form covers the one-rank model")
+        s, h = self.s, self.handles
+        H, F, d, hd, hv = s.hidden, s.ffn, s.gdn_rows, s.head_dim, s.gdn_heads
+        att, kvd = s.n_head * hd, s.n_kv_head * hd
+        g = Graph()
+        names = {"rec": g.input(RECORD), "tok": g.input(16), "logits": g.input(s.vocab), "onorm": g.param(H)}
+        pos, cs = g.view(names["rec"], 0, 16), g.view(names["rec"], 16, 128)
+        x = g.get_rows(names["tok"], h["tok_embd"], Q4_0, H)
+        g.end_segment()
+
+        def param(i, key, n):
+            names[(i, key)] = g.param(n)
+            return names[(i, key)]
+
+        def project_out(i, yy, cols, name, x):
+            return g.add(g.mul_mat(yy, h[f"{i}.{name}"], Q4_0, H, cols), x)
+
+        j = slot = 0
+        for i in range(s.n_layers):
+            xn = g.mul(g.rms_norm(x, s.eps), param(i, "attn_norm", H))
+            if s.is_attn(i):
+                qg = g.mul_mat(xn, h[f"{i}.wq_gate"], Q4_0, 2 * att, H)
+                kk = g.mul_mat(xn, h[f"{i}.wk"], Q4_0, kvd, H)
+                vv = g.mul_mat(xn, h[f"{i}.wv"], Q4_0, kvd, H)
+                qn = g.mul(g.rms_norm(g.view(qg, 0, hd, 2 * hd, s.n_head), s.eps, rows=s.n_head),
+                           param(i, "q_norm", hd))
+                kn = g.mul(g.rms_norm(kk, s.eps, rows=s.n_kv_head), param(i, "k_norm", hd))
+                qr = g.rope(qn, cs, s.rope_dims, hd, s.n_head)
+                kr = g.rope(kn, cs, s.rope_dims, hd, s.n_kv_head)
+                ya = g.attn(qr, kr, vv, pos, s.n_head, s.n_kv_head, hd, slot)
+                yg = g.mul(ya, g.unary(g.view(qg, hd, hd, 2 * hd, s.n_head), UNARY_SIGMOID))
+                x = project_out(i, yg, att, "wo", x)
+                slot += 1
+            else:
+                qkv = g.mul_mat(xn, h[f"{i}.wqkv"], Q4_0, 3 * d, H)
+                qkvc = g.conv(qkv, param(i, "conv_w", 4 * 3 * d), param(i, "conv_hist", 3 * 3 * d))
+                z = g.mul_mat(xn, h[f"{i}.wz"], Q4_0, d, H)
+                beta_raw = g.mul_mat(xn, h[f"{i}.wbeta"], Q4_0, hv, H)
+                alpha_raw = g.mul_mat(xn, h[f"{i}.walpha"], Q4_0, hv, H)
+                q = g.l2_norm(g.view(qkvc, 0, d), s.eps, rows=hv)
+                k = g.l2_norm(g.view(qkvc, d, d), s.eps, rows=hv)
+                gate = g.mul(g.unary(g.add(alpha_raw, param(i, "dt", hv)), UNARY_SOFTPLUS), param(i, "a", hv))
+                y = g.gdn(q, k, g.view(qkvc, 2 * d, d), gate, g.unary(beta_raw, UNARY_SIGMOID), hv, hv, j * d,
+                          GDN_DIM ** -0.5)
+                yn = g.mul(g.mul(g.rms_norm(y, s.eps, rows=hv), param(i, "gdn_norm", GDN_DIM)), g.unary(z, UNARY_SILU))
+                x = project_out(i, yn, d, "ssm_out", x)
+                j += 1
+            xn = g.mul(g.rms_norm(x, s.eps), param(i, "ffn_norm", H))
+            ff = g.swiglu(g.mul_mat(xn, h[f"{i}.gate"], Q4_0, F, H), g.mul_mat(xn, h[f"{i}.up"], Q4_0, F, H))
+            x = project_out(i, ff, F, "down", x)
+            g.end_segment()
+        xn = g.mul(g.rms_norm(x, s.eps), names["onorm"])
+        for jj, (r0, n) in enumerate(s.head_pieces()):
+            g.mul_mat(xn, h[f"output.{jj}"], Q6_K, n, H, dst=g.view(names["logits"], r0, n))
+        g.argmax(names["logits"], dst=names["tok"])
+        g.end_segment()
+        return g, names
+
+    def graph_act(self, names, low) -> np.ndarray:
+        """act for lowered lists: the resident values of initial_act() at the lowering's offsets."""
+        L, a0 = self.L, self.initial_act()
+        act = np.zeros(low.act_floats, np.float32)
+        act[low.offset(names["tok"]):low.offset(names["tok"]) + 16] = a0[L.TOK:L.TOK + 16]
+        act[low.offset(names["onorm"]):low.offset(names["onorm"]) + self.s.hidden] = a0[L.ONORM:L.ONORM + self.s.hidden]
+        for key, node in names.items():
+            if isinstance(key, tuple):
+                i, name = key
+                src = L.layer[i][name]
+                n = low.offset(node), self._param_len(name)
+                act[n[0]:n[0] + n[1]] = a0[src:src + n[1]]
+        return act
+
+    def _param_len(self, name: str) -> int:
+        s = self.ls
+        return {"attn_norm": s.hidden, "ffn_norm": s.hidden, "q_norm": s.head_dim, "k_norm": s.head_dim,
+                "conv_w": 4 * 3 * s.gdn_rows, "conv_hist": 3 * 3 * s.gdn_rows, "dt": s.gdn_heads, "a": s.gdn_heads,
+                "gdn_norm": GDN_DIM}[name]
+
     # ---- running on a context ------------------------------------------------------------------------------------
     def context_config(self, world: int = 1) -> dict:
         """Context arguments that fit this model on one rank: of a world-way row-sharded run (the library shards

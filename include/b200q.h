@@ -419,6 +419,74 @@ B200Q_API int b200q_comm_init_ex(b200q_ctx *ctx, int world, int rank, const uint
 B200Q_API int b200q_row_slice(unsigned rows, unsigned flags, int world, int rank, unsigned *r0, unsigned *r1);
 B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
 
+/* ---- graph lowering (host only): a model's op graph to command lists ------------------------------------------
+ * The reference's backend walks a ggml graph, finds the fusions the kernel supports and emits 8-word command lists
+ * with the operands placed in act (plan and fusion analysis: ggml-xrt.cpp:1815-2188; emission: :2190-2745;
+ * supports_op: :2998-3015). This is that step for callers that hold their graph in another form: an array of nodes in
+ * execution order, each naming its operands by index. The lowering
+ *   - places every tensor in act (16-float aligned; INPUT tensors, which the caller writes, and PARAM tensors, which
+ *     stay resident, too) and reports the offsets;
+ *   - fuses what the command ISA can fuse, each fusion kept only when its feature bit is set (the reference's
+ *     feature-word bits): a SWIGLU of two MUL_MATs on one x read only by it becomes a SwiGLU GEMV pair (bit 3); an
+ *     ADD of a MUL_MAT read only by it and an operand computed before the MUL_MAT becomes the GEMV's ADD epilogue
+ *     (bit 8); a CONV of a MUL_MAT read only by it becomes the GEMV's CONV epilogue (bit 6); an RMS_NORM, with its
+ *     weight MUL, read only by MUL_MATs of the same segment becomes a deferred RMSNORM (bit 9); an RMS_NORM followed
+ *     by a MUL by a PARAM row becomes one weighted RMSNORM; L2_NORMs of a GDN's q and k and the gated output
+ *     MUL(MUL(RMS_NORM(y), w), SILU(z)) fold into the GDN command (bit 7), the gates SIGMOID(beta) and
+ *     MUL(SOFTPLUS(ADD(alpha, dt)), a) too (bit 10), and a MUL_MAT on the GDN output right behind it joins the step's
+ *     pass (bit 15); MUL by SILU(g) becomes SILU_MUL, MUL by SIGMOID(g) (g possibly strided rows) SILU_MUL with the
+ *     sigmoid flag (word 1 bit 0);
+ *   - packs the commands of consecutive segments (a node with B200Q_NODE_SEGMENT_END closes one, e.g. a layer)
+ *     into lists of at most 128 commands, never splitting a segment.
+ * No counterpart type in the reference: it stands for the ggml_cgraph the reference's backend receives. */
+#define B200Q_NODE_INPUT 1u     /* n floats the caller writes before the lists run (or a buffer commands fill) */
+#define B200Q_NODE_PARAM 2u     /* n resident floats the caller writes once (norm weights, conv kernels, states) */
+#define B200Q_NODE_VIEW 3u      /* rows u[3] of u[1] floats every u[2] floats of src[0], from float u[0]; no command */
+#define B200Q_NODE_MUL_MAT 4u   /* y[rows] = W x: src[0] x (cols floats), weight handle, fmt, rows, cols */
+#define B200Q_NODE_RMS_NORM 5u  /* rows of n / rows floats of src[0] (eps) */
+#define B200Q_NODE_L2_NORM 6u   /* as RMS_NORM with the L2 scale */
+#define B200Q_NODE_MUL 7u       /* src[0] * src[1] (src[1] of one row's length: the same row for every row) */
+#define B200Q_NODE_ADD 8u       /* src[0] + src[1] */
+#define B200Q_NODE_SWIGLU 9u    /* silu(src[0]) * src[1] */
+#define B200Q_NODE_UNARY 10u    /* u[0]: B200Q_UNARY_SILU / SIGMOID / SOFTPLUS / COPY of src[0] */
+#define B200Q_NODE_CONV 11u     /* causal conv (k = 4) of src[0] (channels) with kernel PARAM src[1] [4 x ch] and state
+                                 * PARAM src[2] [3 x ch], updated in place; u[0] 1: SiLU of the result */
+#define B200Q_NODE_GDN 12u      /* DeltaNet step: src[0] q, [1] k, [2] v, [3] g, [4] beta; u[0] value heads, u[1] key
+                                 * heads, u[2] the first state row; eps = the q scale; y = hv x 128 floats */
+#define B200Q_NODE_ROPE 13u     /* NEOX rotation of src[0] by the cos/sin row src[1]: u[0] dims, u[1] row length, u[2] rows */
+#define B200Q_NODE_ATTN 14u     /* src[0] q, [1] k, [2] v, [3] position (uint32 bits); u[0] heads, u[1] KV heads,
+                                 * u[2] head size, u[3] KV slot */
+#define B200Q_NODE_GET_ROWS 15u /* row act[src[0]] (uint32 bits) of a Q4_0 / Q8_0 matrix (weight, fmt, cols) */
+#define B200Q_NODE_ARGMAX 16u   /* {first index of the maximum (uint32 bits), maximum} of src[0] */
+#define B200Q_NODE_SEGMENT_END 1u  /* flags: the last node of a segment (lists are cut between segments) */
+#define B200Q_NODE_OUTPUT 2u       /* flags: the caller reads the tensor after the lists (it is kept, not fused away) */
+#define B200Q_NODE_SRCS 6u
+typedef struct b200q_node {
+    uint32_t op, flags;
+    int32_t src[B200Q_NODE_SRCS]; /* operand nodes (earlier indices), -1 for none */
+    int32_t dst;                  /* -1, or an earlier node (INPUT or VIEW of one) whose floats this output overwrites */
+    uint32_t n;                   /* output floats */
+    uint32_t fmt, rows, cols;     /* MUL_MAT / GET_ROWS weight; norms: rows */
+    uint64_t weight;              /* weight handle (b200q_upload_weight) */
+    float eps;
+    uint32_t u[4];
+} b200q_node;
+typedef struct b200q_lowering b200q_lowering;
+/* Lower nodes[0..n_nodes) with `features` (the feature word of b200q_features / a zero-command run: bits 0..15 of
+ * word 0, bit 16 = word 1 bit 0). 0 on success; else B200Q_ERR_ARG with the reason in err, naming the node. */
+B200Q_API int b200q_lower(const b200q_node *nodes, unsigned n_nodes, uint32_t features, b200q_lowering **out,
+                          char *err, unsigned err_len);
+B200Q_API void b200q_lowering_free(b200q_lowering *l);
+B200Q_API unsigned b200q_lowering_lists(const b200q_lowering *l);
+/* the commands of list i (8 words each); NULL past the last list */
+B200Q_API const uint32_t *b200q_lowering_list(const b200q_lowering *l, unsigned i, unsigned *n_cmds);
+/* act offset of node i's floats (SIZE_MAX for a tensor folded into a command, which act never holds) */
+B200Q_API size_t b200q_lowering_offset(const b200q_lowering *l, unsigned node);
+/* act floats the lowered lists use (the context's act_floats must be at least this) */
+B200Q_API size_t b200q_lowering_act_floats(const b200q_lowering *l);
+/* 1 if node i (with its operands) can run on this library, else 0 (the reference backend's supports_op) */
+B200Q_API int b200q_node_supported(const b200q_node *nodes, unsigned i);
+
 #ifdef __cplusplus
 }
 #endif

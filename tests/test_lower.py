@@ -1,0 +1,137 @@
+"""Graph lowering (b200q_lower, host only): op graphs to command lists, the step the reference's backend does on its
+ggml graph (plan / fusion analysis and emission, ggml-xrt.cpp:1815-2745).
+
+  - an FFN block lowers to the fused commands (deferred weighted RMSNORM, SwiGLU GEMV pair, ADD epilogue), and with
+    every feature bit cleared to the plain ones; both run on the oracle to the same values;
+  - the synthetic hybrid decoder's token, written as an op graph (HybridDecoder.token_graph), lowers to the same
+    command sequence as the hand-built lists (opcodes and flags, list by list) and decodes, on the oracle, the same
+    tokens with bit-identical logits, DeltaNet states and KV cache;
+  - invalid graphs fail with the node named; b200q_node_supported follows the command limits."""
+import numpy as np
+import pytest
+
+from conftest import rng
+
+
+def _small_shape(D):
+    return D.Shape(hidden=1024, ffn=2048, n_layers=4, vocab=4096, gdn_heads=4, n_head=4, n_kv_head=2, head_dim=128,
+                   rope_dims=32, kv_ctx=128, prefill=64, head_piece=2048)
+
+
+def _ops(cl):
+    """(opcode, flags word) of each command, the GDN's extension slots skipped."""
+    c = np.asarray(cl).reshape(-1, 8)
+    out, i = [], 0
+    while i < len(c):
+        out.append((int(c[i][0]), int(c[i][1]) if c[i][0] in (1, 7, 12) else int(c[i][7] if c[i][0] == 2 else 0)))
+        if c[i][0] == 7:
+            out.append(("gdn-flags", int(c[i + 1][3])))
+            i += 3 if c[i + 1][3] & 8 else 2
+        else:
+            i += 1
+    return out
+
+
+def _ffn_graph(G, b2, hs, H=1024, F=2048):
+    g = G.Graph()
+    x, w = g.input(H), g.param(H)
+    xn = g.mul(g.rms_norm(x, 1e-6), w)
+    ff = g.swiglu(g.mul_mat(xn, hs[0], b2.Q4_0, F, H), g.mul_mat(xn, hs[1], b2.Q4_0, F, H))
+    y = g.add(g.mul_mat(ff, hs[2], b2.Q4_0, H, F), x)
+    g.mark_output(y)
+    g.end_segment()
+    return g, x, w, y
+
+
+def test_ffn_block_fuses_and_matches_the_plain_form(b2, orc, synth):
+    import fpga_llama_gguf_b200.graph as G
+    H, F = 1024, 2048
+    r = rng(130)
+    mats = [synth.q4_0(r, F, H), synth.q4_0(r, F, H), synth.q4_0(r, H, F)]
+    hs = [4096, 8192, 12288]
+    ws = {h: (m.reshape(-1), rows, cols, b2.Q4_0) for h, m, rows, cols in zip(hs, mats, (F, F, H), (H, H, F))}
+    g, x, w, y = _ffn_graph(G, b2, hs)
+    fused, plain = g.lower(), g.lower(features=0)
+    assert [len(cl) // 8 for cl in fused.lists] == [5]
+    assert _ops(fused.lists[0]) == [(2, b2.NORM_DEFER), (1, b2.Q4_0 | b2.GEMV_SWIGLU), (1, b2.Q4_0),
+                                    (1, b2.Q4_0 | b2.GEMV_ADD), (3, 0)]
+    assert _ops(plain.lists[0]) == [(2, 0), (1, b2.Q4_0), (1, b2.Q4_0), (4, 0), (1, b2.Q4_0), (3, 0)]
+    for low in (fused, plain):
+        assert b2.plan(low.lists[0])[0] == 0
+    outs = []
+    xv, wv = synth.activation(r, H), r.normal(1, 0.1, H).astype(np.float32)
+    for low in (fused, plain):
+        act = np.zeros(low.act_floats, np.float32)
+        act[low.offset(x):low.offset(x) + H] = xv
+        act[low.offset(w):low.offset(w) + H] = wv
+        assert orc.run_list(act, low.lists[0], ws) == 0
+        outs.append(act[low.offset(y):low.offset(y) + H].copy())
+    # the SwiGLU epilogue and SILU_MUL apply the same arithmetic: the block gives the same bits either way
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
+def test_decoder_graph_lowers_to_the_hand_built_lists(b2, orc):
+    import fpga_llama_gguf_b200.decode as D
+    shape = _small_shape(D)
+    m = D.HybridDecoder(shape, seed=5)
+    ws = {}
+    m.upload(lambda g_, rows, cols, fmt, bc, fl: (len(ws) + 1) * 4096, keep=ws)
+    g, names = m.token_graph()
+    low = g.lower()
+    ref = m.token_lists()
+    assert len(low.lists) == len(ref)
+    for a, b in zip(low.lists, ref):
+        assert _ops(a) == _ops(b)
+        assert b2.plan(a)[0] == 0
+    # the same decode on the oracle
+    act1, st1, kv1 = m.initial_act(), m.initial_state(), m.initial_kv()
+    act2, st2, kv2 = m.graph_act(names, low), st1.copy(), kv1.copy()
+    for t in range(2):
+        rec = m.record(shape.prefill + t)
+        act1[m.L.REC:m.L.REC + D.RECORD] = rec
+        r0 = low.offset(names["rec"])
+        act2[r0:r0 + D.RECORD] = rec
+        for cl in m.token_lists():
+            assert orc.run_list(act1, cl, ws, state=st1, kv=kv1, kv_ctx=shape.kv_ctx) == 0
+        for cl in low.lists:
+            assert orc.run_list(act2, cl, ws, state=st2, kv=kv2, kv_ctx=shape.kv_ctx) == 0
+        t1, t2 = m.L.TOK, low.offset(names["tok"])
+        assert act1[t1:t1 + 2].view(np.uint32)[0] == act2[t2:t2 + 2].view(np.uint32)[0]
+    l1, l2 = m.L.LOGITS, low.offset(names["logits"])
+    assert np.array_equal(act1[l1:l1 + shape.vocab].view(np.uint32), act2[l2:l2 + shape.vocab].view(np.uint32))
+    assert np.array_equal(st1.view(np.uint32), st2.view(np.uint32))
+    assert np.array_equal(kv1, kv2)
+
+
+def test_invalid_graphs_name_the_node(b2):
+    import fpga_llama_gguf_b200.graph as G
+    g = G.Graph()
+    x = g.input(100)
+    g.mul_mat(x, 4096, b2.Q4_0, 64, 100)  # 100 columns: not a multiple of 128
+    with pytest.raises(b2.B200QError, match="node 1"):
+        g.lower()
+    assert not g.supported(1) and g.supported(0)
+    g = G.Graph()
+    x = g.input(1024)
+    for _ in range(130):  # one segment of 130 commands does not fit a list
+        x = g.add(x, x)
+    with pytest.raises(b2.B200QError, match="segment 0 has 130 commands"):
+        g.lower()
+    g = G.Graph()
+    x = g.input(1024)
+    g.nodes.append(dict(op=G.NODE_ADD, n=1024, src=[x, 5], dst=-1, fmt=0, rows=0, cols=0, weight=0, eps=0.0, u=[],
+                        flags=0))
+    with pytest.raises(b2.B200QError, match="not an earlier node"):
+        g.lower()
+
+
+def test_segments_pack_into_lists_of_at_most_128_commands(b2):
+    import fpga_llama_gguf_b200.graph as G
+    g = G.Graph()
+    x = g.input(1024)
+    for s in range(5):  # five segments of 40 ADDs: 40 + 40 + 40, then 40 + 40
+        for _ in range(40):
+            x = g.add(x, x)
+        g.end_segment()
+    low = g.lower()
+    assert [len(cl) // 8 for cl in low.lists] == [120, 80]
