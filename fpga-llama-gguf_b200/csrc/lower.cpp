@@ -158,7 +158,7 @@ bool Lowering::validate() {
             if (r >= 0) users[size_t(r)].push_back(int(i));
         }
         if (d.dst < -1 || d.dst >= int(i)) return fail(int(i), "dst is not an earlier node");
-        if (d.op < B200Q_NODE_INPUT || d.op > B200Q_NODE_ARGMAX) return fail(int(i), "unknown op");
+        if (d.op < B200Q_NODE_INPUT || d.op > B200Q_NODE_ALLGATHER) return fail(int(i), "unknown op");
         if (d.n == 0) return fail(int(i), "no floats");
         if (d.op == B200Q_NODE_VIEW) {
             const int b = d.src[0];
@@ -522,6 +522,10 @@ bool Lowering::emit() {
         case B200Q_NODE_ARGMAX:
             push(i, {13u, nd[src(i, 0)].n, o32(src(i, 0)), o32(i)});
             break;
+        case B200Q_NODE_ALLREDUCE:
+        case B200Q_NODE_ALLGATHER:
+            push(i, {d.op == B200Q_NODE_ALLREDUCE ? 15u : 16u, nd[src(i, 0)].n, o32(src(i, 0)), o32(i)});
+            break;
         default:
             return fail(i, "no command for this op");
         }
@@ -614,6 +618,10 @@ int b200q_node_supported(const b200q_node *nodes, unsigned i) {
                d.n == d.cols;
     case B200Q_NODE_ARGMAX:
         return has(0) && d.n == 2;
+    case B200Q_NODE_ALLREDUCE:
+        return has(0) && d.n == n_of(0) && d.n % 16 == 0;
+    case B200Q_NODE_ALLGATHER:
+        return has(0) && n_of(0) % 16 == 0 && d.n % n_of(0) == 0 && d.n / n_of(0) <= b200q::kMaxRanks;
     default:
         return 0;
     }

@@ -459,15 +459,15 @@ class HybridDecoder:
         """One token as an op graph (graph.Graph) computing what token_lists computes, for b200q_lower to fuse and
         place: the embedding row, the layers (norms as RMS_NORM and MUL by the weight, the DeltaNet gates and gated
         norm as the ops they are made of, the attention q / gate rows as strided views), the head pieces writing into
-        one logits buffer and ARGMAX writing the next token's id. Returns (graph, names): names maps "rec", "tok",
-        "logits", "onorm" and (layer, parameter) to the node ids of the INPUT / PARAM tensors (one rank only)."""
+        one logits buffer and ARGMAX writing the next token's id; tensor parallel (world > 1), this rank's slices with
+        ALLREDUCE after each projection back to the hidden size and ALLGATHER of the logits. Returns (graph, names):
+        names maps "rec", "tok", "logits", "onorm" and (layer, parameter) to the node ids of the INPUT / PARAM
+        tensors."""
         from .graph import Graph
         from . import UNARY_SIGMOID, UNARY_SILU, UNARY_SOFTPLUS
-        if self.world != 1:
-            raise ValueError("the graph form covers the one-rank model")
-        s, h = self.s, self.handles
-        H, F, d, hd, hv = s.hidden, s.ffn, s.gdn_rows, s.head_dim, s.gdn_heads
-        att, kvd = s.n_head * hd, s.n_kv_head * hd
+        s, ls, h = self.s, self.ls, self.handles
+        H, F, d, hd, hv = s.hidden, ls.ffn, ls.gdn_rows, s.head_dim, ls.gdn_heads
+        att, kvd, nh, nkv = ls.n_head * hd, ls.n_kv_head * hd, ls.n_head, ls.n_kv_head
         g = Graph()
         names = {"rec": g.input(RECORD), "tok": g.input(16), "logits": g.input(s.vocab), "onorm": g.param(H)}
         pos, cs = g.view(names["rec"], 0, 16), g.view(names["rec"], 16, 128)
@@ -479,7 +479,10 @@ class HybridDecoder:
             return names[(i, key)]
 
         def project_out(i, yy, cols, name, x):
-            return g.add(g.mul_mat(yy, h[f"{i}.{name}"], Q4_0, H, cols), x)
+            part = g.mul_mat(yy, h[f"{i}.{name}"], Q4_0, H, cols)
+            if self.world == 1:
+                return g.add(part, x)
+            return g.allreduce(g.add(part, x) if self.rank == 0 else part)
 
         j = slot = 0
         for i in range(s.n_layers):
@@ -488,13 +491,12 @@ class HybridDecoder:
                 qg = g.mul_mat(xn, h[f"{i}.wq_gate"], Q4_0, 2 * att, H)
                 kk = g.mul_mat(xn, h[f"{i}.wk"], Q4_0, kvd, H)
                 vv = g.mul_mat(xn, h[f"{i}.wv"], Q4_0, kvd, H)
-                qn = g.mul(g.rms_norm(g.view(qg, 0, hd, 2 * hd, s.n_head), s.eps, rows=s.n_head),
-                           param(i, "q_norm", hd))
-                kn = g.mul(g.rms_norm(kk, s.eps, rows=s.n_kv_head), param(i, "k_norm", hd))
-                qr = g.rope(qn, cs, s.rope_dims, hd, s.n_head)
-                kr = g.rope(kn, cs, s.rope_dims, hd, s.n_kv_head)
-                ya = g.attn(qr, kr, vv, pos, s.n_head, s.n_kv_head, hd, slot)
-                yg = g.mul(ya, g.unary(g.view(qg, hd, hd, 2 * hd, s.n_head), UNARY_SIGMOID))
+                qn = g.mul(g.rms_norm(g.view(qg, 0, hd, 2 * hd, nh), s.eps, rows=nh), param(i, "q_norm", hd))
+                kn = g.mul(g.rms_norm(kk, s.eps, rows=nkv), param(i, "k_norm", hd))
+                qr = g.rope(qn, cs, s.rope_dims, hd, nh)
+                kr = g.rope(kn, cs, s.rope_dims, hd, nkv)
+                ya = g.attn(qr, kr, vv, pos, nh, nkv, hd, slot)
+                yg = g.mul(ya, g.unary(g.view(qg, hd, hd, 2 * hd, nh), UNARY_SIGMOID))
                 x = project_out(i, yg, att, "wo", x)
                 slot += 1
             else:
@@ -516,8 +518,13 @@ class HybridDecoder:
             x = project_out(i, ff, F, "down", x)
             g.end_segment()
         xn = g.mul(g.rms_norm(x, s.eps), names["onorm"])
-        for jj, (r0, n) in enumerate(s.head_pieces()):
-            g.mul_mat(xn, h[f"output.{jj}"], Q6_K, n, H, dst=g.view(names["logits"], r0, n))
+        v_l = s.vocab // self.world
+        base = self.rank * v_l  # this rank's vocabulary rows (all rows for one rank)
+        pieces = self.head_pieces() if self.world > 1 else s.head_pieces()
+        for jj, (r0, n) in enumerate(pieces):
+            g.mul_mat(xn, h[f"output.{jj}"], Q6_K, n, H, dst=g.view(names["logits"], base + r0, n))
+        if self.world > 1:
+            g.allgather(g.view(names["logits"], base, v_l), self.world, dst=names["logits"])
         g.argmax(names["logits"], dst=names["tok"])
         g.end_segment()
         return g, names

@@ -19,7 +19,8 @@ import numpy as np
 from . import B200QError, lib
 
 NODE_INPUT, NODE_PARAM, NODE_VIEW, NODE_MUL_MAT, NODE_RMS_NORM, NODE_L2_NORM, NODE_MUL, NODE_ADD, NODE_SWIGLU, \
-    NODE_UNARY, NODE_CONV, NODE_GDN, NODE_ROPE, NODE_ATTN, NODE_GET_ROWS, NODE_ARGMAX = range(1, 17)
+    NODE_UNARY, NODE_CONV, NODE_GDN, NODE_ROPE, NODE_ATTN, NODE_GET_ROWS, NODE_ARGMAX, NODE_ALLREDUCE, \
+    NODE_ALLGATHER = range(1, 19)
 SEGMENT_END, OUTPUT = 1, 2
 SRCS = 6
 ALL_FEATURES = 0x1FFFF  # word 0 bits 0..15 and the SIGMOID_MUL bit of word 1
@@ -104,6 +105,12 @@ class Graph:
 
     def argmax(self, x: int, dst: int = -1) -> int:
         return self._add(NODE_ARGMAX, 2, [x], dst=dst)
+
+    def allreduce(self, x: int) -> int:
+        return self._add(NODE_ALLREDUCE, self.n(x), [x])
+
+    def allgather(self, x: int, world: int, dst: int = -1) -> int:
+        return self._add(NODE_ALLGATHER, self.n(x) * world, [x], dst=dst)
 
     def end_segment(self) -> None:
         """The last node so far closes a segment (lists are cut between segments only)."""

@@ -458,6 +458,9 @@ B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
                                  * u[2] head size, u[3] KV slot */
 #define B200Q_NODE_GET_ROWS 15u /* row act[src[0]] (uint32 bits) of a Q4_0 / Q8_0 matrix (weight, fmt, cols) */
 #define B200Q_NODE_ARGMAX 16u   /* {first index of the maximum (uint32 bits), maximum} of src[0] */
+#define B200Q_NODE_ALLREDUCE 17u /* the sum over the communicator's ranks of src[0] (tensor-parallel lists) */
+#define B200Q_NODE_ALLGATHER 18u /* the ranks' src[0] side by side (n = their floats x ranks); src[0] may be this rank's
+                                  * own part of dst */
 #define B200Q_NODE_SEGMENT_END 1u  /* flags: the last node of a segment (lists are cut between segments) */
 #define B200Q_NODE_OUTPUT 2u       /* flags: the caller reads the tensor after the lists (it is kept, not fused away) */
 #define B200Q_NODE_SRCS 6u

@@ -6,6 +6,8 @@ ggml graph (plan / fusion analysis and emission, ggml-xrt.cpp:1815-2745).
   - the synthetic hybrid decoder's token, written as an op graph (HybridDecoder.token_graph), lowers to the same
     command sequence as the hand-built lists (opcodes and flags, list by list) and decodes, on the oracle, the same
     tokens with bit-identical logits, DeltaNet states and KV cache;
+  - tensor parallel: every rank's graph (ALLREDUCE / ALLGATHER nodes) lowers to that rank's hand-built lists, and the
+    ranks' lowered lists, run in lock step, decode as the hand-built ones;
   - invalid graphs fail with the node named; b200q_node_supported follows the command limits."""
 import numpy as np
 import pytest
@@ -135,3 +137,42 @@ def test_segments_pack_into_lists_of_at_most_128_commands(b2):
         g.end_segment()
     low = g.lower()
     assert [len(cl) // 8 for cl in low.lists] == [120, 80]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_graphs_lower_to_the_hand_built_rank_lists(b2, orc, world):
+    """Each rank's token graph (its slices, ALLREDUCE after every projection back to the hidden size, ALLGATHER of the
+    logits) lowers to that rank's hand-built command sequence; run in lock step on the oracle (the collectives done
+    between lists, tests/tp_emulation.py), the lowered lists of all ranks decode the same tokens with bit-identical
+    logits as the hand-built ones."""
+    import fpga_llama_gguf_b200.decode as D
+    import tp_emulation as tp
+    from test_tensor_parallel_cpu import _decoder_state, _shape
+    shape = _shape(D, world)
+    ranks = [D.HybridDecoder(shape, seed=7, world=world, rank=r) for r in range(world)]
+    per = [_decoder_state(m) for m in ranks]
+    ws = [p[0] for p in per]
+    lowered = [m.token_graph() for m in ranks]
+    lows = [g.lower() for g, _ in lowered]
+    for m, low in zip(ranks, lows):
+        ref = m.token_lists()
+        assert len(low.lists) == len(ref)
+        for a, b in zip(low.lists, ref):
+            assert _ops(a) == _ops(b)
+    acts1, states1, kvs1 = [p[1] for p in per], [p[2] for p in per], [p[3] for p in per]
+    acts2 = [m.graph_act(names, low) for m, (_, names), low in zip(ranks, lowered, lows)]
+    states2, kvs2 = [s.copy() for s in states1], [k.copy() for k in kvs1]
+    for t in range(2):
+        rec = ranks[0].record(shape.prefill + t)
+        for m, a, (_, names), low in zip(ranks, acts1, lowered, lows):
+            a[m.L.REC:m.L.REC + D.RECORD] = rec
+        for a, (_, names), low in zip(acts2, lowered, lows):
+            a[low.offset(names["rec"]):low.offset(names["rec"]) + D.RECORD] = rec
+        tp.run_lists(orc, [m.token_lists() for m in ranks], acts1, ws, states1, kvs1, shape.kv_ctx)
+        tp.run_lists(orc, [low.lists for low in lows], acts2, ws, states2, kvs2, shape.kv_ctx)
+        for m, a1, a2, (_, names), low in zip(ranks, acts1, acts2, lowered, lows):
+            assert a1[m.L.TOK:m.L.TOK + 1].view(np.uint32)[0] == \
+                a2[low.offset(names["tok"]):low.offset(names["tok"]) + 1].view(np.uint32)[0]
+    for m, a1, a2, (_, names), low in zip(ranks, acts1, acts2, lowered, lows):
+        l1, l2 = m.L.LOGITS, low.offset(names["logits"])
+        assert np.array_equal(a1[l1:l1 + shape.vocab].view(np.uint32), a2[l2:l2 + shape.vocab].view(np.uint32))

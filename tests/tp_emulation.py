@@ -22,18 +22,19 @@ def split_at_collectives(cl: np.ndarray):
 
 
 def collective(cs, acts):
-    """cs[r]: rank r's collective command (the same opcode, n and y on every rank; ALLGATHER's x is the rank's own)."""
-    op, n, y = int(cs[0][0]), int(cs[0][1]), int(cs[0][3])
-    xs = [int(c[2]) for c in cs]
+    """cs[r]: rank r's collective command (the same opcode and n on every rank; x and y are offsets in the rank's own
+    act, which may differ between ranks whose lists place their tensors differently)."""
+    op, n = int(cs[0][0]), int(cs[0][1])
+    xs, ys = [int(c[2]) for c in cs], [int(c[3]) for c in cs]
     if op == OP_ALLREDUCE:
         s = acts[0][xs[0]:xs[0] + n].copy()
         for a, x in zip(acts[1:], xs[1:]):
             s = (s + a[x:x + n]).astype(np.float32)
-        for a in acts:
+        for a, y in zip(acts, ys):
             a[y:y + n] = s
     else:
         parts = [a[x:x + n].copy() for a, x in zip(acts, xs)]
-        for a in acts:
+        for a, y in zip(acts, ys):
             for r, p in enumerate(parts):
                 a[y + r * n:y + (r + 1) * n] = p
 
@@ -50,6 +51,5 @@ def run_lists(orc, lists_per_rank, acts, ws, states, kvs, kv_ctx: int) -> None:
                     assert st == 0, (r, li, si, st)
             cs = [sg[si][1] for sg in segs]
             if cs[0] is not None:
-                same = [0, 1, 3] + ([2] if cs[0][0] == OP_ALLREDUCE else [])
-                assert all(c is not None and np.array_equal(c[same], cs[0][same]) for c in cs), "collectives differ"
+                assert all(c is not None and np.array_equal(c[[0, 1]], cs[0][[0, 1]]) for c in cs), "collectives differ"
                 collective(cs, acts)
