@@ -160,6 +160,10 @@ bool Lowering::validate() {
         if (d.dst < -1 || d.dst >= int(i)) return fail(int(i), "dst is not an earlier node");
         if (d.op < B200Q_NODE_INPUT || d.op > B200Q_NODE_ALLGATHER) return fail(int(i), "unknown op");
         if (d.n == 0) return fail(int(i), "no floats");
+        // operands every op needs (the fusion analysis reads them without further checks)
+        static const unsigned kArity[] = {0, 0, 0, 1, 1, 1, 1, 2, 2, 2, 1, 3, 5, 2, 4, 1, 1, 1, 1};
+        for (unsigned k = 0; k < kArity[d.op]; ++k)
+            if (d.src[k] < 0) return fail(int(i), "operand %u missing", k);
         if (d.op == B200Q_NODE_VIEW) {
             const int b = d.src[0];
             if (b < 0 || nd[b].op == B200Q_NODE_VIEW) return fail(int(i), "a VIEW views one non-VIEW node");

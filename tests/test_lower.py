@@ -176,3 +176,59 @@ def test_tensor_parallel_graphs_lower_to_the_hand_built_rank_lists(b2, orc, worl
     for m, a1, a2, (_, names), low in zip(ranks, acts1, acts2, lowered, lows):
         l1, l2 = m.L.LOGITS, low.offset(names["logits"])
         assert np.array_equal(a1[l1:l1 + shape.vocab].view(np.uint32), a2[l2:l2 + shape.vocab].view(np.uint32))
+
+
+def test_random_graphs_either_fail_cleanly_or_give_valid_lists(b2):
+    """Random graphs (ops and operands drawn at random, mostly well-formed, some not): the lowering either refuses with
+    a message or returns lists the planner accepts; it never crashes."""
+    import fpga_llama_gguf_b200.graph as G
+    r = rng(131)
+    sizes = [128, 256, 512, 1024, 2048]
+    lowered = 0
+    for trial in range(300):
+        g = G.Graph()
+        g.input(int(r.choice(sizes)))
+        g.param(int(r.choice(sizes)))
+        for _ in range(int(r.integers(1, 24))):
+            k = len(g.nodes)
+            x = int(r.integers(0, k))
+            same = [i for i in range(k) if g.n(i) == g.n(x)]
+            y = int(r.choice(same))
+            kind = r.random()
+            if kind < 0.25:
+                fmt = int(r.choice([2, 3, 8]))
+                if g.n(x) % 128 == 0:
+                    g.mul_mat(x, 4096 * (1 + int(r.integers(0, 8))), fmt, int(r.choice(sizes)), g.n(x))
+                else:
+                    g.unary(x, 1)
+            elif kind < 0.4:
+                g.add(x, y)
+            elif kind < 0.5:
+                g.mul(x, y)
+            elif kind < 0.6:
+                g.swiglu(x, y)
+            elif kind < 0.7:
+                g.unary(x, int(r.integers(1, 5)))
+            elif kind < 0.8:
+                (g.rms_norm if r.random() < 0.7 else g.l2_norm)(x, 1e-6)
+            elif kind < 0.85:
+                base = x if g.nodes[x]["op"] != G.NODE_VIEW else g.nodes[x]["src"][0]
+                g.view(base, 0, g.n(base))
+            else:  # anything: random op, operands and sizes (mostly refused)
+                op = int(r.integers(1, 19))
+                g.nodes.append(dict(op=op, n=int(r.choice(sizes)), src=[int(r.integers(-1, k)) for _ in range(5)],
+                                    dst=int(r.integers(-1, k)) if r.random() < 0.2 else -1, fmt=int(r.choice([2, 14])),
+                                    rows=int(r.choice([0, 1, 4])), cols=int(r.choice(sizes)), weight=4096, eps=1e-6,
+                                    u=[int(r.choice([0, 1, 2, 16, 128])) for _ in range(4)],
+                                    flags=int(r.integers(0, 4))))
+            if r.random() < 0.2:
+                g.end_segment()
+        try:
+            low = g.lower(features=int(r.choice([0, G.ALL_FEATURES])))
+        except b2.B200QError as e:
+            assert "node" in str(e) or "segment" in str(e)
+            continue
+        lowered += 1
+        for cl in low.lists:
+            assert b2.plan(cl)[0] == 0, (trial, cl.reshape(-1, 8)[:4])
+    assert lowered > 50, lowered
