@@ -5,11 +5,13 @@
 // optionally with q/k L2-normalized per head (RMSNORM with flags 3), the gates beta = sigmoid(beta),
 // g = softplus(g + dt) * a, and the gated output (RMSNORM(y) * w) * silu(z) per head.
 //
-// One cluster of 4 CTAs per value head, 32 state rows per CTA, four threads per state row: each thread holds a
-// 32-float segment of its row in registers for the whole step (read once, written once) and sums its part of both
-// dot products in index order; the four parts are added as (p0 + p1) + (p2 + p3). (One thread per row, the CPU's
-// fully sequential order, left a single warp per SM running ~1800 dependent instructions: ~8 us per step.) The
-// result is within the reference's tolerance, not bit-exact. The per-head sums of squares (L2 of q and k, RMS of y)
+// One cluster of 4 CTAs per value head, 32 state rows per CTA, eight threads per state row: each thread holds a
+// 16-float segment of its row in registers for the whole step (read once, written once). A row's dot products are
+// summed as four 32-float quarters, each in index order — the even thread of a pair adds its 16 products, the odd
+// thread continues from that sum with its own 16 — and the quarters are added as (q0 + q1) + (q2 + q3). (One thread
+// per row, the CPU's fully sequential order, left a single warp per SM running ~1800 dependent instructions: ~8 us
+// per step; the quarters held by four threads per row, 128 threads per CTA, gave the same sums with half the warps
+// and loads in flight.) The result is within the reference's tolerance, not bit-exact. The per-head sums of squares (L2 of q and k, RMS of y)
 // are four 32-value shuffle-tree sums added in row order, as the CPU oracle is checked against; each CTA forms the
 // q / k sums itself and the y sum from the four CTAs' parts, exchanged through distributed shared memory. When the
 // step's WITH_OUT GEMV follows, each CTA also quantizes its 32 outputs (one Q8_0 block) into that GEMV's x image.
@@ -20,8 +22,10 @@
 
 namespace b200q {
 
-constexpr unsigned kGdnSplit = 4;    // CTAs per head (one cluster), 32 state rows each
-constexpr unsigned kGdnThreads = 128;  // four threads per state row
+constexpr unsigned kGdnSplit = 4;      // CTAs per head (one cluster), 32 state rows each
+constexpr unsigned kGdnPerRow = 8;     // threads per state row
+constexpr unsigned kGdnSeg = 128 / kGdnPerRow;  // floats of a row per thread
+constexpr unsigned kGdnThreads = 32 * kGdnPerRow;
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -29,10 +33,24 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
-// sum of the four segment parts of a row, (p0 + p1) + (p2 + p3), in all four threads of the quad
-__device__ __forceinline__ float quad_sum(float p) {
-    p = fadd(p, __shfl_xor_sync(0xffffffffu, p, 1));
-    return fadd(p, __shfl_xor_sync(0xffffffffu, p, 2));
+// A row's sum from the products its eight threads hold (prod: this thread's 16, in index order): quarter t (32
+// floats) is the in-order sum of threads 2t and 2t + 1 — the odd thread continues from the even thread's sum — and
+// the row's sum is (q0 + q1) + (q2 + q3); every thread of the row gets the same bits.
+__device__ __forceinline__ float row_sum(const float (&prod)[kGdnSeg], unsigned seg) {
+    float acc = 0.0f;
+    if ((seg & 1u) == 0) {
+#pragma unroll
+        for (int i = 0; i < int(kGdnSeg); ++i) acc = fadd(acc, prod[i]);
+    }
+    acc = __shfl_xor_sync(0xffffffffu, acc, 1);  // odd threads: the even thread's sum
+    if (seg & 1u) {
+#pragma unroll
+        for (int i = 0; i < int(kGdnSeg); ++i) acc = fadd(acc, prod[i]);
+    }
+    // the quarters sit in the odd threads 1, 3, 5, 7 of the row's eight: q0 + q1 and q2 + q3, then their sum
+    float qsum = fadd(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+    qsum = fadd(qsum, __shfl_xor_sync(0xffffffffu, qsum, 4));
+    return __shfl_sync(0xffffffffu, qsum, (threadIdx.x % 32) | 1u);
 }
 
 __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads) gdn_kernel(const GdnArgs a) {
@@ -47,19 +65,21 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
     peer_wait_rows_cta(a.pw);
     const unsigned part = cluster_rank(), h = blockIdx.x / kGdnSplit, kh = h % a.hk;
     const unsigned tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const unsigned rloc = tid / 4, seg = tid % 4, j = part * 32 + rloc;
-    // this thread's 32-float segment of state row j: issue the loads first
-    const float4 *src = reinterpret_cast<const float4 *>(a.state_in + (size_t(h) * 128 + j) * 128 + seg * 32);
-    float row[32];
+    const unsigned rloc = tid / kGdnPerRow, seg = tid % kGdnPerRow, j = part * 32 + rloc;
+    // this thread's segment of state row j: issue the loads first
+    const float4 *src = reinterpret_cast<const float4 *>(a.state_in + (size_t(h) * 128 + j) * 128 + seg * kGdnSeg);
+    float row[kGdnSeg];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < int(kGdnSeg / 4); ++i) {
         const float4 v = src[i];
         row[4 * i] = v.x;
         row[4 * i + 1] = v.y;
         row[4 * i + 2] = v.z;
         row[4 * i + 3] = v.w;
     }
-    float qv = a.q[kh * 128 + tid], kv = a.k[kh * 128 + tid];
+    // threads 0..127 hold one value each of the head's q and k (warps 0..3)
+    const bool qk = tid < 128;
+    float qv = qk ? a.q[kh * 128 + tid] : 0.0f, kv = qk ? a.k[kh * 128 + tid] : 0.0f;
     // every other input of the step now, so no load waits in the middle of the dependent chain
     const float vj = a.v[h * 128 + j];
     const float zj = a.z ? a.z[h * 128 + j] : 0.0f, wj = a.z ? a.wn[j] : 0.0f;
@@ -74,18 +94,20 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
     }
     if (a.l2) {  // 1 / fmaxf(sqrtf(float(sum x^2)), eps), x * scale (gemvq_ref.h:309-324 with flags 3)
         const double sq = warp_sum_d(double(fmul(qv, qv))), sk = warp_sum_d(double(fmul(kv, kv)));
-        if (lane == 0) red[warp] = sq;
+        if (lane == 0 && qk) red[warp] = sq;
         __syncthreads();
         const double tq = ((red[0] + red[1]) + red[2]) + red[3];
         __syncthreads();
-        if (lane == 0) red[warp] = sk;
+        if (lane == 0 && qk) red[warp] = sk;
         __syncthreads();
         const double tk = ((red[0] + red[1]) + red[2]) + red[3];
         qv = fmul(qv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(tq)), a.l2_eps)));
         kv = fmul(kv, fdiv(1.0f, fmaxf(__fsqrt_rn(__double2float_rn(tk)), a.l2_eps)));
     }
-    qs[tid] = qv;
-    ks[tid] = kv;
+    if (qk) {
+        qs[tid] = qv;
+        ks[tid] = kv;
+    }
     if (tid == 0) {
         float g = g_in, b = b_in;
         if (a.dt) {  // gemvqc_gdn.h:265-280: g = softplus(g + dt) * a, beta = sigmoid(beta)
@@ -97,33 +119,33 @@ __global__ void __cluster_dims__(kGdnSplit, 1, 1) __launch_bounds__(kGdnThreads)
     }
     __syncthreads();
     const float decay = gate[0], beta = gate[1];
-    float kseg[32];
+    float kseg[kGdnSeg];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 k4 = reinterpret_cast<const float4 *>(ks + seg * 32)[i];
+    for (int i = 0; i < int(kGdnSeg / 4); ++i) {
+        const float4 k4 = reinterpret_cast<const float4 *>(ks + seg * kGdnSeg)[i];
         kseg[4 * i] = k4.x;
         kseg[4 * i + 1] = k4.y;
         kseg[4 * i + 2] = k4.z;
         kseg[4 * i + 3] = k4.w;
     }
-    float dot = 0.0f;
+    float prod[kGdnSeg];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < int(kGdnSeg); ++i) {
         row[i] = fmul(row[i], decay);
-        dot = fadd(dot, fmul(row[i], kseg[i]));
+        prod[i] = fmul(row[i], kseg[i]);
     }
-    dot = quad_sum(dot);
+    const float dot = row_sum(prod, seg);
     const float delta = fmul(fsub(vj, dot), beta);
-    float out = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < int(kGdnSeg); ++i) {
         row[i] = fadd(row[i], fmul(kseg[i], delta));
-        out = fadd(out, fmul(row[i], qs[seg * 32 + i]));
+        prod[i] = fmul(row[i], qs[seg * kGdnSeg + i]);
     }
-    out = quad_sum(out);
-    float4 *dst = reinterpret_cast<float4 *>(a.state_out + (size_t(h) * 128 + j) * 128 + seg * 32);
+    const float out = row_sum(prod, seg);
+    float4 *dst = reinterpret_cast<float4 *>(a.state_out + (size_t(h) * 128 + j) * 128 + seg * kGdnSeg);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dst[i] = make_float4(row[4 * i], row[4 * i + 1], row[4 * i + 2], row[4 * i + 3]);
+    for (int i = 0; i < int(kGdnSeg / 4); ++i)
+        dst[i] = make_float4(row[4 * i], row[4 * i + 1], row[4 * i + 2], row[4 * i + 3]);
     float yv = fmul(out, a.scale);
     cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
     if (a.z) {  // (y * rms scale) * w, then silu(z) * that (RMSNORM + SILU_MUL, gemvqc_gdn.h:284-346)
