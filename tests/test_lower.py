@@ -8,7 +8,9 @@ ggml graph (plan / fusion analysis and emission, ggml-xrt.cpp:1815-2745).
     tokens with bit-identical logits, DeltaNet states and KV cache;
   - tensor parallel: every rank's graph (ALLREDUCE / ALLGATHER nodes) lowers to that rank's hand-built lists, and the
     ranks' lowered lists, run in lock step, decode as the hand-built ones;
-  - invalid graphs fail with the node named; b200q_node_supported follows the command limits."""
+  - invalid graphs fail with the node named; b200q_node_supported follows the command limits;
+  - random graphs: every lowering is refused cleanly or planner-valid, and random graphs of the fusable patterns give
+    bit-identical outputs with every fusion and with none."""
 import numpy as np
 import pytest
 
@@ -232,3 +234,73 @@ def test_random_graphs_either_fail_cleanly_or_give_valid_lists(b2):
         for cl in low.lists:
             assert b2.plan(cl)[0] == 0, (trial, cl.reshape(-1, 8)[:4])
     assert lowered > 50, lowered
+
+
+def test_random_graphs_compute_the_same_with_and_without_fusions(b2, orc, synth):
+    """Random well-formed graphs built from the fusable patterns (norm x weight read by GEMVs, SwiGLU of two GEMVs on one
+    x, GEMV + residual ADD, MUL by SILU / SIGMOID) and plain ops, lowered with every fusion and with none, give on the
+    oracle bit-identical values for every tensor the caller marks as an output (outputs are never fused away)."""
+    import fpga_llama_gguf_b200.graph as G
+    r = rng(132)
+    sizes = [256, 512, 1024]
+    checked = fused_trials = 0
+    for trial in range(60):
+        g = G.Graph()
+        ws = {}
+        leaves = [g.input(int(r.choice(sizes))), g.param(int(r.choice(sizes)))]
+
+        def mm(x, rows):
+            fmt = int(r.choice([2, 8]))
+            h = 4096 * (len(ws) + 1)
+            ws[h] = (synth.matrix(fmt, r, rows, g.n(x)).reshape(-1), rows, g.n(x), fmt)
+            return g.mul_mat(x, h, fmt, rows, g.n(x))
+
+        for _ in range(int(r.integers(3, 10))):
+            k = len(g.nodes)
+            x = int(r.integers(0, k))
+            same = [i for i in range(k) if g.n(i) == g.n(x)]
+            y = int(r.choice(same))
+            kind = r.random()
+            if kind < 0.25:    # norm x weight, read by one to three GEMVs
+                w = g.param(g.n(x))
+                leaves.append(w)
+                xn = g.mul(g.rms_norm(x, 1e-6), w)
+                for _ in range(int(r.integers(1, 4))):
+                    mm(xn, int(r.choice(sizes)))
+            elif kind < 0.4:   # SwiGLU of two GEMVs on one x
+                rows = int(r.choice(sizes))
+                g.swiglu(mm(x, rows), mm(x, rows))
+            elif kind < 0.55:  # GEMV + residual
+                g.add(mm(x, g.n(y)), y)
+            elif kind < 0.65:  # MUL by SILU / SIGMOID
+                g.mul(x, g.unary(y, int(r.choice([1, 2]))))
+            elif kind < 0.75:
+                mm(x, int(r.choice(sizes)))
+            elif kind < 0.85:
+                g.add(x, y)
+            elif kind < 0.95:
+                g.unary(x, int(r.integers(1, 4)))
+            else:
+                base = x if g.nodes[x]["op"] != G.NODE_VIEW else g.nodes[x]["src"][0]
+                g.view(base, 0, g.n(base))
+            if r.random() < 0.3:
+                g.mark_output(len(g.nodes) - 1)
+        g.mark_output(len(g.nodes) - 1)
+        outs = [i for i, d in enumerate(g.nodes) if d["flags"] & G.OUTPUT and d["op"] != G.NODE_VIEW]
+        values = {i: r.normal(0, 1, g.n(i)).astype(np.float32) for i in leaves}
+        results, shapes = [], []
+        for feats in (G.ALL_FEATURES, 0):
+            low = g.lower(features=feats)
+            shapes.append([tuple(c.reshape(-1, 8)[:, :2].reshape(-1)) for c in low.lists])
+            act = np.zeros(low.act_floats, np.float32)
+            for i, v in values.items():
+                act[low.offset(i):low.offset(i) + v.size] = v
+            for cl in low.lists:
+                assert b2.plan(cl)[0] == 0
+                assert orc.run_list(act, cl, ws) == 0, trial
+            results.append({i: act[low.offset(i):low.offset(i) + g.n(i)].copy() for i in outs})
+        fused_trials += shapes[0] != shapes[1]
+        for i in outs:
+            assert np.array_equal(results[0][i].view(np.uint32), results[1][i].view(np.uint32)), (trial, i)
+            checked += 1
+    assert checked > 60 and fused_trials > 40, (checked, fused_trials)
