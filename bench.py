@@ -5,14 +5,15 @@ Workload (configs[1] of the benchmark configurations, the fused FFN block of a 4
 gain N(1, 0.1)) deferred into the Q8_0 quantizer, gate and up Q8_0 GEMVs [9216 x 2560] in one pass with the SwiGLU
 epilogue, the down Q8_0 GEMV [2560 x 9216] with the residual ADD epilogue. The blocks are stacked as the layers of a model: L
 blocks with distinct weights, each reading the residual stream the previous one wrote, form one command list of the
-reference ISA, replayed as one CUDA Graph per step (one token through the L-layer stack). L is chosen so that the
+reference ISA (cut into lists of at most 128 commands between blocks), replayed as CUDA Graphs per step (one token
+through the L-layer stack). L is chosen so that the
 weights of one step exceed 3x the 126 MB L2, so every block reads weights that are not L2-resident. Synthetic seeded
 weights with the config's distributions (no model files here).
 
 metric: GEMV HBM GB/s = algorithmic bytes of the block (weights in their GGUF bits + x, gain, residual, y) per step
-/ device time per step. N GPUs (torchrun): every matrix is row-sharded over the GPUs and the outputs all-gathered
-with NCCL inside the graph; the block is the same, so `value` = total algorithmic bytes / max-over-ranks time
-(strong scaling).
+/ device time per step. N GPUs (torchrun): tensor parallel by default (each rank its F / N gate / up rows and down
+columns, one ALLREDUCE of the block's output), or row-sharded with all-gathered outputs (--mp rows); the stack grows
+with N so each GPU still reads > 3x its L2, and `value` = total algorithmic bytes / max-over-ranks time.
 
 Beside the headline the line carries one object per other configuration, each measured on one GPU: `q4_0`
 (configs[0], the standalone Q4_0 GEMV [9216 x 2560]), `kquant` (configs[2], Q5_K [9216 x 2560] and the Q6_K head),
@@ -93,11 +94,25 @@ def block_list(b2, hg, hu, hd, xin=XIN, out=OUT, world=1, rank=0):
 def stack_list(b2, layers, upto=None, world=1, rank=0):
     """Command list of the layer stack (layer c: residual RES[c % 2] -> RES[(c + 1) % 2]); `upto` keeps only the
     first `upto` commands of each block (8 words each)."""
+    return np.concatenate(stack_blocks(b2, layers, upto, world, rank))
+
+
+def stack_blocks(b2, layers, upto=None, world=1, rank=0):
     parts = []
     for c, (hg, hu, hd) in enumerate(layers):
         cl = block_list(b2, hg, hu, hd, RES[c % 2], RES[(c + 1) % 2], world, rank)
         parts.append(cl[: upto * 8] if upto else cl)
-    return np.concatenate(parts)
+    return parts
+
+
+def stack_lists(b2, layers, upto=None, world=1, rank=0):
+    """The stack as command lists of at most 128 commands (a list's limit), cut between blocks at the same blocks on
+    every rank (as many blocks per list as rank 0's, the longest, fit): one step replays them in order, and the
+    ranks' lists hold the same ALLREDUCEs (a collective's slot is its place in its list)."""
+    blocks = stack_blocks(b2, layers, upto, world, rank)
+    longest = max(c.size for c in stack_blocks(b2, layers[:1], upto, world, 0)) // 8
+    per = max(1, b2.MAX_CMDS // longest)
+    return [np.concatenate(blocks[i:i + per]) for i in range(0, len(blocks), per)]
 
 
 def block_slices(mats, world: int, rank: int):
@@ -624,7 +639,7 @@ def main():
     mats = gen_block(synth, 0)
     layers = [tuple(ctx.upload(m, rows, cols, b2.Q8_0) for m, rows, cols in block_slices(mats, tw, tr))
               for _ in range(n_layers)]
-    stack = ctx.graph(stack_list(b2, layers, world=tw, rank=tr))
+    stack = [ctx.graph(cl) for cl in stack_lists(b2, layers, world=tw, rank=tr)]
     r = synth.rng(1, 99)
     x = synth.activation(r, H)
     gain = r.normal(1, 0.1, H).astype(np.float32)
@@ -635,13 +650,13 @@ def main():
     # clocks sampled from the warm-up to the end of the GPU measurements
     clk = ClockSampler(dev).__enter__()
     # warm-up
-    ctx.launch_many([stack], args.warmup)
+    ctx.launch_many(stack, args.warmup * len(stack))
     ctx.synchronize()
     barrier()
     # timed region: K steps (each a replay of the whole stack)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    ctx.launch_many([stack], args.steps)
+    ctx.launch_many(stack, args.steps * len(stack))
     end.record(stream)
     end.synchronize()
     ms = start.elapsed_time(end) / args.steps
@@ -649,17 +664,18 @@ def main():
     barrier()
     step_bytes = n_layers * algorithmic_bytes()
     value = step_bytes / (ms * 1e-3) / 1e9
-    launches = stack.kernels * args.steps
+    launches = sum(g.kernels for g in stack) * args.steps
 
     # roofline of the dominant kernel (the gate+up pass): the stack's gate+up passes alone, one graph, CUDA events
     peak, peak_kind = measured_peak()
-    ru = ctx.graph(stack_list(b2, layers, upto=3, world=tw, rank=tr))  # per layer: norm + gate/up = one GEMV kernel
-    ctx.launch_many([ru], 5)
+    # per layer: norm + gate/up = one GEMV kernel
+    ru = [ctx.graph(cl) for cl in stack_lists(b2, layers, upto=3, world=tw, rank=tr)]
+    ctx.launch_many(ru, 5 * len(ru))
     ctx.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_ru = max(20, args.steps // 4)
     s2.record(stream)
-    ctx.launch_many([ru], n_ru)
+    ctx.launch_many(ru, n_ru * len(ru))
     e2.record(stream)
     e2.synchronize()
     ru_ms = max_over_ranks(s2.elapsed_time(e2) / (n_ru * n_layers))
@@ -692,7 +708,8 @@ def main():
     t0 = time.perf_counter()
     for i in range(e2e_steps):
         ctx.write_async(XIN, xin.data_ptr() + i * 4 * H, H)
-        stack.launch()
+        for g in stack:
+            g.launch()
         ctx.read_async(y_row, yout.data_ptr() + i * 4 * H, H)
     ctx.synchronize()
     t_e2e = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
@@ -701,14 +718,15 @@ def main():
     t0 = time.perf_counter()
     for i in range(e2e_steps):
         ctx.write(XIN, xs)
-        stack.launch()
+        for g in stack:
+            g.launch()
         yout[i].numpy()[:] = ctx.read(y_row, H)
     t_sync = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
     e2e = {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
            "d2h_bytes_per_step": 4 * H, "ms_per_step": round(t_e2e * 1e3, 4),
            "host_synced": {"value": round(step_bytes / t_sync / 1e9, 2), "ms_per_step": round(t_sync * 1e3, 4)}}
 
-    for g in (stack, ru):
+    for g in stack + ru:
         g.close()
     ctx.close()
 

@@ -70,6 +70,7 @@ struct Lowering {
     std::string err;
     std::vector<std::vector<int>> users;  // direct users (VIEW nodes included)
     std::vector<int> seg;
+    std::vector<char> seg_list_end;  // the list ends after this segment
     // fusion roles
     std::vector<char> silent;   // emits nothing at its own position
     std::vector<char> storage;  // holds floats in act
@@ -147,11 +148,16 @@ struct Lowering {
 bool Lowering::validate() {
     users.assign(n, {});
     seg.assign(n, 0);
+    seg_list_end.assign(1, 0);
     int s = 0;
     for (unsigned i = 0; i < n; ++i) {
         const b200q_node &d = nd[i];
         seg[i] = s;
-        if (d.flags & B200Q_NODE_SEGMENT_END) ++s;
+        if (d.flags & B200Q_NODE_LIST_END) seg_list_end[size_t(s)] = 1;
+        if (d.flags & B200Q_NODE_SEGMENT_END) {
+            ++s;
+            seg_list_end.push_back(0);
+        }
         for (unsigned k = 0; k < B200Q_NODE_SRCS; ++k) {
             const int r = d.src[k];
             if (r < -1 || r >= int(i)) return fail(int(i), "operand %u is not an earlier node", k);
@@ -550,6 +556,10 @@ bool Lowering::emit() {
             cur.clear();
         }
         cur.insert(cur.end(), c.begin(), c.end());
+        if (seg_list_end[s]) {
+            lists.push_back(cur);
+            cur.clear();
+        }
     }
     if (!cur.empty()) lists.push_back(cur);
     return true;

@@ -431,8 +431,8 @@ class HybridDecoder:
         cmds.append(argmax(s.vocab, L.LOGITS, L.TOK))
         return cmds
 
-    def token_lists(self):
-        """The lists of one token, each at most 128 commands, cut at layer boundaries."""
+    def _blocks(self):
+        """The token's command blocks: the embedding row, one per layer, the head."""
         s, L = self.s, self.L
         blocks = [[get_row(Q4_0, s.hidden, self.handles["tok_embd"], L.TOK, L.X)]]
         j = slot = 0
@@ -444,14 +444,33 @@ class HybridDecoder:
                 blocks.append(self._gdn_layer(i, j))
                 j += 1
         blocks.append(self._head())
-        lists, cur = [], []
-        for b in blocks:
-            block = cmd_list(*b)
-            if cur and sum(c.size for c in cur) + block.size > MAX_CMDS * CMD_WORDS:
-                lists.append(cmd_list(*cur))
-                cur = []
-            cur.append(block)
-        lists.append(cmd_list(*cur))
+        return [cmd_list(*b) for b in blocks]
+
+    def list_ends(self):
+        """Indices of the blocks that end a list: as many blocks per list as fit 128 commands. Tensor parallel, every
+        rank cuts where rank 0 (whose blocks also hold the residual ADDs) cuts, so the ranks' lists hold the same
+        collectives (a collective's slot is its place in its list)."""
+        ref = self
+        if self.world > 1 and self.rank != 0:
+            import copy
+            ref = copy.copy(self)
+            ref.rank = 0
+        ends, n = [], 0
+        sizes = [b.size for b in ref._blocks()]
+        for k, sz in enumerate(sizes):
+            if n and n + sz > MAX_CMDS * CMD_WORDS:
+                ends.append(k - 1)
+                n = 0
+            n += sz
+        ends.append(len(sizes) - 1)
+        return ends
+
+    def token_lists(self):
+        """The lists of one token, each at most 128 commands, cut at layer boundaries (list_ends)."""
+        blocks, lists, start = self._blocks(), [], 0
+        for e in self.list_ends():
+            lists.append(cmd_list(*blocks[start:e + 1]))
+            start = e + 1
         return lists
 
     # ---- the same token as an op graph, for the lowering -----------------------------------------------------------
@@ -471,8 +490,9 @@ class HybridDecoder:
         g = Graph()
         names = {"rec": g.input(RECORD), "tok": g.input(16), "logits": g.input(s.vocab), "onorm": g.param(H)}
         pos, cs = g.view(names["rec"], 0, 16), g.view(names["rec"], 16, 128)
+        ends = set(self.list_ends())  # blocks that end a list: 0 the embedding row, 1 + i layer i, then the head
         x = g.get_rows(names["tok"], h["tok_embd"], Q4_0, H)
-        g.end_segment()
+        g.end_list() if 0 in ends else g.end_segment()
 
         def param(i, key, n):
             names[(i, key)] = g.param(n)
@@ -516,7 +536,7 @@ class HybridDecoder:
             xn = g.mul(g.rms_norm(x, s.eps), param(i, "ffn_norm", H))
             ff = g.swiglu(g.mul_mat(xn, h[f"{i}.gate"], Q4_0, F, H), g.mul_mat(xn, h[f"{i}.up"], Q4_0, F, H))
             x = project_out(i, ff, F, "down", x)
-            g.end_segment()
+            g.end_list() if 1 + i in ends else g.end_segment()
         xn = g.mul(g.rms_norm(x, s.eps), names["onorm"])
         v_l = s.vocab // self.world
         base = self.rank * v_l  # this rank's vocabulary rows (all rows for one rank)
@@ -526,7 +546,7 @@ class HybridDecoder:
         if self.world > 1:
             g.allgather(g.view(names["logits"], base, v_l), self.world, dst=names["logits"])
         g.argmax(names["logits"], dst=names["tok"])
-        g.end_segment()
+        g.end_list()
         return g, names
 
     def graph_act(self, names, low) -> np.ndarray:

@@ -21,7 +21,7 @@ from . import B200QError, lib
 NODE_INPUT, NODE_PARAM, NODE_VIEW, NODE_MUL_MAT, NODE_RMS_NORM, NODE_L2_NORM, NODE_MUL, NODE_ADD, NODE_SWIGLU, \
     NODE_UNARY, NODE_CONV, NODE_GDN, NODE_ROPE, NODE_ATTN, NODE_GET_ROWS, NODE_ARGMAX, NODE_ALLREDUCE, \
     NODE_ALLGATHER = range(1, 19)
-SEGMENT_END, OUTPUT = 1, 2
+SEGMENT_END, OUTPUT, LIST_END = 1, 2, 4
 SRCS = 6
 ALL_FEATURES = 0x1FFFF  # word 0 bits 0..15 and the SIGMOID_MUL bit of word 1
 
@@ -115,6 +115,10 @@ class Graph:
     def end_segment(self) -> None:
         """The last node so far closes a segment (lists are cut between segments only)."""
         self.nodes[-1]["flags"] |= SEGMENT_END
+
+    def end_list(self) -> None:
+        """The last node so far closes a segment and the list (ranks of a tensor-parallel run cut at the same places)."""
+        self.nodes[-1]["flags"] |= SEGMENT_END | LIST_END
 
     def mark_output(self, i: int) -> int:
         self.nodes[i]["flags"] |= OUTPUT

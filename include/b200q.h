@@ -437,7 +437,8 @@ B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
  *     pass (bit 15); MUL by SILU(g) becomes SILU_MUL, MUL by SIGMOID(g) (g possibly strided rows) SILU_MUL with the
  *     sigmoid flag (word 1 bit 0);
  *   - packs the commands of consecutive segments (a node with B200Q_NODE_SEGMENT_END closes one, e.g. a layer)
- *     into lists of at most 128 commands, never splitting a segment.
+ *     into lists of at most 128 commands, never splitting a segment, and ends a list after a segment holding a node
+ *     flagged B200Q_NODE_LIST_END.
  * No counterpart type in the reference: it stands for the ggml_cgraph the reference's backend receives. */
 #define B200Q_NODE_INPUT 1u     /* n floats the caller writes before the lists run (or a buffer commands fill) */
 #define B200Q_NODE_PARAM 2u     /* n resident floats the caller writes once (norm weights, conv kernels, states) */
@@ -463,6 +464,9 @@ B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
                                   * own part of dst */
 #define B200Q_NODE_SEGMENT_END 1u  /* flags: the last node of a segment (lists are cut between segments) */
 #define B200Q_NODE_OUTPUT 2u       /* flags: the caller reads the tensor after the lists (it is kept, not fused away) */
+#define B200Q_NODE_LIST_END 4u     /* flags: the list ends with this node's segment (tensor-parallel ranks whose
+                                    * segments differ in length cut their lists at the same segments this way, so
+                                    * their lists hold the same collectives) */
 #define B200Q_NODE_SRCS 6u
 typedef struct b200q_node {
     uint32_t op, flags;
