@@ -357,6 +357,37 @@ def batch_bench(b2, torch, synth, dev: int, world: int) -> dict:
     return out
 
 
+def prefill_bench(b2, torch, synth, dev: int, world: int, batch8_rows_per_s: float | None) -> dict:
+    """The prompt's matrix product on the tensor cores: a GEMV_BATCH command of T > 8 rows (tokens) runs as the token
+    quantizer plus the tcgen05 GEMM (int8 MMA per 32-value block, FP32 block terms in block order, every output the
+    GEMV's bits). Q4_0 [9216 x 2560] (the configs[0] matrix), 4 distinct copies per list, T = 128 and 512; per T the
+    time per command, tokens per second (against the batch kernel's 8 rows per weight read) and the int8 MAC rate."""
+    if world > 1:
+        return {"note": "measured on one GPU only"}
+    rows, cols, n = 9216, H, 4
+    ctx = b2.Context(device=dev, weight_bytes=n * (b2.weight_device_bytes(rows, cols, b2.Q4_0) + (1 << 20)),
+                     act_floats=1 << 24)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", dev))
+    r = synth.rng(0, 2)
+    w = synth.q4_0(r, rows, cols)
+    tmax = 512
+    ctx.write(0, np.concatenate([synth.activation(r, cols) for _ in range(tmax)]))
+    hs = [ctx.upload(w, rows, cols, b2.Q4_0) for _ in range(n)]
+    out = {"workload": "GEMV_BATCH of T tokens x Q4_0 [9216x2560] (configs[0] matrix) on the tensor cores", "copies": n}
+    y0 = tmax * cols
+    for t in (128, tmax):
+        cl = b2.cmd_list(*[b2.gemv_batch(b2.Q4_0, rows, cols, h, 0, y0 + (i % 2) * t * rows, t) for i, h in enumerate(hs)])
+        ms, kernels = timed_graph(ctx, torch, stream, cl, 20)
+        us = ms * 1e3 / n
+        tok_s = t / (us * 1e-6)
+        out[f"t{t}"] = {"us_per_command": round(us, 3), "tokens_per_s": round(tok_s, 1),
+                        "int8_tops": round(2.0 * rows * cols * t / (us * 1e-6) / 1e12, 2),
+                        "weight_gbs": round(w.nbytes / (us * 1e-6) / 1e9, 1), "kernels_per_command": kernels / n,
+                        "vs_batch8": round(tok_s / batch8_rows_per_s, 2) if batch8_rows_per_s else None}
+    ctx.close()
+    return out
+
+
 def gdn_bench(b2, torch, synth, dev: int, world: int, steps: int = 128) -> dict:
     """128 sequential Gated DeltaNet decode steps (hidden 2560, 16 heads, d_k = d_v = 128): the causal
     conv1d (k = 4) over the qkv projection with its 3-token state, the step with L2-normalized q / k, the gates from
@@ -730,11 +761,12 @@ def main():
         g.close()
     ctx.close()
 
-    q40 = gdn = batch = {}
+    q40 = gdn = batch = prefill = {}
     if not args.no_extras:
         q40 = q4_0_bench(b2, torch, synth, dev, world)
         gdn = gdn_bench(b2, torch, synth, dev, world)
         batch = batch_bench(b2, torch, synth, dev, world)
+        prefill = prefill_bench(b2, torch, synth, dev, world, batch.get("m8", {}).get("rows_per_s"))
     decode = run_decodes()
     kquant = kquant_bench(b2, torch, synth, dev, world, max_over_ranks, barrier) if not args.no_kquant else {}
     clk.__exit__(None, None, None)
@@ -754,7 +786,7 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": DATA, "config": config,
                 "frac_of_peak": round(value / (peak * world), 4), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks, "q4_0": q40, "kquant": kquant, "gdn_step": gdn, "gemv_batch": batch,
-                "decode": decode}
+                "prefill": prefill, "decode": decode}
         print(json.dumps(line), flush=True)
     return 0
 

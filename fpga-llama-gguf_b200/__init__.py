@@ -27,7 +27,7 @@ OP_GEMV, OP_RMSNORM, OP_ADD, OP_SILU_MUL, OP_MUL, OP_UNARY, OP_GDN, OP_CONV = 1,
 OP_STATE_LOAD, OP_ROPE, OP_TRACE = 9, 10, 11
 OP_ATTN, OP_ARGMAX, OP_GET_ROW, OP_ALLREDUCE, OP_ALLGATHER = 12, 13, 14, 15, 16  # extensions of this library
 OP_GEMV_BATCH = 17
-BATCH_MAX = 8  # activation rows of one GEMV_BATCH
+BATCH_MAX = 8  # activation rows of one gemv_batch_kernel launch (more: the tensor-core GEMM)
 GEMV_SWIGLU, GEMV_CONV, GEMV_ADD = 0x100, 0x200, 0x400
 GDN_WITH_GEMV, GDN_L2_QK, GDN_GATED, GDN_GATES, GDN_WITH_OUT = 1, 2, 4, 8, 16
 NORM_L2, NORM_NO_WEIGHT, NORM_DEFER = 1, 2, 4
@@ -148,8 +148,9 @@ def allgather(n: int, x_off: int, y_off: int) -> np.ndarray:
 
 def gemv_batch(fmt: int, rows: int, cols: int, w_off: int, x_off: int, y_off: int, batch: int,
                flags: int = 0) -> np.ndarray:
-    """GEMV_BATCH extension: y_m = W x_m (flags GEMV_ADD: + y_m) for m < batch <= BATCH_MAX; x rows `cols` floats
-    apart from x_off, y rows round16(rows) floats apart from y_off; the weights are read once for all rows."""
+    """GEMV_BATCH extension: y_m = W x_m (flags GEMV_ADD: + y_m) for m < batch <= 65536; x rows `cols` floats apart
+    from x_off, y rows round16(rows) floats apart from y_off. Up to BATCH_MAX rows one kernel reads the weights once
+    for all rows; more rows run as the tensor-core GEMM (prefill)."""
     return cmd(OP_GEMV_BATCH, fmt | flags | ((batch - 1) << 16), rows, cols, w_off & 0xFFFFFFFF, w_off >> 32,
                x_off, y_off)
 
@@ -693,8 +694,15 @@ class Context:
         return q, scales, bs
 
     def debug_block_sums(self, command: np.ndarray) -> np.ndarray:
+        """Integer block sums of one GEMV command (rows x blocks), or of a GEMV_BATCH command of more than
+        BATCH_MAX rows: block 0 of weight rows 0..127 x batch rows 0..127 (a 128 x 128 array, the GEMM's MMA)."""
         c = np.ascontiguousarray(command, dtype=np.uint32)
         fmt, rows, cols = int(c[1]) & 0xFF, int(c[2]), int(c[3])
+        if int(c[0]) == OP_GEMV_BATCH and (int(c[1]) >> 16) + 1 > BATCH_MAX:
+            out = np.zeros(128 * 128, dtype=np.int32)
+            self._check(lib().b200q_debug_block_sums(self.h, c.ctypes.data_as(ctypes.c_void_p),
+                                                     out.ctypes.data_as(ctypes.c_void_p)))
+            return out.reshape(128, 128)
         n = rows * (cols // 256) * 9 if fmt in (Q5_K, Q6_K) else rows * (cols // 32)
         out = np.zeros(n, dtype=np.int32)
         self._check(lib().b200q_debug_block_sums(self.h, c.ctypes.data_as(ctypes.c_void_p),

@@ -115,6 +115,13 @@ struct b200q_ctx {
     // layout), two alternating buffers
     uint8_t *qimg[2] = {nullptr, nullptr};
     double *nsq[2] = {nullptr, nullptr};  // per-panel sums of squares handed to a deferred norm (alternating)
+    // quantized tokens of GEMV_BATCH commands of more than kBatchMax rows (the tensor-core GEMM's image), sized
+    // before a list runs or is captured; a buffer replaced by a larger one stays allocated until the context ends
+    // (captured graphs may still use it)
+    uint8_t *gemm_img = nullptr;
+    size_t gemm_img_bytes = 0;
+    std::vector<uint8_t *> gemm_img_old;
+    int32_t *gemm_sums = nullptr;  // debug: where the next GEMM stores its first block's integer sums
     float *snap = nullptr;
     size_t snap_used = 0;
     unsigned *dstatus = nullptr;
@@ -626,7 +633,6 @@ int exec_gdn(b200q_ctx *c, const Pass &p, const ImageLink &nsq_link) {
     return 0;
 }
 
-static_assert(kBatchRows == kBatchMax, "the planner's and the kernel's GEMV_BATCH row limits agree");
 
 int exec_ext(b200q_ctx *c, const Pass &p) {
     const uint32_t *cmd = p.cmd[0];
@@ -688,10 +694,31 @@ int exec_ext(b200q_ctx *c, const Pass &p) {
         if (!w) return set_err(c, B200Q_ERR_ARG, "GEMV_BATCH: unknown weight");
         if (c->world > 1 && !c->explicit_comm)
             return set_err(c, B200Q_ERR_ARG, "GEMV_BATCH: not in a row-sharded context (its matrices hold a row slice)");
+        const unsigned batch = ((cmd[1] >> 16) & 0xffffu) + 1u;
+        if (batch > kBatchMax) {  // prefill: the tokens quantized once, then the tensor-core GEMM
+            GemmArgs g;
+            g.w = view_of(c, *w);
+            g.x = A + cmd[6];
+            g.cols = cmd[3];
+            g.tokens = batch;
+            g.act = (cmd[1] & 0xffu) == 3u ? 1u : 0u;
+            g.xq = c->gemm_img;
+            g.y = A + cmd[7];
+            g.ystride = (cmd[2] + 15u) & ~15u;
+            g.add = (cmd[1] & B200Q_GEMV_ADD) != 0;
+            g.err = c->dstatus + 1;
+            g.sums = c->gemm_sums;
+            if (!g.xq || c->gemm_img_bytes < gemm_image_bytes(g.cols, batch))
+                return set_err(c, B200Q_ERR_STATE, "GEMV_BATCH: token image not prepared");
+            if ((rc = flush_wait(c))) return rc;
+            CUDA_TRY(c, launch_gemm(g, c->stream, c->pdl));
+            c->launches += 2;  // the quantizer and the GEMM
+            return 0;
+        }
         BatchArgs a;
         a.w = view_of(c, *w);
         a.cols = cmd[3];
-        a.batch = ((cmd[1] >> 16) & 0xffu) + 1u;
+        a.batch = batch;
         a.act = (cmd[1] & 0xffu) == 3u ? 1u : 0u;
         a.x = A + cmd[6];
         a.y = A + cmd[7];
@@ -911,6 +938,28 @@ int exec_chain(b200q_ctx *c, ChainArgs &a) {
 }
 
 // Executes the passes of a plan on the context stream (no synchronization).
+// The image of the quantized tokens that the list's GEMV_BATCH commands of more than kBatchMax rows need, allocated
+// before the list runs or is captured (no allocation inside a capture).
+int prepare_gemm_image(b200q_ctx *c, const Plan &plan) {
+    size_t need = 0;
+    for (const Pass &p : plan.passes) {
+        if (p.op != 17 || p.kind != PassKind::Ext) continue;
+        const unsigned batch = ((p.cmd[0][1] >> 16) & 0xffffu) + 1u;
+        if (batch > kBatchMax) need = std::max(need, gemm_image_bytes(p.cmd[0][3], batch));
+    }
+    if (need <= c->gemm_img_bytes) return 0;
+    uint8_t *img = nullptr;
+    const cudaError_t e = cudaMalloc(&img, need);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(c, B200Q_ERR_NOMEM, "GEMV_BATCH token image (%zu bytes): %s", need, cudaGetErrorString(e));
+    }
+    if (c->gemm_img) c->gemm_img_old.push_back(c->gemm_img);
+    c->gemm_img = img;
+    c->gemm_img_bytes = need;
+    return 0;
+}
+
 int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
     c->launches = 0;
@@ -1163,6 +1212,8 @@ void b200q_destroy(b200q_ctx *c) {
     cudaFree(c->kv);
     cudaFree(c->attn_part);
     cudaFree(c->xq);
+    cudaFree(c->gemm_img);
+    for (uint8_t *p : c->gemm_img_old) cudaFree(p);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1349,6 +1400,7 @@ int b200q_run_async(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds) {
     if (!cmds) return B200Q_ERR_ARG;
     const Plan plan = plan_list(cmds, n_cmds, limits_of(c));
     if (plan.status == 129) return 129;
+    if ((rc = prepare_gemm_image(c, plan))) return rc;
     if ((rc = exec_plan(c, plan, n_cmds))) return rc;
     if (plan.status) c->err = plan.error;
     return plan.status;
@@ -1457,6 +1509,7 @@ int b200q_graph_create(b200q_ctx *c, const uint32_t *cmds, unsigned n_cmds, b200
         c->err = plan.error;
         return plan.status;
     }
+    if ((rc = prepare_gemm_image(c, plan))) return rc;
     b200q_graph *g = new b200q_graph();
     g->ctx = c;
     CUDA_TRY(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
@@ -1590,6 +1643,25 @@ int b200q_debug_block_sums(b200q_ctx *c, const uint32_t cmd[8], int32_t *out) {
     if (rc) return rc;
     if (!cmd || !out) return B200Q_ERR_ARG;
     std::lock_guard<std::mutex> lock(c->mu);
+    if (cmd[0] == 17u && ((cmd[1] >> 16) & 0xffffu) + 1u > kBatchMax) {
+        // the tensor-core GEMM of a GEMV_BATCH command: the int32 sums of block 0 for rows and tokens 0..127
+        const Plan plan = plan_list(cmd, 1, limits_of(c));
+        if (plan.status) return set_err(c, B200Q_ERR_ARG, "debug_block_sums: invalid GEMV_BATCH (%s)", plan.error.c_str());
+        const size_t count = size_t(kGemmRows) * kGemmTokens;
+        int32_t *d = nullptr;
+        CUDA_TRY(c, cudaMalloc(&d, count * 4));
+        cudaMemset(d, 0, count * 4);
+        c->gemm_sums = d;
+        rc = prepare_gemm_image(c, plan);
+        if (!rc) rc = exec_plan(c, plan, 1);
+        c->gemm_sums = nullptr;
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (!rc && e == cudaSuccess) e = cudaMemcpy(out, d, count * 4, cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        if (rc) return rc;
+        if (e != cudaSuccess) return set_err(c, B200Q_ERR_CUDA, "debug_block_sums: %s", cudaGetErrorString(e));
+        return check_device_status(c);
+    }
     uint32_t one[8];
     std::memcpy(one, cmd, sizeof(one));
     one[1] &= 0xffu;  // no epilogue

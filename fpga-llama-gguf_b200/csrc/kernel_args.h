@@ -189,4 +189,23 @@ struct BatchArgs {
     unsigned *err = nullptr;      // set when a bounded wait runs out
 };
 
+// GEMV_BATCH of more than kBatchMax rows (prefill): the rows ("tokens") quantized once into an image in global
+// memory, then Y = W X on the tensor cores. Image layout for `tpad` tokens (a multiple of kGemmTokens, the tokens past
+// `tokens` zero): the 32 quants of (block b, token t) at xq + (b tpad + t) 32 (values 0..15, then 16..31), d and s of
+// Q8_0 / Q8_1 at xd / xs + b tpad + t (FP32 holding the FP16-rounded values).
+constexpr unsigned kGemmRows = 128;    // weight rows per tile (the MMA's M)
+constexpr unsigned kGemmTokens = 128;  // tokens per tile (the MMA's N)
+struct GemmArgs {
+    MatrixView w;
+    const float *x = nullptr;     // token t at x + t * cols
+    unsigned cols = 0, tokens = 0, tpad = 0;
+    unsigned act = 0;             // 0 Q8_0 (Q4_0, Q8_0 weights), 1 Q8_1 (Q4_1)
+    uint8_t *xq = nullptr;        // the image (device scratch, gemm_image_bytes)
+    float *xd = nullptr, *xs = nullptr;
+    float *y = nullptr;           // token t at y + t * ystride
+    unsigned ystride = 0, add = 0;
+    unsigned *err = nullptr;      // set when a bounded wait runs out
+    int32_t *sums = nullptr;      // optional: the integer block sums of block 0 of tile (0, 0), [128 rows][128 tokens]
+};
+
 }  // namespace b200q

@@ -108,6 +108,10 @@ cudaError_t launch_quantize(const QuantArgs &a, cudaStream_t st);
 // launches of one command (the quantizer, then one or more batch launches)
 unsigned gemv_batch_rows_per_launch(const MatrixView &w, unsigned cols);
 cudaError_t launch_gemv_batch(const BatchArgs &a, unsigned sms, cudaStream_t st, bool pdl);
+// GEMV_BATCH of more than kBatchMax rows: bytes of the quantized-token image, and the two launches (quantizer,
+// tensor-core GEMM); a.xq must hold gemm_image_bytes(a.cols, a.tokens) bytes.
+size_t gemm_image_bytes(unsigned cols, unsigned tokens);
+cudaError_t launch_gemm(GemmArgs a, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *y, unsigned n, unsigned rows, unsigned stride,
                            float eps, unsigned flags, const PeerWait &pw, cudaStream_t st, bool pdl);
 cudaError_t launch_ew(const EwArgs &a, cudaStream_t st, bool pdl);

@@ -135,7 +135,7 @@ void pass_writes(const Pass &p, std::vector<std::pair<size_t, size_t>> &w) {
         else if (p.op == 14) w.push_back({c[6], c[2]});
         else if (p.op == 15) w.push_back({c[3], c[1]});
         else if (p.op == 16) w.push_back({c[3], size_t(c[1]) * kMaxRanks});
-        else if (p.op == 17) w.push_back({c[7], size_t((c[1] >> 16 & 0xffu) + 1u) * round16(c[2])});
+        else if (p.op == 17) w.push_back({c[7], size_t((c[1] >> 16 & 0xffffu) + 1u) * round16(c[2])});
         break;
     default: break;
     }
@@ -571,12 +571,12 @@ Plan plan_list(const uint32_t *cmds, unsigned n_cmds, const Limits &lim) {
             p.kind = PassKind::Ext;
         } else if (op == 17) {
             // ---- GEMV_BATCH extension: y_m = W x_m (+ y_m) for m < batch, x rows cols apart, y rows round16(rows)
-            const unsigned fmt = cmd[1] & 0xffu, fl = cmd[1] & 0xff00u, batch = ((cmd[1] >> 16) & 0xffu) + 1u;
+            const unsigned fmt = cmd[1] & 0xffu, fl = cmd[1] & 0xff00u, batch = ((cmd[1] >> 16) & 0xffffu) + 1u;
             const unsigned rows = cmd[2], cols = cmd[3];
             const uint64_t h = uint64_t(cmd[4]) | (uint64_t(cmd[5]) << 32);
             const size_t xs = size_t(batch) * cols, ys = size_t(batch) * round16(rows);
-            bool ok = (fmt == 2 || fmt == 3 || fmt == 8) && (fl == 0 || fl == 0x400u) && (cmd[1] >> 24) == 0 &&
-                      batch <= kBatchRows && rows != 0 && rows <= kMaxRows && cols != 0 && cols <= kMaxCols &&
+            bool ok = (fmt == 2 || fmt == 3 || fmt == 8) && (fl == 0 || fl == 0x400u) && batch <= kBatchRows &&
+                      rows != 0 && rows <= kMaxRows && cols != 0 && cols <= kMaxCols &&
                       cols % 128 == 0 && cmd[6] % 16 == 0 && cmd[7] % 16 == 0 && C.act(cmd[6], xs) &&
                       C.act(cmd[7], ys) && !ranges_meet(cmd[6], xs, cmd[7], ys);
             if (ok && lim.check_weights) {

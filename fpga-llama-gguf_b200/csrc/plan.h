@@ -17,7 +17,7 @@
 namespace b200q {
 
 constexpr unsigned kMaxRows = 65536, kMaxCols = 16384, kPairRows = 16384, kAddRows = 16384;
-constexpr unsigned kBatchRows = 8;  // GEMV_BATCH: activation rows per command (kernel_args.h kBatchMax)
+constexpr unsigned kBatchRows = 65536;  // GEMV_BATCH: activation rows per command (the 16-bit batch field)
 constexpr unsigned kBufWords = 4096, kMaxNormRows = 4096, kMaxConvChannels = 16384, kNxFloats = 16384;
 constexpr unsigned kMaxHeads = 32, kStateUnits = 4, kHead = 128, kMaxBlockedRows = 512 * 20;
 constexpr unsigned kMaxRopeDims = 128;

@@ -207,4 +207,41 @@ __device__ __forceinline__ void write_image_block(uint8_t *img, unsigned n, unsi
     }
 }
 
+// One 32-value block of an activation row quantized to Q8_0 / Q8_1 by one thread from registers: the arithmetic of
+// quant_block_q80 (gemvq_ref.h:196-245), the image words of an XBlock (values 0..15, 16..31, {d, s, sum of q, 0}).
+__device__ __forceinline__ void batch_quant_block(const float *x32, bool q81, uint4 &q0, uint4 &q1, uint4 &meta) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = reinterpret_cast<const float4 *>(x32)[i];
+        v[4 * i] = f.x;
+        v[4 * i + 1] = f.y;
+        v[4 * i + 2] = f.z;
+        v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    const float sc = fdiv(amax, 127.0f);
+    const float id = sc != 0.0f ? fdiv(1.0f, sc) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int q = int(roundf(fmul(v[4 * k + e], id)));
+            sum += q;
+            word |= uint32_t(q & 0xff) << (8 * e);
+        }
+        w[k] = word;
+    }
+    q0 = make_uint4(w[0], w[1], w[2], w[3]);
+    q1 = make_uint4(w[4], w[5], w[6], w[7]);
+    const float d = half_bits_to_float(float_to_half_bits(sc));
+    const float s8 = q81 ? half_bits_to_float(float_to_half_bits(fmul(float(sum), sc))) : 0.0f;
+    meta = make_uint4(__float_as_uint(d), __float_as_uint(s8), uint32_t(sum), 0u);
+}
+
 }  // namespace b200q

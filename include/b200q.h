@@ -82,12 +82,15 @@ extern "C" {
  * rank y = x. x and y are disjoint, or x is rank r's own part of y. */
 #define B200Q_OP_ALLGATHER 16u
 /* [17, format | flags | (batch - 1) << 16, rows, cols, w_off lo, w_off hi, x_off, y_off]: y_m = W x_m for m < batch
- * (at most 8), x_m the cols floats at x_off + m cols, y_m the rows floats at y_off + m round16(rows) (zero padding up
- * to a multiple of 16, as a GEMV's y); flags 0 or B200Q_GEMV_ADD (y_m = W x_m + y_m). Formats Q4_0, Q8_0, Q4_1;
- * cols a multiple of 128; the x and y ranges disjoint; not in a row-sharded context. The weights are read once for
- * all rows (when the rows' quantized images and term buffers do not fit one CTA's shared memory, once per group of
- * rows), and every y_m has the bits of the GEMV command on x_m. A GEMV_BATCH does not consume a deferred RMSNORM:
- * it reads x as act holds it. The batch path of the reference's roadmap (docs/ROADMAP.md:80-96, P2). */
+ * (1 to 65536), x_m the cols floats at x_off + m cols, y_m the rows floats at y_off + m round16(rows) (zero padding
+ * up to a multiple of 16, as a GEMV's y); flags 0 or B200Q_GEMV_ADD (y_m = W x_m + y_m). Formats Q4_0, Q8_0, Q4_1;
+ * cols a multiple of 128; the x and y ranges disjoint; not in a row-sharded context. Every y_m has the bits of the
+ * GEMV command on x_m. Up to 8 rows: one kernel reads the weights once for all rows (when the rows' quantized images
+ * and term buffers do not fit one CTA's shared memory, once per group of rows). More rows (prefill): the rows are
+ * quantized once into a device image the context allocates (before the list runs or is captured), then a tensor-core
+ * GEMM (int8 MMA per 32-value block, FP32 block terms in block order) takes tiles of 128 weight rows x 128 rows.
+ * A GEMV_BATCH does not consume a deferred RMSNORM: it reads x as act holds it. The batch path of the reference's
+ * roadmap (docs/ROADMAP.md:80-96, P2), and the prompt's matrix products. */
 #define B200Q_OP_GEMV_BATCH 17u
 
 #define B200Q_GEMV_SWIGLU 0x100u
@@ -322,7 +325,9 @@ B200Q_API int b200q_debug_quantize(b200q_ctx *ctx, unsigned format, size_t x_off
                          float norm_eps, unsigned norm_flags, int8_t *q, void *scales, int32_t *bsums);
 /* Per-block integer dot products of one GEMV command (Q4_0/Q8_0: rows x cols/32 int32 sumi, the ints that scale
  * into each FP32 term; Q5_K/Q6_K: rows x cols/256 x 9 int32: the 8 lane sums of the scaled products, then the
- * mins sum (0 for Q6_K); Q4_1: rows x cols/32). */
+ * mins sum (0 for Q6_K); Q4_1: rows x cols/32). For a GEMV_BATCH command of more than 8 rows (the tensor-core
+ * GEMM, which it runs): the 128 x 128 int32 sums of block 0 of weight rows 0..127 and batch rows 0..127, row-major
+ * by weight row (entries of batch rows past the batch: 0). */
 B200Q_API int b200q_debug_block_sums(b200q_ctx *ctx, const uint32_t cmd[8], int32_t *out);
 
 /* ---- the activation quantizer without a context and without allocation -------------------------------------

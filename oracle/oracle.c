@@ -942,13 +942,12 @@ ORC_API int orc_run_list(float *act, size_t act_floats, float *state, size_t sta
             }
             orc_dequantize_row(w->data + (size_t)row * orc_row_bytes(cols, fmt), cols, fmt, M.act + c[6]);
         } else if (op == 17) { /* GEMV_BATCH extension: y_m = W x_m (+ y_m) for m < batch, as batch GEMV commands */
-            const unsigned fmt = c[1] & 0xffu, fl = c[1] & 0xff00u, batch = ((c[1] >> 16) & 0xffu) + 1u;
+            const unsigned fmt = c[1] & 0xffu, fl = c[1] & 0xff00u, batch = ((c[1] >> 16) & 0xffffu) + 1u;
             const unsigned rows = c[2], cols = c[3], ys = (rows + 15u) / 16u * 16u;
             const uint64_t h = (uint64_t)c[4] | ((uint64_t)c[5] << 32);
             const orc_weight *w = find_w(M.ws, M.nw, h);
             const size_t xn = (size_t)batch * cols, yn = (size_t)batch * ys;
-            if ((fmt != 2 && fmt != 3 && fmt != 8) || (fl != 0 && fl != 0x400u) || (c[1] >> 24) != 0 || batch > 8 ||
-                rows == 0 || rows > 65536 || cols == 0 || cols > 16384 || cols % 128 || c[6] % 16 || c[7] % 16 ||
+            if ((fmt != 2 && fmt != 3 && fmt != 8) || (fl != 0 && fl != 0x400u) || rows == 0 || rows > 65536 || cols == 0 || cols > 16384 || cols % 128 || c[6] % 16 || c[7] % 16 ||
                 !in_act(&M, c[6], xn) || !in_act(&M, c[7], yn) || (c[6] < c[7] + yn && c[7] < c[6] + xn) || !w ||
                 w->format != fmt || w->cols != cols || w->rows != rows) {
                 status = (int)i + 1;

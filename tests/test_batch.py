@@ -1,6 +1,7 @@
 """GEMV_BATCH (opcode 17, no GPU): the host planner's validation agrees with the oracle's interpreter on valid and
 invalid commands, and the oracle's batch command is, row by row, the GEMV command on each activation row (with the
-ADD flag: plus the old y row; y rows zero-padded to a multiple of 16). The GPU kernel is held to the same in
+ADD flag: plus the old y row; y rows zero-padded to a multiple of 16), for a few rows and for more than 8 (the
+batch field is 16 bits wide; the GPU runs those as the tensor-core GEMM). The GPU kernel is held to the same in
 tests/test_gpu_batch.py."""
 import numpy as np
 import pytest
@@ -22,7 +23,7 @@ def _act(n=1 << 17, seed=0):
     return rng(121, seed).normal(0, 1, n).astype(np.float32)
 
 
-@pytest.mark.parametrize("h,batch", [(H1, 1), (H1, 5), (H2, 8), (H3, 3)])
+@pytest.mark.parametrize("h,batch", [(H1, 1), (H1, 5), (H2, 8), (H3, 3), (H1, 9), (H2, 40), (H3, 130)])
 @pytest.mark.parametrize("add", [False, True])
 def test_oracle_batch_is_the_gemv_of_every_row(b2, orc, synth, h, batch, add):
     ws = _weights(synth)
@@ -50,11 +51,12 @@ def _status(b2, orc, ws, cmd):
 def test_planner_and_oracle_agree_on_valid_and_invalid_batches(b2, orc, synth):
     ws = _weights(synth)
     gb = b2.gemv_batch
-    valid = [gb(2, 100, 256, H1, X, Y, 8), gb(8, 64, 512, H2, X, Y, 2, b2.GEMV_ADD), gb(3, 48, 384, H3, 256, Y, 1)]
+    valid = [gb(2, 100, 256, H1, X, Y, 8), gb(8, 64, 512, H2, X, Y, 2, b2.GEMV_ADD), gb(3, 48, 384, H3, 256, Y, 1),
+             gb(2, 100, 256, H1, X, Y, 9), gb(8, 64, 512, H2, X, Y, 100)]  # more than 8 rows: the GEMM
     for cmd in valid:
         assert _status(b2, orc, ws, cmd) == (0, 0)
     invalid = [
-        gb(2, 100, 256, H1, X, Y, 9),                    # more than 8 rows
+        gb(2, 100, 256, H1, X, Y, 300),                  # 300 rows of x reach into y
         gb(2, 100, 256, H1, X, 512, 4),                  # y overlaps x
         gb(2, 100, 256, H1, X, Y, 2, b2.GEMV_SWIGLU),    # no epilogue but ADD
         gb(2, 100, 256, H1, 8, Y, 2),                    # x not 16-aligned
