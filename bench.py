@@ -583,6 +583,8 @@ def main():
                     "per projection (default); rows = every matrix row-sharded by the library, outputs all-gathered")
     ap.add_argument("--decode-only", action="store_true", help="run only the decode measurement (for profiling "
                     "runs); the line then carries the decode object and no GEMV metric")
+    ap.add_argument("--prefill-only", action="store_true", help="run only the prefill GEMM measurement (for "
+                    "profiling runs); the line then carries the prefill object and no GEMV metric")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -649,6 +651,15 @@ def main():
             out[key] = decode_bench(b2, torch, dist, dev, world, rank, shape, label, args.decode_tokens,
                                     max(3, min(args.warmup, 16)), max_over_ranks, barrier, args.mp)
         return out
+
+    if args.prefill_only:
+        prefill = prefill_bench(b2, torch, synth, dev, world, None)
+        if dist:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"metric": "prefill tokens/s", "n_gpus": world, "impl": "b200q", "mode": "prefill-only",
+                              "data": "synthetic", "prefill": prefill}), flush=True)
+        return 0
 
     if args.decode_only:
         decode = run_decodes()
