@@ -98,6 +98,9 @@ struct Lowering {
     }
     int src(int i, int k) const { return nd[i].src[k]; }
     bool is(int i, uint32_t op) const { return i >= 0 && nd[i].op == op; }
+    // a MUL_MAT of one activation row (a GEMV, which the fusions may join); one of several rows (u[0] > 1) is a
+    // GEMV_BATCH of its own
+    bool gemv_mm(int i) const { return is(i, B200Q_NODE_MUL_MAT) && nd[i].u[0] <= 1; }
     bool output(int i) const { return (nd[i].flags & B200Q_NODE_OUTPUT) != 0; }
     // the non-VIEW nodes that read i, directly or through views of it
     void real_readers(int i, std::vector<int> &out) const {
@@ -182,7 +185,7 @@ bool Lowering::validate() {
             const int t = d.dst, tb = nd[t].op == B200Q_NODE_VIEW ? nd[t].src[0] : t;
             if (nd[tb].op != B200Q_NODE_INPUT || !contiguous(t) || nd[t].n < d.n)
                 return fail(int(i), "dst must be a contiguous INPUT region of at least n floats");
-            if (d.op == B200Q_NODE_MUL_MAT && d.rows % 16 && nd[t].n < round16(d.rows))
+            if (d.op == B200Q_NODE_MUL_MAT && d.u[0] <= 1 && d.rows % 16 && nd[t].n < round16(d.rows))
                 return fail(int(i), "a GEMV pads its output to 16 floats: dst needs that room");
             if (d.op == B200Q_NODE_ARGMAX && nd[t].n < 16) return fail(int(i), "ARGMAX writes into 16 floats of dst");
         }
@@ -207,7 +210,7 @@ void Lowering::fuse() {
     for (unsigned i = 0; i < n; ++i)
         if (nd[i].op == B200Q_NODE_VIEW) storage[i] = 0;
     const auto plain_mm = [&](int m, int reader) {
-        return is(m, B200Q_NODE_MUL_MAT) && !silent[size_t(m)] && only_reader(m, reader) && add_epi[size_t(m)] < 0 &&
+        return gemv_mm(m) && !silent[size_t(m)] && only_reader(m, reader) && add_epi[size_t(m)] < 0 &&
                conv_epi[size_t(m)] < 0;
     };
     // ---- the DeltaNet step's folds first (their nodes are then not fused otherwise)
@@ -354,7 +357,7 @@ void Lowering::fuse() {
         real_readers(int(i), rr);
         bool ok = !rr.empty();
         for (int r : rr)
-            ok = ok && is(r, B200Q_NODE_MUL_MAT) && src(r, 0) == int(i) && seg[size_t(emit_at[size_t(r)])] == seg[i];
+            ok = ok && gemv_mm(r) && src(r, 0) == int(i) && seg[size_t(emit_at[size_t(r)])] == seg[i];
         if (ok) deferred[i] = 1;
     }
     // ---- SILU / SIGMOID folded into the MUL that reads them
@@ -388,7 +391,7 @@ void Lowering::fuse() {
             m = int(j);
             break;
         }
-        if (m >= 0 && is(m, B200Q_NODE_MUL_MAT) && src(m, 0) == y && nd[m].cols == hv * kHead &&
+        if (m >= 0 && gemv_mm(m) && src(m, 0) == y && nd[m].cols == hv * kHead &&
             (hv * kHead) % 256 == 0 && nd[m].rows <= kMaxBlockedRows && conv_epi[size_t(m)] < 0 &&
             seg[size_t(m)] == seg[size_t(G)]) {
             f.with_out = m;
@@ -439,7 +442,13 @@ bool Lowering::emit() {
         if (!b200q_node_supported(nd, ii)) return fail(i, "not supported (operands, sizes or format)");
         switch (d.op) {
         case B200Q_NODE_MUL_MAT:
-            emit_gemv_with_epilogue(i, i);
+            if (d.u[0] > 1) {  // several activation rows, cols floats apart: one GEMV_BATCH command
+                if (!contiguous(src(i, 0))) return fail(i, "the activation rows of a batched MUL_MAT must be contiguous");
+                push(i, {17u, d.fmt | ((d.u[0] - 1u) << 16), d.rows, d.cols, uint32_t(d.weight),
+                         uint32_t(d.weight >> 32), o32(src(i, 0)), o32(i)});
+            } else {
+                emit_gemv_with_epilogue(i, i);
+            }
             break;
         case B200Q_NODE_SWIGLU:
             if (pair_g[ii] >= 0) {
@@ -586,6 +595,11 @@ int b200q_node_supported(const b200q_node *nodes, unsigned i) {
     case B200Q_NODE_VIEW:
         return 1;
     case B200Q_NODE_MUL_MAT: {
+        if (d.u[0] > 1)  // batched: GEMV_BATCH (Q8_0 family), y rows round16(rows) floats apart
+            return (d.fmt == 2 || d.fmt == 3 || d.fmt == 8) && d.rows >= 1 && d.rows <= kMaxRows && d.cols >= 1 &&
+                   d.cols <= kMaxCols && d.cols % 128 == 0 && d.u[0] <= 65536u &&
+                   size_t(d.n) == size_t(d.u[0]) * round16(d.rows) && has(0) &&
+                   size_t(n_of(0)) == size_t(d.u[0]) * d.cols;
         const bool kq = d.fmt == 13 || d.fmt == 14;
         return (d.fmt == 2 || d.fmt == 3 || d.fmt == 8 || kq) && d.rows >= 1 && d.rows <= kMaxRows && d.cols >= 1 &&
                d.cols <= kMaxCols && d.cols % (kq ? 256u : 128u) == 0 && d.n == d.rows && has(0) && n_of(0) == d.cols;

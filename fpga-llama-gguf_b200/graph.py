@@ -67,7 +67,12 @@ class Graph:
         return self._add(NODE_VIEW, row * rows, [src], u=[offset, row, stride or row, rows])
 
     # ops
-    def mul_mat(self, x: int, weight: int, fmt: int, rows: int, cols: int, dst: int = -1) -> int:
+    def mul_mat(self, x: int, weight: int, fmt: int, rows: int, cols: int, dst: int = -1, batch: int = 1) -> int:
+        """y = W x; with batch > 1, x holds `batch` rows of cols floats and y `batch` rows of round16(rows) floats
+        (one GEMV_BATCH command: the prompt's rows, on the tensor cores beyond 8)."""
+        if batch > 1:
+            return self._add(NODE_MUL_MAT, batch * ((rows + 15) // 16 * 16), [x], dst=dst, fmt=fmt, rows=rows,
+                             cols=cols, weight=weight, u=[batch])
         return self._add(NODE_MUL_MAT, rows, [x], dst=dst, fmt=fmt, rows=rows, cols=cols, weight=weight)
 
     def rms_norm(self, x: int, eps: float, rows: int = 1) -> int:

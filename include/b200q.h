@@ -448,7 +448,9 @@ B200Q_API int b200q_comm_world(const b200q_ctx *ctx);
 #define B200Q_NODE_INPUT 1u     /* n floats the caller writes before the lists run (or a buffer commands fill) */
 #define B200Q_NODE_PARAM 2u     /* n resident floats the caller writes once (norm weights, conv kernels, states) */
 #define B200Q_NODE_VIEW 3u      /* rows u[3] of u[1] floats every u[2] floats of src[0], from float u[0]; no command */
-#define B200Q_NODE_MUL_MAT 4u   /* y[rows] = W x: src[0] x (cols floats), weight handle, fmt, rows, cols */
+#define B200Q_NODE_MUL_MAT 4u   /* y[rows] = W x: src[0] x (cols floats), weight handle, fmt, rows, cols; u[0] > 1:
+                                 * u[0] rows of x (u[0] cols floats) into u[0] rows of round16(rows) floats (n), one
+                                 * GEMV_BATCH command (Q4_0 / Q8_0 / Q4_1; joins no fusion) */
 #define B200Q_NODE_RMS_NORM 5u  /* rows of n / rows floats of src[0] (eps) */
 #define B200Q_NODE_L2_NORM 6u   /* as RMS_NORM with the L2 scale */
 #define B200Q_NODE_MUL 7u       /* src[0] * src[1] (src[1] of one row's length: the same row for every row) */

@@ -10,7 +10,9 @@ ggml graph (plan / fusion analysis and emission, ggml-xrt.cpp:1815-2745).
     ranks' lowered lists, run in lock step, decode as the hand-built ones;
   - invalid graphs fail with the node named; b200q_node_supported follows the command limits;
   - random graphs: every lowering is refused cleanly or planner-valid, and random graphs of the fusable patterns give
-    bit-identical outputs with every fusion and with none."""
+    bit-identical outputs with every fusion and with none;
+  - batched MUL_MATs (the prompt's rows) lower to GEMV_BATCH commands, and a batched FFN block gives, row by row,
+    the bits of the one-row block."""
 import numpy as np
 import pytest
 
@@ -304,3 +306,66 @@ def test_random_graphs_compute_the_same_with_and_without_fusions(b2, orc, synth)
             assert np.array_equal(results[0][i].view(np.uint32), results[1][i].view(np.uint32)), (trial, i)
             checked += 1
     assert checked > 60 and fused_trials > 40, (checked, fused_trials)
+
+
+def test_batched_ffn_block_is_the_one_row_block_for_every_row(b2, orc, synth):
+    """The prompt's form of the FFN block: T rows through a multi-row RMS_NORM, batched MUL_MATs (one GEMV_BATCH
+    command each, joining no fusion; more than 8 rows run as the tensor-core GEMM on the GPU), SWIGLU and ADD over all
+    rows. On the oracle every output row has the bits of the one-row block on that row."""
+    import fpga_llama_gguf_b200.graph as G
+    H, F, T = 256, 512, 12
+    r = rng(131)
+    mats = [synth.q4_0(r, F, H), synth.q8_0(r, F, H), synth.q4_1(r, H, F)]
+    fmts = [b2.Q4_0, b2.Q8_0, b2.Q4_1]
+    hs = [4096, 8192, 12288]
+    ws = {h: (m.reshape(-1), rows, cols, f) for h, m, rows, cols, f in zip(hs, mats, (F, F, H), (H, H, F), fmts)}
+    g = G.Graph()
+    x, w = g.input(T * H), g.param(H)
+    xn = g.mul(g.rms_norm(x, 1e-6, rows=T), w)
+    ff = g.swiglu(g.mul_mat(xn, hs[0], fmts[0], F, H, batch=T), g.mul_mat(xn, hs[1], fmts[1], F, H, batch=T))
+    y = g.add(g.mul_mat(ff, hs[2], fmts[2], H, F, batch=T), x)
+    g.mark_output(y)
+    g.end_segment()
+    low = g.lower()
+    ops = [int(c) for c in np.asarray(low.lists[0]).reshape(-1, 8)[:, 0]]
+    assert ops.count(17) == 3 and 1 not in ops, ops
+    assert b2.plan(low.lists[0])[0] == 0
+    xv = np.concatenate([synth.activation(r, H) * (1 + t % 3) for t in range(T)]).astype(np.float32)
+    wv = r.normal(1, 0.1, H).astype(np.float32)
+    act = np.zeros(low.act_floats, np.float32)
+    act[low.offset(x):low.offset(x) + T * H] = xv
+    act[low.offset(w):low.offset(w) + H] = wv
+    assert orc.run_list(act, low.lists[0], ws) == 0
+    got = act[low.offset(y):low.offset(y) + T * H].reshape(T, H)
+    # the one-row block, every feature off (plain commands), row by row
+    g1 = G.Graph()
+    x1, w1 = g1.input(H), g1.param(H)
+    xn1 = g1.mul(g1.rms_norm(x1, 1e-6), w1)
+    ff1 = g1.swiglu(g1.mul_mat(xn1, hs[0], fmts[0], F, H), g1.mul_mat(xn1, hs[1], fmts[1], F, H))
+    y1 = g1.add(g1.mul_mat(ff1, hs[2], fmts[2], H, F), x1)
+    g1.mark_output(y1)
+    g1.end_segment()
+    one = g1.lower(features=0)
+    for t in range(T):
+        a1 = np.zeros(one.act_floats, np.float32)
+        a1[one.offset(x1):one.offset(x1) + H] = xv[t * H:(t + 1) * H]
+        a1[one.offset(w1):one.offset(w1) + H] = wv
+        assert orc.run_list(a1, one.lists[0], ws) == 0
+        assert np.array_equal(got[t].view(np.uint32), a1[one.offset(y1):one.offset(y1) + H].view(np.uint32)), t
+
+
+def test_batched_mul_mat_limits(b2):
+    import fpga_llama_gguf_b200.graph as G
+    g = G.Graph()
+    x = g.input(4 * 256)
+    ok = g.mul_mat(x, 4096, b2.Q4_0, 100, 256, batch=4)
+    kq = g.mul_mat(x, 4096, b2.Q6_K, 100, 256, batch=4)     # K-quants are not batched
+    assert g.supported(ok) and not g.supported(kq)
+    assert g.n(ok) == 4 * 112                               # rows padded to 16 floats, row by row
+    g = G.Graph()
+    x = g.input(4 * 256)
+    v = g.view(x, 0, 128, 256, 4)                            # rows of 128 floats every 256: not contiguous
+    g.mul_mat(v, 4096, b2.Q4_0, 100, 128, batch=4)
+    g.end_segment()
+    with pytest.raises(b2.B200QError, match="contiguous"):
+        g.lower()
