@@ -34,7 +34,7 @@ NORM_L2, NORM_NO_WEIGHT, NORM_DEFER = 1, 2, 4
 UNARY_SILU, UNARY_SIGMOID, UNARY_SOFTPLUS, UNARY_COPY = 1, 2, 3, 4
 SILU_MUL_SIGMOID = 1
 Q4_0, Q4_1, Q8_0, Q5_K, Q6_K = 2, 3, 8, 13, 14
-FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53003F)
+FEATURES = (0x6B51FFFF, 0x6B520001, 0x6B53007F)
 COMM_EXPLICIT = 1
 UPLOAD_REPLICATE = 1
 UPLOAD_SRC_Q4_0X8 = 2

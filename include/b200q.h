@@ -125,10 +125,11 @@ extern "C" {
 /* feature words written by a zero-command b200q_run() into act[0], act[1] (reference gemvqc16.h:126-134): the
  * reference's marker and bit meanings, all bits set (Q5_K, Q6_K, Q4_1, every fusion, ROPE, TRACE). act[2] holds
  * this library's own word: marker 0x6B53 in the high half, bit 0 ATTN, bit 1 ARGMAX, bit 2 GET_ROW, bit 3
- * row-sharded multi-GPU lists, bit 4 ALLREDUCE / ALLGATHER, bit 5 GEMV_BATCH. */
+ * row-sharded multi-GPU lists, bit 4 ALLREDUCE / ALLGATHER, bit 5 GEMV_BATCH, bit 6 GEMV_BATCH of more than 8
+ * rows (the 16-bit batch field; the tensor-core prefill GEMM). */
 #define B200Q_FEATURES 0x6B51FFFFu
 #define B200Q_FEATURES2 0x6B520001u
-#define B200Q_FEATURES3 0x6B53003Fu
+#define B200Q_FEATURES3 0x6B53007Fu
 
 /* ---- status codes ------------------------------------------------------------------------------------------ */
 #define B200Q_OK 0

@@ -621,7 +621,7 @@ ORC_API int orc_run_list(float *act, size_t act_floats, float *state, size_t sta
                          unsigned n_cmds) {
     if (n_cmds == 0) {
         /* feature probe (gemvqc16.h:124-134): the features this library reports */
-        const uint32_t f[3] = {0x6B51FFFFu, 0x6B520001u, 0x6B53003Fu};
+        const uint32_t f[3] = {0x6B51FFFFu, 0x6B520001u, 0x6B53007Fu};
         memcpy(act, f, sizeof(f));
         return 0;
     }
