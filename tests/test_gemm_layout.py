@@ -4,7 +4,8 @@ of a 128-row tile reads block b of that row out of the device layout at unit u =
 over the bytes the library's own repack produces (b200q_repack_host), for every panel height P the layout picks
 (1 to 32 rows, C = 32 / P blocks per tile), and must give back every quant and scale of every GGUF row; the canonical
 placement must be the layout the MMA's shared-memory descriptor describes (leading byte offset 128, stride byte
-offset 256). The GPU tests (test_gpu_gemm.py) check the kernel's results themselves for several of these heights."""
+offset 256); and the decomposition itself (one integer product per block, FP32 terms folded in block order) gives
+the oracle GEMV's bits. The GPU tests (test_gpu_gemm.py) check the kernel's results themselves."""
 import numpy as np
 import pytest
 
@@ -98,3 +99,43 @@ def test_canonical_placement_is_the_descriptors_layout():
     addr = (m % 8) * 16 + (m // 8) * sbo + (k // 16) * lbo + k % 16
     assert np.array_equal(buf[addr], m * 32 + k)
     assert np.array_equal(np.sort(addr.reshape(-1)), np.arange(4096))  # the 4 KB tile, each byte once
+
+
+@pytest.mark.parametrize("fmt", [2, 8, 3])
+def test_block_matmul_and_ordered_fold_is_the_oracle_gemv(b2, synth, orc, fmt):
+    """The GEMM's decomposition, restated in numpy: per 32-value block one integer matrix product of the weight
+    quants (Q4_0 nibbles - 8) with the tokens' Q8_0 / Q8_1 quants (what one int8 MMA computes for a tile), then the
+    FP32 terms float(sumi) * (d_w * d_x) [Q4_1: (d_w * d_x) * float(sumi) + m_w * s_x] added in block order from 0,
+    each operation rounded once. Every output has the oracle GEMV's bits."""
+    rows, cols, T = 200, 512, 20
+    r = rng(133, fmt)
+    w = synth.matrix(fmt, r, rows, cols)
+    xs = np.stack([synth.activation(r, cols) * (1 + t % 5) for t in range(T)]).astype(np.float32)
+    wq, wd, wm = _gguf_blocks(w, rows, cols, fmt)
+    dw = wd.view(np.float16).astype(np.float32)
+    nb = cols // 32
+    xq = np.zeros((T, nb, 32), np.int32)
+    xd = np.zeros((T, nb), np.float32)
+    xsum = np.zeros((T, nb), np.float32)
+    for t in range(T):
+        if fmt == 3:
+            q, ds, _ = orc.quantize_q8_1(xs[t])
+            pair = ds.reshape(nb, 2).view(np.float16).astype(np.float32)
+            xd[t], xsum[t] = pair[:, 0], pair[:, 1]
+        else:
+            q, d, _ = orc.quantize_q8_0(xs[t])
+            xd[t] = d.view(np.float16).astype(np.float32)
+        xq[t] = q.reshape(nb, 32)
+    acc = np.zeros((rows, T), np.float32)
+    for b in range(nb):
+        sumi = (wq[:, b, :] @ xq[:, b, :].T).astype(np.float32)  # exact: |sumi| < 2^24
+        p = (dw[:, b, None] * xd[None, :, b]).astype(np.float32)
+        if fmt == 3:
+            mw = wm.view(np.float16).astype(np.float32)
+            term = (p * sumi).astype(np.float32) + (mw[:, b, None] * xsum[None, :, b]).astype(np.float32)
+        else:
+            term = (sumi * p).astype(np.float32)
+        acc = (acc + term.astype(np.float32)).astype(np.float32)
+    for t in range(T):
+        y, _ = orc.gemv(w, xs[t], rows, cols, fmt)
+        assert np.array_equal(acc[:, t].view(np.uint32), y.view(np.uint32)), t
