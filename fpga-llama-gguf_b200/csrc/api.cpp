@@ -948,6 +948,8 @@ int prepare_gemm_image(b200q_ctx *c, const Plan &plan) {
         if (batch > kBatchMax) need = std::max(need, gemm_image_bytes(p.cmd[0][3], batch));
     }
     if (need <= c->gemm_img_bytes) return 0;
+    // at least double: a caller whose prompts grow a little at a time retires O(log) buffers, not one per size
+    need = std::max(need, 2 * c->gemm_img_bytes);
     uint8_t *img = nullptr;
     const cudaError_t e = cudaMalloc(&img, need);
     if (e != cudaSuccess) {
