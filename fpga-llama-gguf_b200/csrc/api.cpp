@@ -937,7 +937,6 @@ int exec_chain(b200q_ctx *c, ChainArgs &a) {
     return 0;
 }
 
-// Executes the passes of a plan on the context stream (no synchronization).
 // The image of the quantized tokens that the list's GEMV_BATCH commands of more than kBatchMax rows need, allocated
 // before the list runs or is captured (no allocation inside a capture).
 int prepare_gemm_image(b200q_ctx *c, const Plan &plan) {
@@ -948,20 +947,27 @@ int prepare_gemm_image(b200q_ctx *c, const Plan &plan) {
         if (batch > kBatchMax) need = std::max(need, gemm_image_bytes(p.cmd[0][3], batch));
     }
     if (need <= c->gemm_img_bytes) return 0;
-    // at least double: a caller whose prompts grow a little at a time retires O(log) buffers, not one per size
-    need = std::max(need, 2 * c->gemm_img_bytes);
+    // at least double the old size, so that a caller whose prompts grow a little at a time retires O(log) buffers;
+    // exactly the need when the doubled size does not fit
     uint8_t *img = nullptr;
-    const cudaError_t e = cudaMalloc(&img, need);
+    size_t bytes = std::max(need, 2 * c->gemm_img_bytes);
+    cudaError_t e = cudaMalloc(&img, bytes);
+    if (e != cudaSuccess && bytes > need) {
+        cudaGetLastError();
+        bytes = need;
+        e = cudaMalloc(&img, bytes);
+    }
     if (e != cudaSuccess) {
         cudaGetLastError();
         return set_err(c, B200Q_ERR_NOMEM, "GEMV_BATCH token image (%zu bytes): %s", need, cudaGetErrorString(e));
     }
     if (c->gemm_img) c->gemm_img_old.push_back(c->gemm_img);
     c->gemm_img = img;
-    c->gemm_img_bytes = need;
+    c->gemm_img_bytes = bytes;
     return 0;
 }
 
+// Executes the passes of a plan on the context stream (no synchronization).
 int exec_plan(b200q_ctx *c, const Plan &plan, unsigned n_cmds) {
     c->snap_used = 0;
     c->launches = 0;
