@@ -633,7 +633,6 @@ int exec_gdn(b200q_ctx *c, const Pass &p, const ImageLink &nsq_link) {
     return 0;
 }
 
-
 int exec_ext(b200q_ctx *c, const Pass &p) {
     const uint32_t *cmd = p.cmd[0];
     float *A = c->act;
